@@ -1,0 +1,471 @@
+"""Benchmark of the B200 kernels on the BASELINE.json workloads; prints one JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Headline workload ("RL loss pipeline"): per GPU a batch of
+B=4096 trajectories x T=1000 steps; one step = discounted reward-to-go over the batch plus the
+PPO clipped loss with its diagnostics and the mean entropy over the same 4,096,000 samples.
+`value` is samples (trajectory steps) per second over all GPUs, inputs resident in HBM; the
+per-op microseconds and roofline fractions that BASELINE.json's metric names are reported beside
+it.  With N > 1 each rank processes its own batch (weak scaling) and the PPO reduction is global:
+the ranks exchange their per-chunk partials with one NCCL all-gather and all finish identically.
+
+Timing: W untimed warm-up steps, then exactly K steps between barriers and device syncs, timed
+with CUDA events on the launching stream, max over ranks.  Each step reads a different one of
+four input sets (4 x 102 MB, larger than the 126 MB L2), so every step streams from HBM.
+`e2e` repeats the step through the same entry points with the inputs in pinned host memory:
+host-to-device copies of that step's inputs and a device-to-host read of its results are inside
+the timed region.  `--impl reference` times the CPU restatement of the reference's PyTorch-eager
+implementation of the same step on all host cores (rank 0 only).
+"""
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "per-op µs and % of HBM or FP8-tensor roofline, 1–8 B200, vs CPU eager"
+B, T = 4096, 1000
+N_SAMPLES = B * T
+ROTATE = 4
+# Algorithmic bytes per call (reads + writes of each op's inputs and outputs).
+RTG_BYTES = (4 + 1 + 4) * N_SAMPLES                 # reward f32 + done u8 -> output f32
+PPO_BYTES = 16 * N_SAMPLES + 7 * 4                  # cur, old, adv, entropy f32 -> 7 f32
+ROBUST_L1_BYTES = 2 * 4 * (1 << 26) + 4
+LIF_BYTES = 4 * 2 * (256 * 64 * 4096) + 4 * 2 * (64 * 4096) + 4 * 2 * 4096
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------------ distributed set-up
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples of the SM clock and throttle reasons while it runs."""
+
+    QUERY = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        ident = str(device)
+        try:
+            u = torch.cuda.get_device_properties(device).uuid
+            ident = "GPU-" + str(u)
+        except Exception:
+            pass
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", ident], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                smax.append(float(f[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------ inputs
+def make_sets(dev, rank, n_sets):
+    from oracle import inputs  # seeded synthetic inputs of BASELINE.json configs[1]
+    sets = []
+    for i in range(n_sets):
+        s = inputs.baseline_inputs("rl_pipeline", seed=1000 * rank + i)
+        sets.append({k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in s.items()})
+    return sets
+
+
+# -------------------------------------------------------------------------------- GPU arm
+def run_b200(args, world, rank, local):
+    pkg = importlib.import_module("cuda-optimization-benchmark_b200")
+    lib = pkg.load()
+    ops = pkg.ops
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    sets = make_sets(dev, rank, ROTATE)
+    gamma, eps = sets[0]["gamma"], sets[0]["clip_epsilon"]
+    rtg_out = torch.empty(B, T, device=dev)
+    ppo_out = torch.empty(7, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        chunk = lib.b200_ppo_chunk_elems()
+        n_parts = (N_SAMPLES + chunk - 1) // chunk
+        rec = lib.b200_ppo_partial_bytes()
+        local_parts = torch.empty((n_parts, rec), dtype=torch.uint8, device=dev)
+        all_parts = torch.empty((world * n_parts, rec), dtype=torch.uint8, device=dev)
+
+    # Pre-bound C-ABI argument tuples per input set: the timed loop is two ctypes calls per step.
+    import ctypes
+    P = ctypes.c_void_p
+    cs = P(stream.cuda_stream)
+    ws = ops.workspace("ppo", lib.b200_ppo_workspace_bytes(N_SAMPLES), dev)
+    rtg_args, ppo_args = [], []
+    for s in sets:
+        rtg_args.append((P(s["reward"].data_ptr()), P(s["done"].data_ptr()), gamma, B, T, P(rtg_out.data_ptr()), cs))
+        ppo_args.append((P(s["current_log_prob"].data_ptr()), P(s["old_log_prob"].data_ptr()),
+                         P(s["advantage"].data_ptr()), P(s["entropy"].data_ptr()), N_SAMPLES, eps,
+                         P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), cs))
+    f_rtg, f_ppo = lib.b200_reward_to_go_async, lib.b200_ppo_async
+
+    def step(i, evs=None):
+        k = i % ROTATE
+        if evs is not None:
+            evs[0].record(stream)
+        f_rtg(*rtg_args[k])
+        if evs is not None:
+            evs[1].record(stream)
+        if world == 1:
+            f_ppo(*ppo_args[k])
+        else:
+            s = sets[k]
+            parts = ops.ppo_partials(s["current_log_prob"], s["old_log_prob"], s["advantage"], eps, s["entropy"])
+            local_parts.copy_(parts)
+            dist.all_gather_into_tensor(all_parts, local_parts)
+            ops.ppo_finish(all_parts, world * N_SAMPLES, True, out=ppo_out)
+        if evs is not None:
+            evs[2].record(stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(i, evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clk = clocks.stop()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+    rtg_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs), world)
+    ppo_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in evs), world)
+
+    # Same K steps replayed from a CUDA graph (one graph per input set), no events between kernels:
+    # shows how much of the eager step time is host launch overhead.
+    graph_ms = None
+    if world == 1:
+        graphs = []
+        side = torch.cuda.Stream(dev)
+        for k in range(ROTATE):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                cs_side = P(torch.cuda.current_stream(dev).cuda_stream)
+                f_rtg(*rtg_args[k][:-1], cs_side)
+                f_ppo(*ppo_args[k][:-1], cs_side)
+            graphs.append(g)
+        for i in range(args.warmup):
+            graphs[i % ROTATE].replay()
+        torch.cuda.synchronize(dev)
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for i in range(args.steps):
+            graphs[i % ROTATE].replay()
+        g1.record(stream)
+        torch.cuda.synchronize(dev)
+        graph_ms = g0.elapsed_time(g1) / args.steps
+        del graphs
+
+    # ---- e2e: same entry points, inputs from pinned host memory, results read back each step
+    host = []
+    for s in sets[:2]:
+        host.append({k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in s.items()})
+    dbuf = {k: torch.empty_like(v) for k, v in sets[0].items() if isinstance(v, torch.Tensor)}
+    rtg_host = torch.empty(B, T).pin_memory()
+    ppo_host = torch.empty(7).pin_memory()
+    names = ["reward", "done", "current_log_prob", "old_log_prob", "advantage", "entropy"]
+    h2d = sum(dbuf[k].numel() * dbuf[k].element_size() for k in names)
+    d2h = rtg_host.numel() * 4 + ppo_host.numel() * 4
+
+    def e2e_step(i):
+        h = host[i % 2]
+        for k in names:
+            dbuf[k].copy_(h[k], non_blocking=True)
+        ops.reward_to_go(dbuf["reward"], dbuf["done"], gamma, out=rtg_out)
+        if world == 1:
+            ops.ppo_clip(dbuf["current_log_prob"], dbuf["old_log_prob"], dbuf["advantage"], eps, dbuf["entropy"],
+                         out=ppo_out)
+        else:
+            parts = ops.ppo_partials(dbuf["current_log_prob"], dbuf["old_log_prob"], dbuf["advantage"], eps,
+                                     dbuf["entropy"])
+            local_parts.copy_(parts)
+            dist.all_gather_into_tensor(all_parts, local_parts)
+            ops.ppo_finish(all_parts, world * N_SAMPLES, True, out=ppo_out)
+        rtg_host.copy_(rtg_out, non_blocking=True)
+        ppo_host.copy_(ppo_out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 50))
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps, world)
+
+    extra = {}
+    if not args.no_ops:
+        extra = other_ops(ops, dev, world, rank)
+
+    peak, peak_kind = peaks()
+    dominant = "ppo_clip_ext" if ppo_ms >= rtg_ms else "reward_to_go"
+    dom_bytes = PPO_BYTES if ppo_ms >= rtg_ms else RTG_BYTES
+    dom_ms = max(ppo_ms, rtg_ms)
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    per_step_launches = 2 if world == 1 else 3
+    line = {
+        "metric": METRIC,
+        "value": world * N_SAMPLES / (ms * 1e-3),
+        "unit": "samples/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "us_per_step": ms * 1e3,
+        "graph_us_per_step": graph_ms * 1e3 if graph_ms is not None else None,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE.json configs[1] distributions)",
+        "config": {"workload": "rl_pipeline: reward_to_go + ppo_clip_ext", "B": B, "T": T, "H": 1,
+                   "samples_per_gpu": N_SAMPLES, "gamma": 0.99, "done_p": 0.01, "clip_epsilon": 0.2,
+                   "l2": f"rotating {ROTATE} input sets of {(RTG_BYTES - 4 * N_SAMPLES + PPO_BYTES) / 1e6:.0f} MB "
+                         f"(> 126 MB L2)",
+                   "parallelism": f"dp{world}: rows sharded, PPO partials all-gathered (NCCL)" if world > 1
+                   else "1 GPU"},
+        "per_op": {
+            "reward_to_go": {"us": rtg_ms * 1e3, "bytes": RTG_BYTES,
+                             "gbs": RTG_BYTES / (rtg_ms * 1e-3) / 1e9,
+                             "frac_of_hbm": RTG_BYTES / (rtg_ms * 1e-3) / 1e9 / peak},
+            "ppo_clip_ext": {"us": ppo_ms * 1e3, "bytes": PPO_BYTES,
+                             "gbs": PPO_BYTES / (ppo_ms * 1e-3) / 1e9,
+                             "frac_of_hbm": PPO_BYTES / (ppo_ms * 1e-3) / 1e9 / peak},
+        },
+        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_kind == "measured" else "fallback 6650 GB/s",
+                     "traffic": None},
+        "e2e": {"value": world * N_SAMPLES / (e2e_ms * 1e-3), "unit": "samples/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": per_step_launches * args.steps,
+        "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                   "samples": clk["samples"]},
+    }
+    if extra:
+        line["ops"] = extra
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(args)
+    return line
+
+
+def other_ops(ops, dev, world, rank):
+    """Device-timed µs of the other streaming ops at their BASELINE sizes (one input set each,
+    already larger than L2)."""
+    from oracle import inputs
+    peak, _ = peaks()
+    res = {}
+
+    def timeit(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / reps
+
+    s = inputs.baseline_inputs("robust_l1", seed=rank)
+    x, y = s["inp"].to(dev), s["target"].to(dev)
+    out = torch.empty((), device=dev)
+    ms = timeit(lambda: ops.robust_l1(x, y, out=out))
+    res["robust_l1"] = {"us": ms * 1e3, "bytes": ROBUST_L1_BYTES, "gbs": ROBUST_L1_BYTES / ms / 1e6,
+                        "frac_of_hbm": ROBUST_L1_BYTES / ms / 1e6 / peak}
+    del x, y
+    s = inputs.baseline_inputs("lif", seed=rank)
+    xs, m0, be, th = (s[k].to(dev) for k in ("input_current", "mem0", "beta", "threshold"))
+    sp = torch.empty_like(xs)
+    fm = torch.empty_like(m0)
+    ms = timeit(lambda: ops.leaky(xs, m0, be, th, spikes=sp, final_mem=fm))
+    res["leaky"] = {"us": ms * 1e3, "bytes": LIF_BYTES, "gbs": LIF_BYTES / ms / 1e6,
+                    "frac_of_hbm": LIF_BYTES / ms / 1e6 / peak}
+    torch.cuda.synchronize(dev)
+    return res
+
+
+# -------------------------------------------------------------------------------- CPU baseline
+def cpu_step_fn():
+    from oracle import eager, inputs
+    s = inputs.baseline_inputs("rl_pipeline", seed=0)
+
+    def run():
+        eager.reward_to_go(s["reward"], s["done"], s["gamma"])
+        eager.ppo_clip(s["current_log_prob"], s["old_log_prob"], s["advantage"], s["clip_epsilon"], s["entropy"])
+    return run
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(args, reps=None):
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    run = cpu_step_fn()
+    run()
+    times = []
+    reps = reps or 5
+    for _ in range(reps):
+        t = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t)
+    sec = statistics.median(times)
+    return {"value": N_SAMPLES / sec, "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"full configs[1] batch (B={B}, T={T}); median of {reps} after 1 warm-up; "
+                      f"PyTorch-eager fp32 restatement of the reference's reference() for reward_to_go and "
+                      f"ppo_clip (+ entropy mean)",
+            "ms_per_step": sec * 1e3}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    run = cpu_step_fn()
+    for _ in range(args.warmup):
+        run()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    sec = (time.perf_counter() - t) / args.steps
+    v = N_SAMPLES / sec
+    return {"metric": METRIC, "value": v, "unit": "samples/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE.json configs[1] distributions)",
+            "config": {"workload": "rl_pipeline: reward_to_go + ppo_clip_ext", "B": B, "T": T, "H": 1,
+                       "samples_per_gpu": N_SAMPLES},
+            "cpu_baseline": {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
+                             "sample": f"full configs[1] batch per step, {args.steps} steps after {args.warmup} "
+                                       f"warm-up; PyTorch-eager fp32 restatement of the reference's reference()"},
+            "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    line = run_b200(args, world, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

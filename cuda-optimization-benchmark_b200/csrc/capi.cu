@@ -1,0 +1,128 @@
+// C ABI of libb200ops.so: the declarations live in include/b200ops.h.
+//
+// Each drop-in entry point has the argument list of the reference's `void reference(...)` for its
+// task and runs on the legacy default stream, as the reference grader expects
+// (tasks/*/prompt.md "Launch your work on the default stream").  The stream forms return a
+// status and take the stream (and, for reductions, the workspace) from the caller.
+#include <cuda_runtime.h>
+
+#include "../../include/b200ops.h"
+#include "ops/lif.cuh"
+#include "ops/ppo_clip.cuh"
+#include "ops/reward_to_go.cuh"
+#include "ops/robust_l1.cuh"
+
+namespace {
+thread_local int g_last_status = 0;
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline void record(int s) { g_last_status = s; }
+}  // namespace
+
+extern "C" {
+
+const char* b200_status_string(int status) { return b200::status_string(status); }
+int b200_last_status(void) { return g_last_status; }
+
+// ---------------------------------------------------------------------------------- robust-L1
+void b200_pow_abs_sqrt_mean(const float* inp, const float* target, int64_t batch_size, int64_t height,
+                            int64_t width, float* output) {
+  const int64_t n = b200::robust_l1::abi_count(batch_size, height, width);
+  if (n < 0) return record(b200::kInvalidArgument);
+  int st = 0;
+  const size_t ws = b200::robust_l1::workspace_bytes(n);
+  void* w = b200::arena_get(ws, nullptr, &st);
+  if (st != 0) return record(st);
+  record(b200::robust_l1::run(inp, target, n, output, w, ws, nullptr));
+}
+
+size_t b200_robust_l1_workspace_bytes(int64_t n) { return n < 0 ? 0 : b200::robust_l1::workspace_bytes(n); }
+
+int b200_robust_l1_async(const float* inp, const float* target, int64_t n, float* output, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  return b200::robust_l1::run(inp, target, n, output, workspace, workspace_bytes, as_stream(stream));
+}
+
+int64_t b200_robust_l1_chunk_elems(void) { return b200::robust_l1::kChunk; }
+
+int b200_robust_l1_shard_partials(const float* inp, const float* target, int64_t n, double* partials,
+                                  void* stream) {
+  return b200::robust_l1::shard_partials(inp, target, n, partials, as_stream(stream));
+}
+
+int b200_robust_l1_finish(const double* partials, int64_t n_partials, int64_t n_total, float* output,
+                          void* stream) {
+  return b200::robust_l1::shard_finish(partials, n_partials, n_total, output, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------------------- PPO
+static void ppo_dropin(int32_t B, int32_t T, int32_t H, const float* cur, const float* old, const float* adv,
+                       const float* ent, float eps, float* out) {
+  const int64_t n = b200::ppo::abi_count(B, T, H);
+  if (n < 0) return record(b200::kInvalidArgument);
+  int st = 0;
+  const size_t ws = b200::ppo::workspace_bytes(n);
+  void* w = b200::arena_get(ws, nullptr, &st);
+  if (st != 0) return record(st);
+  record(b200::ppo::run(cur, old, adv, ent, n, eps, out, w, ws, nullptr));
+}
+
+void b200_ppo_clip(const int32_t B, const int32_t T, const int32_t H, const float* current_log_prob,
+                   const float* old_log_prob, const float* advantage, const float clip_epsilon, float* output) {
+  ppo_dropin(B, T, H, current_log_prob, old_log_prob, advantage, nullptr, clip_epsilon, output);
+}
+
+void b200_ppo_clip_ext(const int32_t B, const int32_t T, const int32_t H, const float* current_log_prob,
+                       const float* old_log_prob, const float* advantage, const float* entropy,
+                       const float clip_epsilon, float* output) {
+  if (entropy == nullptr) return record(b200::kInvalidArgument);
+  ppo_dropin(B, T, H, current_log_prob, old_log_prob, advantage, entropy, clip_epsilon, output);
+}
+
+size_t b200_ppo_workspace_bytes(int64_t n) { return n < 0 ? 0 : b200::ppo::workspace_bytes(n); }
+
+int b200_ppo_async(const float* current_log_prob, const float* old_log_prob, const float* advantage,
+                   const float* entropy, int64_t n, float clip_epsilon, float* output, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  return b200::ppo::run(current_log_prob, old_log_prob, advantage, entropy, n, clip_epsilon, output, workspace,
+                        workspace_bytes, as_stream(stream));
+}
+
+int64_t b200_ppo_chunk_elems(void) { return b200::ppo::kChunk; }
+size_t b200_ppo_partial_bytes(void) { return sizeof(b200::ppo::Partial); }
+
+int b200_ppo_shard_partials(const float* current_log_prob, const float* old_log_prob, const float* advantage,
+                            const float* entropy, int64_t n, float clip_epsilon, void* partials, void* stream) {
+  return b200::ppo::shard_partials(current_log_prob, old_log_prob, advantage, entropy, n, clip_epsilon,
+                                   static_cast<b200::ppo::Partial*>(partials), as_stream(stream));
+}
+
+int b200_ppo_finish(const void* partials, int64_t n_partials, int64_t n_total, int with_entropy, float* output,
+                    void* stream) {
+  return b200::ppo::shard_finish(static_cast<const b200::ppo::Partial*>(partials), n_partials, n_total,
+                                 with_entropy != 0, output, as_stream(stream));
+}
+
+// ------------------------------------------------------------------------------- reward-to-go
+void b200_reward_to_go(const float* reward, const bool* done, float gamma, int32_t B, int32_t T, float* output) {
+  record(b200::rtg::run(reward, reinterpret_cast<const unsigned char*>(done), gamma, B, T, output, nullptr));
+}
+
+int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                            float* output, void* stream) {
+  return b200::rtg::run(reward, done, gamma, B, T, output, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------------------- LIF
+void b200_leaky(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem) {
+  record(b200::lif::run(input_current, mem0, beta, threshold, T, B, H, spikes, final_mem, nullptr));
+}
+
+int b200_leaky_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                     int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, void* stream) {
+  return b200::lif::run(input_current, mem0, beta, threshold, T, B, H, spikes, final_mem, as_stream(stream));
+}
+
+}  // extern "C"

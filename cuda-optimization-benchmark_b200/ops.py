@@ -1,0 +1,176 @@
+"""PyTorch-tensor front end of the native ops (device memory and streams come from torch; the
+work is done by libb200ops.so on the current CUDA stream).
+
+`reference(task, inp)` mirrors the reference's per-task `reference(inp) -> dict`
+(tasks/<task>/reference.py): the same input dict keys (the C argument names), the same output
+names and shapes, so a caller of the reference's PyTorch entry can switch to this one unchanged.
+Every function raises on a non-CUDA tensor, a wrong dtype or a non-contiguous input, and on a
+non-zero native status; there is no CPU fallback.
+"""
+import ctypes
+
+import torch
+
+from . import _native
+
+_WS = {}
+
+
+def _lib():
+    return _native.load()
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need(t, name, dtype, device=None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name}: expected a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name}: expected a CUDA tensor (no CPU path)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name}: expected {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: expected a contiguous tensor")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name}: on {t.device}, expected {device}")
+    return t
+
+
+def workspace(op, nbytes, device):
+    """Zero-initialised scratch for `op` on `device` and the current stream, grown on demand.
+
+    The reduction kernels leave their completion counter at zero, so one buffer serves every
+    later call issued on the same stream."""
+    key = (op, device.index, torch.cuda.current_stream(device).cuda_stream)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(int(nbytes), 4096), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+# ----------------------------------------------------------------------------------- robust-L1
+def robust_l1(inp, target, out=None):
+    """mean(sqrt((inp - target)^2 + 1e-6)) as a 0-d fp32 tensor."""
+    _need(inp, "inp", torch.float32)
+    _need(target, "target", torch.float32, inp.device)
+    if inp.numel() != target.numel():
+        raise ValueError("inp and target differ in size")
+    n = inp.numel()
+    out = torch.empty((), dtype=torch.float32, device=inp.device) if out is None else out
+    lib = _lib()
+    ws = workspace("robust_l1", lib.b200_robust_l1_workspace_bytes(n), inp.device)
+    _native.check(lib.b200_robust_l1_async(_ptr(inp), _ptr(target), n, _ptr(out), _ptr(ws), ws.numel(),
+                                           _stream(inp.device)), "robust_l1")
+    return out
+
+
+def robust_l1_partials(inp, target):
+    """Chunk partials (fp64, one per b200_robust_l1_chunk_elems() elements) of one shard."""
+    _need(inp, "inp", torch.float32)
+    _need(target, "target", torch.float32, inp.device)
+    lib = _lib()
+    n = inp.numel()
+    chunk = lib.b200_robust_l1_chunk_elems()
+    parts = torch.empty((n + chunk - 1) // chunk, dtype=torch.float64, device=inp.device)
+    _native.check(lib.b200_robust_l1_shard_partials(_ptr(inp), _ptr(target), n, _ptr(parts),
+                                                    _stream(inp.device)), "robust_l1_partials")
+    return parts
+
+
+def robust_l1_finish(partials, n_total, out=None):
+    _need(partials, "partials", torch.float64)
+    out = torch.empty((), dtype=torch.float32, device=partials.device) if out is None else out
+    _native.check(_lib().b200_robust_l1_finish(_ptr(partials), partials.numel(), int(n_total), _ptr(out),
+                                               _stream(partials.device)), "robust_l1_finish")
+    return out
+
+
+# ----------------------------------------------------------------------------------------- PPO
+def ppo_clip(cur, old, adv, clip_epsilon, entropy=None, out=None):
+    """[loss, clip_fraction, approx_kl, ess, max_ratio, mean_ratio] (+ mean entropy)."""
+    _need(cur, "current_log_prob", torch.float32)
+    _need(old, "old_log_prob", torch.float32, cur.device)
+    _need(adv, "advantage", torch.float32, cur.device)
+    if entropy is not None:
+        _need(entropy, "entropy", torch.float32, cur.device)
+    n = cur.numel()
+    if old.numel() != n or adv.numel() != n or (entropy is not None and entropy.numel() != n):
+        raise ValueError("PPO inputs differ in size")
+    k = 7 if entropy is not None else 6
+    out = torch.empty(k, dtype=torch.float32, device=cur.device) if out is None else out
+    lib = _lib()
+    ws = workspace("ppo", lib.b200_ppo_workspace_bytes(n), cur.device)
+    _native.check(lib.b200_ppo_async(_ptr(cur), _ptr(old), _ptr(adv), _ptr(entropy), n, float(clip_epsilon),
+                                     _ptr(out), _ptr(ws), ws.numel(), _stream(cur.device)), "ppo_clip")
+    return out
+
+
+def ppo_partials(cur, old, adv, clip_epsilon, entropy=None):
+    """Per-chunk partial records (uint8 rows of b200_ppo_partial_bytes()) of one shard."""
+    lib = _lib()
+    n = cur.numel()
+    chunk = lib.b200_ppo_chunk_elems()
+    rec = lib.b200_ppo_partial_bytes()
+    parts = torch.empty(((n + chunk - 1) // chunk, rec), dtype=torch.uint8, device=cur.device)
+    _native.check(lib.b200_ppo_shard_partials(_ptr(cur), _ptr(old), _ptr(adv), _ptr(entropy), n,
+                                              float(clip_epsilon), _ptr(parts), _stream(cur.device)),
+                  "ppo_partials")
+    return parts
+
+
+def ppo_finish(partials, n_total, with_entropy, out=None):
+    k = 7 if with_entropy else 6
+    out = torch.empty(k, dtype=torch.float32, device=partials.device) if out is None else out
+    _native.check(_lib().b200_ppo_finish(_ptr(partials), partials.shape[0], int(n_total), int(bool(with_entropy)),
+                                         _ptr(out), _stream(partials.device)), "ppo_finish")
+    return out
+
+
+# -------------------------------------------------------------------------------- reward-to-go
+def reward_to_go(reward, done, gamma, out=None):
+    _need(reward, "reward", torch.float32)
+    _need(done, "done", torch.bool, reward.device)
+    if reward.dim() != 2 or done.shape != reward.shape:
+        raise ValueError("reward and done must both be (B, T)")
+    B, T = reward.shape
+    out = torch.empty_like(reward) if out is None else out
+    _native.check(_lib().b200_reward_to_go_async(_ptr(reward), _ptr(done), float(gamma), B, T, _ptr(out),
+                                                 _stream(reward.device)), "reward_to_go")
+    return out
+
+
+# ----------------------------------------------------------------------------------------- LIF
+def leaky(input_current, mem0, beta, threshold, spikes=None, final_mem=None):
+    _need(input_current, "input_current", torch.float32)
+    dev = input_current.device
+    for t, nm in ((mem0, "mem0"), (beta, "beta"), (threshold, "threshold")):
+        _need(t, nm, torch.float32, dev)
+    T, B, H = input_current.shape
+    spikes = torch.empty_like(input_current) if spikes is None else spikes
+    final_mem = torch.empty((B, H), dtype=torch.float32, device=dev) if final_mem is None else final_mem
+    _native.check(_lib().b200_leaky_async(_ptr(input_current), _ptr(mem0), _ptr(beta), _ptr(threshold), T, B, H,
+                                          _ptr(spikes), _ptr(final_mem), _stream(dev)), "leaky")
+    return spikes, final_mem
+
+
+# ------------------------------------------------------------------- reference-interface mirror
+def reference(task, inp):
+    """Drop-in for tasks/<task>/reference.py:reference(inp): same keys in, same keys out."""
+    if task == "pow_abs_sqrt_mean":
+        return {"output": robust_l1(inp["inp"], inp["target"])}
+    if task == "ppo_clip":
+        return {"output": ppo_clip(inp["current_log_prob"], inp["old_log_prob"], inp["advantage"],
+                                   inp["clip_epsilon"], inp.get("entropy"))}
+    if task == "reward_to_go":
+        return {"output": reward_to_go(inp["reward"], inp["done"], inp["gamma"])}
+    if task == "leaky":
+        s, m = leaky(inp["input_current"], inp["mem0"], inp["beta"], inp["threshold"])
+        return {"spikes": s, "final_mem": m}
+    raise KeyError(f"unknown or not yet built task: {task}")

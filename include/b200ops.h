@@ -1,0 +1,126 @@
+/*
+ * b200ops.h - C ABI of the B200 (sm_100a) kernels for the six ops of
+ * Mohamed-Alaboudi/cuda-optimization-benchmark.
+ *
+ * Two forms per op:
+ *
+ *  - Drop-in form, b200_<task>(...): the exact argument list and meaning of the reference's
+ *    `void reference(...)` for that task (tasks/<task>/tests/task.json:3), with C linkage so a
+ *    ctypes/cffi/dlsym caller can bind it by name.  Device pointers, work on the legacy default
+ *    stream, nothing returned; errors surface at the caller's next synchronize, as with the
+ *    reference.  b200_last_status() reports the status of the calling thread's last drop-in call.
+ *    Ops that need scratch take it from a per-device arena allocated on first use.
+ *
+ *  - Stream form, b200_<op>_async(...): the same work on a caller stream (a cudaStream_t passed
+ *    as void*), returning a b200 status code (0 = ok).  Reductions also take a caller workspace
+ *    and expose shard/finish halves for multi-GPU use.
+ *
+ * All pointers are device pointers to contiguous row-major data.  `bool` is one byte (0 or 1);
+ * fp8 E4M3 and bf16 buffers are passed as uint8_t / uint16_t.
+ */
+#ifndef B200OPS_H
+#define B200OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes of the stream forms and of b200_last_status(). */
+#define B200_OK 0
+#define B200_INVALID_ARGUMENT 1
+#define B200_CUDA_ERROR 2
+#define B200_UNSUPPORTED 3
+#define B200_WORKSPACE_TOO_SMALL 4
+#define B200_TIMEOUT 5
+
+const char* b200_status_string(int status);
+int b200_last_status(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * Robust-L1 mean (task pow_abs_sqrt_mean): output[0] = mean(sqrt((inp - target)^2 + 1e-6)).
+ * Replaces `void reference(const float* inp, const float* target, int64_t batch_size,
+ * int64_t height, int64_t width, float* output)`: tasks/pow_abs_sqrt_mean/tests/task.json:3,
+ * reference/pow_abs_sqrt_mean/solution.cu:99.
+ * ------------------------------------------------------------------------------------------- */
+void b200_pow_abs_sqrt_mean(const float* inp, const float* target, int64_t batch_size, int64_t height,
+                            int64_t width, float* output);
+
+/* Stream form over n elements.  workspace: b200_robust_l1_workspace_bytes(n) bytes, zero-filled
+ * once before its first use (every call leaves it ready for the next). */
+size_t b200_robust_l1_workspace_bytes(int64_t n);
+int b200_robust_l1_async(const float* inp, const float* target, int64_t n, float* output, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Multi-GPU halves.  The global element range is cut into chunks of b200_robust_l1_chunk_elems();
+ * a shard must start on a chunk boundary.  shard_partials writes one double per local chunk;
+ * finish sums the gathered partials of all shards (in chunk order) and divides by n_total.  The
+ * result is bit-identical to b200_robust_l1_async on the whole range. */
+int64_t b200_robust_l1_chunk_elems(void);
+int b200_robust_l1_shard_partials(const float* inp, const float* target, int64_t n, double* partials,
+                                  void* stream);
+int b200_robust_l1_finish(const double* partials, int64_t n_partials, int64_t n_total, float* output,
+                          void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * PPO clipped loss + diagnostics (task ppo_clip): output[0..6) = [loss, clip_fraction,
+ * approx_kl, ess, max_ratio, mean_ratio].
+ * Replaces `void reference(const int32_t B, const int32_t T, const int32_t H,
+ * const float* current_log_prob, const float* old_log_prob, const float* advantage,
+ * const float clip_epsilon, float* output)`: tasks/ppo_clip/tests/task.json:3,
+ * reference/ppo_clip/solution.cu:165.
+ * ------------------------------------------------------------------------------------------- */
+void b200_ppo_clip(const int32_t B, const int32_t T, const int32_t H, const float* current_log_prob,
+                   const float* old_log_prob, const float* advantage, const float clip_epsilon, float* output);
+
+/* Extended form (no reference counterpart; the BASELINE RL-pipeline metric set): also reads a
+ * per-sample entropy stream and writes a 7th output, its mean. */
+void b200_ppo_clip_ext(const int32_t B, const int32_t T, const int32_t H, const float* current_log_prob,
+                       const float* old_log_prob, const float* advantage, const float* entropy,
+                       const float clip_epsilon, float* output);
+
+/* Stream form over n samples; entropy may be NULL (6 outputs) or a stream (7 outputs).
+ * workspace: b200_ppo_workspace_bytes(n) bytes, zero-filled once before first use. */
+size_t b200_ppo_workspace_bytes(int64_t n);
+int b200_ppo_async(const float* current_log_prob, const float* old_log_prob, const float* advantage,
+                   const float* entropy, int64_t n, float clip_epsilon, float* output, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Multi-GPU halves: one b200_ppo_partial_bytes() record per chunk of b200_ppo_chunk_elems()
+ * samples; shards start on chunk boundaries; finish is bit-identical to the one-device form. */
+int64_t b200_ppo_chunk_elems(void);
+size_t b200_ppo_partial_bytes(void);
+int b200_ppo_shard_partials(const float* current_log_prob, const float* old_log_prob, const float* advantage,
+                            const float* entropy, int64_t n, float clip_epsilon, void* partials, void* stream);
+int b200_ppo_finish(const void* partials, int64_t n_partials, int64_t n_total, int with_entropy, float* output,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Discounted reward-to-go with done flags (task reward_to_go).
+ * Replaces `void reference(const float* reward, const bool* done, float gamma, int32_t B,
+ * int32_t T, float* output)`: tasks/reward_to_go/tests/task.json:3,
+ * reference/reward_to_go/solution.cu:237.
+ * ------------------------------------------------------------------------------------------- */
+void b200_reward_to_go(const float* reward, const bool* done, float gamma, int32_t B, int32_t T, float* output);
+int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                            float* output, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Leaky integrate-and-fire layer (task leaky).
+ * Replaces `void reference(const float* input_current, const float* mem0, const float* beta,
+ * const float* threshold, int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem)`:
+ * tasks/leaky/tests/task.json:3, reference/leaky/solution.cu:106.
+ * ------------------------------------------------------------------------------------------- */
+void b200_leaky(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem);
+int b200_leaky_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                     int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200OPS_H */
