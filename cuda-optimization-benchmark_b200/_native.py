@@ -21,6 +21,7 @@ c_str = ctypes.c_char_p
 SIGNATURES = {
     "b200_status_string": (c_str, [c_int]),
     "b200_last_status": (c_int, []),
+    "b200_device_fault": (c_int, []),
     # robust-L1
     "b200_pow_abs_sqrt_mean": (None, [c_p, c_p, c_i64, c_i64, c_i64, c_p]),
     "b200_robust_l1_workspace_bytes": (c_sz, [c_i64]),

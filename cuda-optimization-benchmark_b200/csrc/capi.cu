@@ -25,6 +25,15 @@ extern "C" {
 const char* b200_status_string(int status) { return b200::status_string(status); }
 int b200_last_status(void) { return g_last_status; }
 
+int b200_device_fault(void) {
+  unsigned v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, b200::g_b200_fault, sizeof(v)) != cudaSuccess) return -1;
+  const unsigned zero = 0;
+  if (cudaMemcpyToSymbol(b200::g_b200_fault, &zero, sizeof(zero)) != cudaSuccess) return -1;
+  return int(v);
+}
+
 // ---------------------------------------------------------------------------------- robust-L1
 void b200_pow_abs_sqrt_mean(const float* inp, const float* target, int64_t batch_size, int64_t height,
                             int64_t width, float* output) {

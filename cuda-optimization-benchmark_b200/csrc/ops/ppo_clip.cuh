@@ -12,31 +12,48 @@
 // Per element (lw = cur - old):
 //   ratio r = exp(lw); clipped = lw < log1p(-eps) or lw > log1p(eps);
 //   gain = min(r*adv, exp(clamp(lw))*adv)  (exp(clamp(lw)) is 1-eps / 1+eps when clipped, else r)
-//   kl   = (r - 1) - lw  (evaluated as expm1(lw) - lw to avoid cancellation)
+//   kl   = (r - 1) - lw
 // Reductions: sum gain, count clipped, sum kl, sum r, sum r^2, max r, [sum entropy].
 // ESS = exp(2 lse(lw) - lse(2 lw)) / N = (sum r)^2 / (sum r^2) / N.
 //
-// B200 design: 12 (16 with entropy) bytes per element streamed with 128-bit loads; fixed global
-// chunking with one 48-byte partial per chunk, fp32 per-thread accumulation and fp64 above it;
-// single-launch finish by the last CTA.  Deterministic for any grid and any chunk-aligned split
-// across GPUs.  The clip decision matches the fp64 oracle exactly: lw is formed in fp32 and only
-// elements within 1e-6 of a clip boundary are re-decided in fp64.  Elements with lw > 30 (outside
-// the reference's stated input range, where r^2 could overflow fp32 sums) take an fp64 path.
+// B200 design.  12 (16 with entropy) bytes per element.  The element range is cut into fixed
+// chunks of kChunk elements, each reduced by one CTA in a fixed order into a 48-byte partial
+// (fp32 per thread, fp64 above), and the last CTA to finish combines the partials in chunk order:
+// the result is bit-identical for any grid, any pointer alignment, and any chunk-aligned split of
+// the range across GPUs (the multi-GPU path gathers the same partials and runs the same finish).
+// Aligned inputs stream through a TMA bulk-copy pipeline: a producer warp keeps kStages chunks
+// (48-64 KB each) in flight into shared memory with cp.async.bulk while 8 consumer warps reduce
+// the resident chunk, so loads never wait for compute.  The clip decision matches the fp64
+// oracle exactly: it is taken in fp32 and re-taken in fp64 for elements within 1e-6 of a clip
+// boundary.  Elements with lw > 30 (outside the reference's stated input range, where r^2 could
+// overflow fp32 sums) take an fp64 path.
 #pragma once
 
 #include <math.h>
 
 #include "../common/b200_common.cuh"
+#include "../common/bulk.cuh"
 #include "../common/workspace.cuh"
 
 namespace b200 {
 namespace ppo {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;                                       // consumer threads
 constexpr int kVecPerThread = 4;                                    // float4 per input per thread
 constexpr int64_t kChunk = int64_t(kThreads) * kVecPerThread * 4;  // 4096 elements per chunk
+constexpr int kPipeThreads = kThreads + 32;                         // + one producer warp
+constexpr uint32_t kRedBar = 1;                                     // named barrier of the consumers
 constexpr int kOutputs = 6;
 constexpr int kOutputsExt = 7;
+
+template <bool kEnt>
+struct Pipe {
+  static constexpr int kArrays = kEnt ? 4 : 3;
+  static constexpr int kArrayBytes = int(kChunk) * 4;
+  static constexpr int kStageBytes = kArrays * kArrayBytes;
+  static constexpr int kStages = kEnt ? 3 : 4;
+  static constexpr int kSmem = kStages * kStageBytes;
+};
 
 struct __align__(16) Partial {
   double gain, kl, r, r2, ent;
@@ -48,7 +65,7 @@ static_assert(sizeof(Partial) == 48, "partial layout");
 // Clip constants derived on the host from the fp32 epsilon, in fp64 like the oracle.
 struct Clip {
   double lo_d, hi_d;   // log1p(-eps), log1p(eps)
-  float lo_f, hi_f;    // the same rounded to fp32 (fast decision away from the boundary)
+  float mid, hw;       // centre and half-width of [lo, hi] in fp32 (fast decision)
   float down, up;      // exp(log1p(-eps)), exp(log1p(eps)) rounded to fp32
 };
 
@@ -57,8 +74,8 @@ inline Clip make_clip(float eps) {
   const double e = double(eps);
   c.lo_d = log1p(-e);
   c.hi_d = log1p(e);
-  c.lo_f = float(c.lo_d);
-  c.hi_f = float(c.hi_d);
+  c.mid = float(0.5 * (c.lo_d + c.hi_d));
+  c.hw = float(0.5 * (c.hi_d - c.lo_d));
   c.down = float(exp(c.lo_d));
   c.up = float(exp(c.hi_d));
   return c;
@@ -75,28 +92,30 @@ struct Acc {
 
 __device__ __forceinline__ void add_element(Acc& acc, float cur, float old, float adv, const Clip& c) {
   const float lw = __fsub_rn(cur, old);
-  bool lo = lw < c.lo_f, hi = lw > c.hi_f;
-  // Near a boundary the fp32 difference may sit on the other side of the fp64 one: redo it in fp64.
-  if (fabsf(__fsub_rn(lw, c.hi_f)) < 1e-6f || fabsf(__fsub_rn(lw, c.lo_f)) < 1e-6f) {
+  const float dm = __fsub_rn(lw, c.mid);
+  const float adm = fabsf(dm);
+  bool clipped = adm > c.hw;
+  bool below = dm < 0.0f;
+  // Within 1e-6 of a boundary the fp32 decision may differ from the fp64 one: take it in fp64.
+  if (fabsf(__fsub_rn(adm, c.hw)) < 1e-6f) {
     const double lwd = double(cur) - double(old);
-    lo = lwd < c.lo_d;
-    hi = lwd > c.hi_d;
+    below = lwd < c.lo_d;
+    clipped = below || lwd > c.hi_d;
   }
-  acc.clipped += (lo || hi) ? 1u : 0u;
+  acc.clipped += clipped ? 1u : 0u;
   if (lw <= 30.0f) {
-    const float em1 = expm1f(lw);
-    const float r = __fadd_rn(em1, 1.0f);
-    const float rc = lo ? c.down : (hi ? c.up : r);
+    const float r = __expf(lw);
+    const float rc = clipped ? (below ? c.down : c.up) : r;
     const float g = fminf(__fmul_rn(r, adv), __fmul_rn(rc, adv));
     acc.gain = __fadd_rn(acc.gain, g);
-    acc.kl = __fadd_rn(acc.kl, __fsub_rn(em1, lw));
+    acc.kl = __fadd_rn(acc.kl, __fsub_rn(__fsub_rn(r, 1.0f), lw));
     acc.r = __fadd_rn(acc.r, r);
     acc.r2 = __fmaf_rn(r, r, acc.r2);
     acc.rmax = fmaxf(acc.rmax, r);
   } else {
     const double lwd = double(cur) - double(old);
     const double r = exp(lwd);
-    const double rc = hi ? exp(c.hi_d) : r;
+    const double rc = exp(c.hi_d);
     acc.big_gain += fmin(r * double(adv), rc * double(adv));
     acc.big_kl += (r - 1.0) - lwd;
     acc.big_r += r;
@@ -105,11 +124,27 @@ __device__ __forceinline__ void add_element(Acc& acc, float cur, float old, floa
   }
 }
 
-// Per-thread pass over elements (k*kThreads + t)*4 + j of one chunk, same order on every path.
+template <bool kEnt>
+__device__ __forceinline__ void add4(Acc& acc, float4 c4, float4 o4, float4 a4, float4 e4, const Clip& c) {
+  add_element(acc, c4.x, o4.x, a4.x, c);
+  add_element(acc, c4.y, o4.y, a4.y, c);
+  add_element(acc, c4.z, o4.z, a4.z, c);
+  add_element(acc, c4.w, o4.w, a4.w, c);
+  if (kEnt) {
+    acc.ent = __fadd_rn(acc.ent, e4.x);
+    acc.ent = __fadd_rn(acc.ent, e4.y);
+    acc.ent = __fadd_rn(acc.ent, e4.z);
+    acc.ent = __fadd_rn(acc.ent, e4.w);
+  }
+}
+
+// Per-thread pass over elements (k*kThreads + t)*4 + j of one chunk straight from global memory
+// (k outer, j inner: the same order as the pipelined path), skipping elements past n.
 template <bool kVec, bool kEnt>
-__device__ __forceinline__ void thread_chunk(Acc& acc, const float* __restrict__ cur, const float* __restrict__ old,
-                                             const float* __restrict__ adv, const float* __restrict__ ent,
-                                             int64_t base, int64_t n, const Clip& c) {
+__device__ __forceinline__ void thread_chunk_global(Acc& acc, const float* __restrict__ cur,
+                                                    const float* __restrict__ old, const float* __restrict__ adv,
+                                                    const float* __restrict__ ent, int64_t base, int64_t n,
+                                                    const Clip& c) {
   const int t = threadIdx.x;
   if (kVec && base + kChunk <= n) {
     float4 vc[kVecPerThread], vo[kVecPerThread], va[kVecPerThread], ve[kVecPerThread];
@@ -119,21 +154,10 @@ __device__ __forceinline__ void thread_chunk(Acc& acc, const float* __restrict__
       vc[k] = ld_stream_f4(cur + i);
       vo[k] = ld_stream_f4(old + i);
       va[k] = ld_stream_f4(adv + i);
-      if (kEnt) ve[k] = ld_stream_f4(ent + i);
+      ve[k] = kEnt ? ld_stream_f4(ent + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
-    for (int k = 0; k < kVecPerThread; ++k) {
-      add_element(acc, vc[k].x, vo[k].x, va[k].x, c);
-      add_element(acc, vc[k].y, vo[k].y, va[k].y, c);
-      add_element(acc, vc[k].z, vo[k].z, va[k].z, c);
-      add_element(acc, vc[k].w, vo[k].w, va[k].w, c);
-      if (kEnt) {
-        acc.ent = __fadd_rn(acc.ent, ve[k].x);
-        acc.ent = __fadd_rn(acc.ent, ve[k].y);
-        acc.ent = __fadd_rn(acc.ent, ve[k].z);
-        acc.ent = __fadd_rn(acc.ent, ve[k].w);
-      }
-    }
+    for (int k = 0; k < kVecPerThread; ++k) add4<kEnt>(acc, vc[k], vo[k], va[k], ve[k], c);
   } else {
 #pragma unroll 1
     for (int k = 0; k < kVecPerThread; ++k) {
@@ -150,7 +174,8 @@ __device__ __forceinline__ void thread_chunk(Acc& acc, const float* __restrict__
   }
 }
 
-// Fixed-order CTA reduction of the per-thread accumulators into one chunk partial (thread 0).
+// Fixed-order reduction of the consumer threads' accumulators into one chunk partial (valid in
+// thread 0).  Uses a named barrier over the kThreads consumer threads only.
 __device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
   __shared__ double s_d[5][kThreads / 32];
   __shared__ float s_max[kThreads / 32];
@@ -168,7 +193,7 @@ __device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
     s_max[w] = m;
     s_cnt[w] = cnt;
   }
-  __syncthreads();
+  named_sync(kRedBar, kThreads);
   Partial p{};
   if (threadIdx.x == 0) {
     p.gain = p.kl = p.r = p.r2 = p.ent = 0.0;
@@ -185,12 +210,12 @@ __device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
       p.clipped += s_cnt[i];
     }
   }
-  __syncthreads();
+  named_sync(kRedBar, kThreads);
   return p;
 }
 
-// Final combination of partials[0..n_parts) in a fixed order; writes 6 (or 7) outputs.
-// Every ratio is > 0, so 0 is the identity of the max.
+// Final combination of partials[0..n_parts) in a fixed order by the kThreads consumer threads;
+// writes 6 (or 7) outputs.  Every ratio is > 0, so 0 is the identity of the max.
 __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, int64_t n_total, bool ext, float* out) {
   __shared__ double s_d[5][kThreads / 32];
   __shared__ float s_max[kThreads / 32];
@@ -217,7 +242,7 @@ __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, in
     s_max[w] = m;
     s_cnt[w] = cnt;
   }
-  __syncthreads();
+  named_sync(kRedBar, kThreads);
   if (threadIdx.x == 0) {
     double t[5] = {0, 0, 0, 0, 0};
     float mx = 0.f;
@@ -239,6 +264,7 @@ __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, in
   }
 }
 
+// Direct form (unaligned inputs): CTA c handles chunks c, c + gridDim.x, ... from global memory.
 template <bool kVec, bool kEnt, bool kFinish>
 __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict__ cur, const float* __restrict__ old,
                                                          const float* __restrict__ adv, const float* __restrict__ ent,
@@ -247,7 +273,7 @@ __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict
   const int64_t n_chunks = (n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     Acc acc;
-    thread_chunk<kVec, kEnt>(acc, cur, old, adv, ent, c * kChunk, n, clip);
+    thread_chunk_global<kVec, kEnt>(acc, cur, old, adv, ent, c * kChunk, n, clip);
     const Partial p = cta_reduce(acc);
     if (threadIdx.x == 0) partials[c] = p;
   }
@@ -256,15 +282,100 @@ __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict
   }
 }
 
+// Pipelined form (16-byte aligned inputs).  Warps 0-7 consume, warp 8 produces.  Full chunks go
+// through the bulk-copy ring; a trailing partial chunk is reduced from global memory by the CTA
+// that owns it, with the same element order.
+template <bool kEnt, bool kFinish>
+__global__ void __launch_bounds__(kPipeThreads, 1)
+    pipe_kernel(const float* __restrict__ cur, const float* __restrict__ old, const float* __restrict__ adv,
+                const float* __restrict__ ent, int64_t n, Clip clip, Partial* __restrict__ partials,
+                unsigned* __restrict__ ticket, float* __restrict__ out) {
+  using P = Pipe<kEnt>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t full[P::kStages], empty[P::kStages];
+  const int64_t n_chunks = (n + kChunk - 1) / kChunk;
+  const int64_t n_full = n / kChunk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kThreads / 32);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kThreads / 32) {
+    // Producer: one lane keeps the ring full.
+    if (lane == 0) {
+      const float* src[4] = {cur, old, adv, ent};
+      uint32_t i = 0;
+      for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x, ++i) {
+        const uint32_t s = i % P::kStages, ph = (i / P::kStages) & 1u;
+        mbar_wait(&empty[s], ph ^ 1u);
+        mbar_arrive_expect_tx(&full[s], P::kStageBytes);
+        unsigned char* dst = smem + s * P::kStageBytes;
+#pragma unroll
+        for (int a = 0; a < P::kArrays; ++a)
+          bulk_g2s(dst + a * P::kArrayBytes, src[a] + c * kChunk, P::kArrayBytes, &full[s]);
+      }
+    }
+  } else {
+    uint32_t i = 0;
+    for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x, ++i) {
+      const uint32_t s = i % P::kStages, ph = (i / P::kStages) & 1u;
+      mbar_wait(&full[s], ph);
+      const float* st = reinterpret_cast<const float*>(smem + s * P::kStageBytes);
+      Acc acc;
+#pragma unroll
+      for (int k = 0; k < kVecPerThread; ++k) {
+        const int e = (k * kThreads + threadIdx.x) * 4;
+        const float4 c4 = *reinterpret_cast<const float4*>(st + e);
+        const float4 o4 = *reinterpret_cast<const float4*>(st + kChunk + e);
+        const float4 a4 = *reinterpret_cast<const float4*>(st + 2 * kChunk + e);
+        const float4 e4 = kEnt ? *reinterpret_cast<const float4*>(st + 3 * kChunk + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+        add4<kEnt>(acc, c4, o4, a4, e4, clip);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      const Partial p = cta_reduce(acc);
+      if (threadIdx.x == 0) partials[c] = p;
+    }
+    if (n_full < n_chunks && (n_chunks - 1) % gridDim.x == blockIdx.x) {
+      Acc acc;
+      thread_chunk_global<true, kEnt>(acc, cur, old, adv, ent, (n_chunks - 1) * kChunk, n, clip);
+      const Partial p = cta_reduce(acc);
+      if (threadIdx.x == 0) partials[n_chunks - 1] = p;
+    }
+  }
+  if (kFinish) {
+    const bool last = elect_last_cta(ticket);
+    if (last && threadIdx.x < kThreads) finish(partials, n_chunks, n, kEnt, out);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) finish_kernel(const Partial* __restrict__ partials, int64_t n_parts,
                                                           int64_t n_total, int ext, float* __restrict__ out) {
   finish(partials, n_parts, n_total, ext != 0, out);
 }
 
-template <bool kVec, bool kEnt, bool kFinish>
-inline void launch_one(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
-                       const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
-  auto kern = chunk_kernel<kVec, kEnt, kFinish>;
+template <bool kEnt, bool kFinish>
+inline void launch_pipe(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
+                        const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
+  auto kern = pipe_kernel<kEnt, kFinish>;
+  static bool configured = false;  // per instantiation; the attribute is per function
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Pipe<kEnt>::kSmem);
+    configured = true;
+  }
+  const int grid = balanced_grid(num_chunks(n), 1);
+  kern<<<grid, kPipeThreads, Pipe<kEnt>::kSmem, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, out);
+}
+
+template <bool kEnt, bool kFinish>
+inline void launch_direct(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
+                          const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
+  auto kern = chunk_kernel<false, kEnt, kFinish>;
   const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
   kern<<<grid, kThreads, 0, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, out);
 }
@@ -274,11 +385,11 @@ inline void launch_chunks(const float* cur, const float* old, const float* adv, 
                           const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
   const bool vec = aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
   if (ent != nullptr) {
-    if (vec) launch_one<true, true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-    else launch_one<false, true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    if (vec) launch_pipe<true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    else launch_direct<true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
   } else {
-    if (vec) launch_one<true, false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-    else launch_one<false, false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    if (vec) launch_pipe<false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    else launch_direct<false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
   }
 }
 

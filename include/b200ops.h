@@ -40,6 +40,12 @@ extern "C" {
 const char* b200_status_string(int status);
 int b200_last_status(void);
 
+/* Device-side fault word of the current device: bit 0 = a bounded wait inside a kernel gave up
+ * (its results are then unreliable).  Synchronizes the device, returns the word (or -1 when the
+ * read itself fails) and clears it.  No reference counterpart: the reference's kernels have no
+ * waits. */
+int b200_device_fault(void);
+
 /* ---------------------------------------------------------------------------------------------
  * Robust-L1 mean (task pow_abs_sqrt_mean): output[0] = mean(sqrt((inp - target)^2 + 1e-6)).
  * Replaces `void reference(const float* inp, const float* target, int64_t batch_size,
