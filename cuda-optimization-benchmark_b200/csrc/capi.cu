@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/b200ops.h"
+#include "ops/fp8_linear.cuh"
 #include "ops/lif.cuh"
 #include "ops/ppo_clip.cuh"
 #include "ops/reward_to_go.cuh"
@@ -132,6 +133,30 @@ void b200_leaky(const float* input_current, const float* mem0, const float* beta
 int b200_leaky_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
                      int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, void* stream) {
   return b200::lif::run(input_current, mem0, beta, threshold, T, B, H, spikes, final_mem, as_stream(stream));
+}
+
+// --------------------------------------------------------------------------------- FP8 linear
+void b200_fp8_linear(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8, float scale_x,
+                     const uint8_t* w_fp8, float scale_w, const uint16_t* bias, uint16_t* output) {
+  record(b200::fp8::run(M, K, N, x_fp8, scale_x, w_fp8, scale_w, bias, output, nullptr));
+}
+
+int b200_fp8_linear_async(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8, float scale_x,
+                          const uint8_t* w_fp8, float scale_w, const uint16_t* bias, uint16_t* output,
+                          void* stream) {
+  return b200::fp8::run(M, K, N, x_fp8, scale_x, w_fp8, scale_w, bias, output, as_stream(stream));
+}
+
+int b200_fp8_linear_cuda_core_async(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8,
+                                    float scale_x, const uint8_t* w_fp8, float scale_w, const uint16_t* bias,
+                                    uint16_t* output, void* stream) {
+  return b200::fp8::run_simt(M, K, N, x_fp8, scale_x, w_fp8, scale_w, bias, output, as_stream(stream));
+}
+
+int b200_fp8_linear_plan(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8,
+                         const uint8_t* w_fp8) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return b200::fp8::plan_bn(M, N, K, x_fp8, w_fp8);
 }
 
 }  // extern "C"

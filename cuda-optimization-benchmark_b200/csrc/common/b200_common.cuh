@@ -79,6 +79,28 @@ inline int resident_ctas_per_sm(Kernel kernel, int threads, size_t dyn_smem) {
   return n;
 }
 
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device).  Returns false when the
+// runtime refuses.
+template <typename Kernel>
+inline bool ensure_dyn_smem(Kernel kernel, int bytes) {
+  struct Entry {
+    const void* fn;
+    int dev;
+  };
+  static Entry done[256];
+  static int used = 0;
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const void* key = reinterpret_cast<const void*>(kernel);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (done[i].fn == key && done[i].dev == dev) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  if (used < 256) done[used++] = Entry{key, dev};
+  return true;
+}
+
 // CTAs for a single-wave grid over `units` equal work units: at most the resident capacity, and
 // sized so every CTA gets the same number of units (up to one).
 inline int balanced_grid(int64_t units, int ctas_per_sm) {

@@ -363,11 +363,7 @@ template <bool kEnt, bool kFinish>
 inline void launch_pipe(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
                         const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
   auto kern = pipe_kernel<kEnt, kFinish>;
-  static bool configured = false;  // per instantiation; the attribute is per function
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Pipe<kEnt>::kSmem);
-    configured = true;
-  }
+  ensure_dyn_smem(kern, Pipe<kEnt>::kSmem);
   const int grid = balanced_grid(num_chunks(n), 1);
   kern<<<grid, kPipeThreads, Pipe<kEnt>::kSmem, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, out);
 }

@@ -125,6 +125,28 @@ void b200_leaky(const float* input_current, const float* mem0, const float* beta
 int b200_leaky_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
                      int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * FP8 E4M3 linear layer (task fp8_linear): output[M, N] (bf16) =
+ * (x_fp8[M, K] . w_fp8[N, K]^T) / (scale_x * scale_w) + bias[N].
+ * Replaces `void reference(const int32_t M, const int32_t K, const int32_t N,
+ * const __nv_fp8_e4m3* x_fp8, float scale_x, const __nv_fp8_e4m3* w_fp8, float scale_w,
+ * const __nv_bfloat16* bias, __nv_bfloat16* output)`: tasks/fp8_linear/tests/task.json:3,
+ * reference/fp8_linear/solution.cu:276.  x_fp8 / w_fp8 are E4M3 bytes, bias / output bf16 bits.
+ * ------------------------------------------------------------------------------------------- */
+void b200_fp8_linear(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8, float scale_x,
+                     const uint8_t* w_fp8, float scale_w, const uint16_t* bias, uint16_t* output);
+int b200_fp8_linear_async(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8, float scale_x,
+                          const uint8_t* w_fp8, float scale_w, const uint16_t* bias, uint16_t* output,
+                          void* stream);
+/* The CUDA-core path alone (any shape and alignment), for cross-checking the tensor-core path. */
+int b200_fp8_linear_cuda_core_async(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8,
+                                    float scale_x, const uint8_t* w_fp8, float scale_w, const uint16_t* bias,
+                                    uint16_t* output, void* stream);
+/* Tile width the tensor-core path would use for this call (256, 128 or 64), or 0 when the call
+ * takes the CUDA-core path (K not a multiple of 16, or an operand not 16-byte aligned). */
+int b200_fp8_linear_plan(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8,
+                         const uint8_t* w_fp8);
+
 #ifdef __cplusplus
 }
 #endif

@@ -168,10 +168,14 @@ def fp8_linear(inp, rows=None):
     xq = _np(inp["x_fp8"]).astype(np.uint8)
     if rows is not None:
         xq = xq[rows]
-    x = tab[xq] / float(inp["scale_x"])
-    w = tab[_np(inp["w_fp8"]).astype(np.uint8)] / float(inp["scale_w"])
+    x = tab[xq]
+    x /= float(inp["scale_x"])
+    w = tab[_np(inp["w_fp8"]).astype(np.uint8)]
+    w /= float(inp["scale_w"])
     bias = bf16_bits_to_f64(_np(inp["bias"]))
-    y = x @ w.T + bias[None, :]
+    y = x @ w.T
+    del w
+    y += bias[None, :]
     return {"output": f32_to_bf16_bits(y.astype(np.float32)), "output_f64": y}
 
 
