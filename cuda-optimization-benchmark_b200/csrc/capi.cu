@@ -8,6 +8,7 @@
 
 #include "../../include/b200ops.h"
 #include "ops/fp8_linear.cuh"
+#include "ops/kan.cuh"
 #include "ops/lif.cuh"
 #include "ops/ppo_clip.cuh"
 #include "ops/reward_to_go.cuh"
@@ -157,6 +158,32 @@ int b200_fp8_linear_plan(const int32_t M, const int32_t K, const int32_t N, cons
                          const uint8_t* w_fp8) {
   if (M <= 0 || K <= 0 || N <= 0) return 0;
   return b200::fp8::plan_bn(M, N, K, x_fp8, w_fp8);
+}
+
+// ----------------------------------------------------------------------------------------- KAN
+void b200_efficient_kan(const float* x, const float* grid, const float* base_weight, const float* spline_weight,
+                        const float* spline_scaler, int32_t grid_size, int32_t spline_order, int32_t B, int32_t I,
+                        int32_t O, float* out) {
+  if (B < 0 || I < 0 || O < 0 || grid_size < 1 || spline_order < 0) return record(b200::kInvalidArgument);
+  int st = 0;
+  const size_t ws = b200::kan::workspace_bytes(B, I, O, grid_size + spline_order);
+  void* w = b200::arena_get(ws, nullptr, &st);
+  if (st != 0) return record(st);
+  record(b200::kan::run(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, B, I, O, out, w,
+                        ws, nullptr));
+}
+
+size_t b200_efficient_kan_workspace_bytes(int32_t grid_size, int32_t spline_order, int32_t B, int32_t I, int32_t O) {
+  if (B < 0 || I < 0 || O < 0 || grid_size < 1 || spline_order < 0) return 0;
+  return b200::kan::workspace_bytes(B, I, O, grid_size + spline_order);
+}
+
+int b200_efficient_kan_async(const float* x, const float* grid, const float* base_weight, const float* spline_weight,
+                             const float* spline_scaler, int32_t grid_size, int32_t spline_order, int32_t B,
+                             int32_t I, int32_t O, float* out, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  return b200::kan::run(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, B, I, O, out,
+                        workspace, workspace_bytes, as_stream(stream));
 }
 
 }  // extern "C"

@@ -79,13 +79,15 @@ inline int resident_ctas_per_sm(Kernel kernel, int threads, size_t dyn_smem) {
   return n;
 }
 
-// Raise a kernel's dynamic shared-memory limit once per (kernel, device).  Returns false when the
-// runtime refuses.
+// Make sure a kernel may use `bytes` of dynamic shared memory on the current device: the limit
+// recorded per (kernel, device) is raised whenever a launch needs more than any earlier one.
+// Returns false when the runtime refuses.
 template <typename Kernel>
 inline bool ensure_dyn_smem(Kernel kernel, int bytes) {
   struct Entry {
     const void* fn;
     int dev;
+    int bytes;
   };
   static Entry done[256];
   static int used = 0;
@@ -94,10 +96,13 @@ inline bool ensure_dyn_smem(Kernel kernel, int bytes) {
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const void* key = reinterpret_cast<const void*>(kernel);
   std::lock_guard<std::mutex> lock(mu);
+  Entry* e = nullptr;
   for (int i = 0; i < used; ++i)
-    if (done[i].fn == key && done[i].dev == dev) return true;
+    if (done[i].fn == key && done[i].dev == dev) e = &done[i];
+  if (e != nullptr && e->bytes >= bytes) return true;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
-  if (used < 256) done[used++] = Entry{key, dev};
+  if (e != nullptr) e->bytes = bytes;
+  else if (used < 256) done[used++] = Entry{key, dev, bytes};
   return true;
 }
 

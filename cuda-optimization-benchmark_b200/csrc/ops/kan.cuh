@@ -1,0 +1,380 @@
+// KAN linear layer (efficient-kan KANLinear forward):
+//   out[b, o] = sum_i silu(x[b,i]) * W_base[o,i] + sum_i sum_c basis_c(x[b,i]) * sw[o,i,c] * scaler[o,i]
+// with the C = G + K cubic (order K) B-spline bases of x on each input's knot grid (Cox-de Boor).
+//
+// Reference semantics: tasks/efficient_kan/reference.py:33-46 (fp64 oracle :54-57), tolerance
+// 1e-5/1e-5 (tasks/efficient_kan/tests/task.json).  The drop-in boundary it replaces is
+// `void reference(const float* x, const float* grid, const float* base_weight, const float*
+// spline_weight, const float* spline_scaler, int32_t grid_size, int32_t spline_order, int32_t B,
+// int32_t I, int32_t O, float* out)` (task.json:3; expert launcher
+// reference/efficient_kan/solution.cu:177-288, which builds A and W and calls cuBLAS).
+//
+// B200 design.  The op is one GEMM out = A . W'^T over K' = I*(1+C): A[b, p*I + i] holds silu(x)
+// (p = 0) and basis p-1 (p >= 1), W'[o, p*I + i] holds W_base (p = 0) and sw*scaler (p >= 1).
+// The 1e-5 tolerance against fp64 rules out a single fp16/bf16/tf32 pass, so every operand value
+// v is split into fp16 v_hi = fp16(v) and v_lo = fp16((v - v_hi) * 2^11) (22 significant bits
+// together), and the tensor cores form
+//   D0 = A_hi . W_hi^T      D1 = A_hi . W_lo^T + A_lo . W_hi^T      out = D0 + D1 * 2^-11
+// in two fp32 TMEM accumulators (the dropped A_lo . W_lo term is 2^-22 relative).  Rows of A and
+// of W' are scaled by powers of two so every value fits fp16; the epilogue undoes them.
+//   1. prep_w_kernel: W' hi/lo planes (one CTA per output row);
+//   2. prep_a_kernel: silu + Cox-de Boor bases of x in fp32, hi/lo planes (one CTA per batch row);
+//   3. gemm_kernel: persistent warp-specialised tcgen05 GEMM (kind::f16, 128 x 256 tiles,
+//      128-byte-swizzled TMA loads of the four planes, 12 MMAs per stage), fused combine/rescale
+//      epilogue writing fp32 rows.
+// Planes are K-padded to a multiple of 64 with zeros so every TMA row pitch is 16-byte aligned.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "../common/b200_common.cuh"
+#include "../common/bulk.cuh"
+#include "../common/tcgen05.cuh"
+#include "../common/workspace.cuh"
+
+namespace b200 {
+namespace kan {
+
+constexpr int kMaxKnots = 64;  // G + 2K + 1 knots per input at most
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBKe = 64;       // fp16 elements of K per stage (one 128-byte swizzle row)
+constexpr int kUmmaK = 16;     // K per tcgen05.mma for 16-bit operands
+constexpr int kThreads = 192;  // warp 0 loads, warp 1 issues MMAs, warps 2-5 epilogue
+constexpr int kGroupM = 8;
+constexpr float kLoScale = 2048.0f;      // 2^11
+constexpr float kLoUnscale = 1.0f / 2048.0f;
+constexpr float kFp16Safe = 16384.0f;    // rows are scaled so |value| < 2^14
+
+constexpr int kATile = kBM * kBKe * 2;   // 16 KB per A plane per stage
+constexpr int kWTile = kBN * kBKe * 2;   // 32 KB per W plane per stage
+constexpr int kStage = 2 * kATile + 2 * kWTile;  // 96 KB
+constexpr int kStages = 2;
+constexpr int kSmem = kStages * kStage + 1024;
+constexpr int kTmemCols = 2 * kBN;       // D0 and D1
+
+inline int64_t padded_k(int I, int C) { return (int64_t(I) * (1 + C) + kBKe - 1) / kBKe * kBKe; }
+
+// Workspace layout (all 256-byte aligned): A_hi, A_lo [B][Kp] fp16; W_hi, W_lo [O][Kp] fp16;
+// row scales rs[B], col scales cs[O] (fp32 powers of two).
+struct Layout {
+  size_t a_hi, a_lo, w_hi, w_lo, rs, cs, total;
+};
+
+inline Layout layout(int B, int I, int O, int C) {
+  const int64_t kp = padded_k(I, C);
+  Layout L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align256(bytes);
+    return at;
+  };
+  L.a_hi = take(size_t(B) * kp * 2);
+  L.a_lo = take(size_t(B) * kp * 2);
+  L.w_hi = take(size_t(O) * kp * 2);
+  L.w_lo = take(size_t(O) * kp * 2);
+  L.rs = take(size_t(B) * 4);
+  L.cs = take(size_t(O) * 4);
+  L.total = off;
+  return L;
+}
+
+// Power-of-two factor f (f <= 1) with amax * f < 2^14.
+__device__ __forceinline__ float fp16_row_factor(float amax) {
+  float f = 1.0f;
+  while (amax * f >= kFp16Safe && f > 1e-30f) f *= 0.5f;
+  return f;
+}
+
+__device__ __forceinline__ void split_store(float v, __half* hi, __half* lo) {
+  const __half h = __float2half_rn(v);
+  *hi = h;
+  *lo = __float2half_rn((v - __half2float(h)) * kLoScale);
+}
+
+__device__ __forceinline__ float block_max(float v, float* s_red) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float m = threadIdx.x < (blockDim.x >> 5) ? s_red[threadIdx.x] : 0.0f;
+    m = warp_max(m);
+    if (threadIdx.x == 0) s_red[32] = m;
+  }
+  __syncthreads();
+  const float r = s_red[32];
+  __syncthreads();
+  return r;
+}
+
+// ---------------------------------------------------------------------------------- W' planes
+// One CTA per output row o.  w'(p=0, i) = W_base[o,i]; w'(p=1+c, i) = sw[o,i,c] * scaler[o,i]
+// (the fp32 product the reference forms, tasks/efficient_kan/reference.py:45).
+__global__ void __launch_bounds__(256) prep_w_kernel(const float* __restrict__ wb, const float* __restrict__ sw,
+                                                     const float* __restrict__ sc, int I, int O, int C, int64_t kp,
+                                                     __half* __restrict__ w_hi, __half* __restrict__ w_lo,
+                                                     float* __restrict__ cs) {
+  __shared__ float s_red[33];
+  const int o = blockIdx.x;
+  const int64_t kk = int64_t(I) * (1 + C);
+  float amax = 0.0f;
+  for (int64_t q = threadIdx.x; q < kk; q += blockDim.x) {
+    const int p = int(q / I), i = int(q - int64_t(p) * I);
+    const float v = p == 0 ? wb[int64_t(o) * I + i]
+                           : __fmul_rn(sw[(int64_t(o) * I + i) * C + (p - 1)], sc[int64_t(o) * I + i]);
+    amax = fmaxf(amax, fabsf(v));
+  }
+  const float f = fp16_row_factor(block_max(amax, s_red));
+  if (threadIdx.x == 0) cs[o] = 1.0f / f;
+  __half* hr = w_hi + int64_t(o) * kp;
+  __half* lr = w_lo + int64_t(o) * kp;
+  for (int64_t q = threadIdx.x; q < kp; q += blockDim.x) {
+    float v = 0.0f;
+    if (q < kk) {
+      const int p = int(q / I), i = int(q - int64_t(p) * I);
+      v = p == 0 ? wb[int64_t(o) * I + i]
+                 : __fmul_rn(sw[(int64_t(o) * I + i) * C + (p - 1)], sc[int64_t(o) * I + i]);
+    }
+    split_store(v * f, hr + q, lr + q);
+  }
+}
+
+// -------------------------------------------------------------------------------- A planes
+// silu(x) and the C bases of x on knots g[0..nk) (nk = G + 2K + 1) by the Cox-de Boor recurrence
+// of tasks/efficient_kan/reference.py:33-39: order-0 indicators g[j] <= x < g[j+1], then K rounds
+// b[j] = (x - g[j]) / (g[j+k] - g[j]) * b[j] + (g[j+k+1] - x) / (g[j+k+1] - g[j+1]) * b[j+1].
+__device__ __forceinline__ void bases_of(float x, const float* g, int nk, int K, float* b) {
+  for (int j = 0; j < nk - 1; ++j) b[j] = (x >= g[j] && x < g[j + 1]) ? 1.0f : 0.0f;
+  for (int k = 1; k <= K; ++k) {
+    for (int j = 0; j < nk - 1 - k; ++j) {
+      const float l = __fdiv_rn(__fsub_rn(x, g[j]), __fsub_rn(g[j + k], g[j]));
+      const float r = __fdiv_rn(__fsub_rn(g[j + k + 1], x), __fsub_rn(g[j + k + 1], g[j + 1]));
+      b[j] = __fadd_rn(__fmul_rn(l, b[j]), __fmul_rn(r, b[j + 1]));
+    }
+  }
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// One CTA per batch row b; the grid is read per input (knots of input i at grid + i*nk).
+__global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x, const float* __restrict__ grid,
+                                                     int I, int C, int K, int64_t kp, __half* __restrict__ a_hi,
+                                                     __half* __restrict__ a_lo, float* __restrict__ rs) {
+  __shared__ float s_red[33];
+  const int bi = blockIdx.x;
+  const int nk = C + K + 1;
+  const float* xr = x + int64_t(bi) * I;
+  float amax = 0.0f;
+  for (int i = threadIdx.x; i < I; i += blockDim.x) amax = fmaxf(amax, fabsf(silu(xr[i])));
+  // B-spline bases on a non-decreasing grid lie in [0, 1].
+  const float f = fp16_row_factor(fmaxf(block_max(amax, s_red), 1.0f));
+  if (threadIdx.x == 0) rs[bi] = 1.0f / f;
+  __half* hr = a_hi + int64_t(bi) * kp;
+  __half* lr = a_lo + int64_t(bi) * kp;
+  float g[kMaxKnots], b[kMaxKnots];
+  for (int i = threadIdx.x; i < I; i += blockDim.x) {
+    const float xv = xr[i];
+    for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
+    bases_of(xv, g, nk, K, b);
+    split_store(silu(xv) * f, hr + i, lr + i);
+    for (int c = 0; c < C; ++c) split_store(b[c] * f, hr + int64_t(1 + c) * I + i, lr + int64_t(1 + c) * I + i);
+  }
+  const int64_t kk = int64_t(I) * (1 + C);
+  for (int64_t q = kk + threadIdx.x; q < kp; q += blockDim.x) {
+    hr[q] = __float2half_rn(0.0f);
+    lr[q] = __float2half_rn(0.0f);
+  }
+}
+
+// ------------------------------------------------------------------------------------- GEMM
+__device__ __forceinline__ void tile_coords(int tile, int n_m, int n_n, int& mb, int& nb) {
+  const int group = kGroupM * n_n;
+  const int g = tile / group;
+  const int first = g * kGroupM;
+  const int gm = min(n_m - first, kGroupM);
+  const int r = tile - g * group;
+  mb = first + r % gm;
+  nb = r / gm;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                const __grid_constant__ CUtensorMap tm_whi, const __grid_constant__ CUtensorMap tm_wlo, int M, int N,
+                int64_t kp, const float* __restrict__ rs, const float* __restrict__ cs, float* __restrict__ out) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full[kStages], empty[kStages], tfull, tempty;
+  __shared__ uint32_t tmem_base_s;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_m = (M + kBM - 1) / kBM, n_n = (N + kBN - 1) / kBN, n_tiles = n_m * n_n;
+  const int nkb = int(kp / kBKe);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull, 1);
+    mbar_init(&tempty, 4);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&tm_ahi);
+    tc::prefetch_tensormap(&tm_alo);
+    tc::prefetch_tensormap(&tm_whi);
+    tc::prefetch_tensormap(&tm_wlo);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&tmem_base_s, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t kb_all = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, n_m, n_n, mb, nb);
+        for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
+          const uint32_t s = kb_all % kStages, ph = (kb_all / kStages) & 1u;
+          mbar_wait(&empty[s], ph ^ 1u);
+          mbar_arrive_expect_tx(&full[s], kStage);
+          uint8_t* st = smem + s * kStage;
+          const int kc = kb * kBKe;
+          tc::tma_load_2d(st, &tm_ahi, kc, mb * kBM, &full[s]);
+          tc::tma_load_2d(st + kATile, &tm_alo, kc, mb * kBM, &full[s]);
+          tc::tma_load_2d(st + 2 * kATile, &tm_whi, kc, nb * kBN, &full[s]);
+          tc::tma_load_2d(st + 2 * kATile + kWTile, &tm_wlo, kc, nb * kBN, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id = tc::idesc(kBM, kBN, 0);  // F16 x F16 -> F32
+      uint32_t kb_all = 0, it = 0;
+      const uint32_t d0 = tmem, d1 = tmem + kBN;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        mbar_wait(&tempty, (it & 1u) ^ 1u);
+        tc::fence_after_sync();
+        for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
+          const uint32_t s = kb_all % kStages, ph = (kb_all / kStages) & 1u;
+          mbar_wait(&full[s], ph);
+          tc::fence_after_sync();
+          const uint32_t base = smem_addr(smem + s * kStage);
+          const uint64_t ahi = tc::sdesc_kmajor_sw128(base);
+          const uint64_t alo = tc::sdesc_kmajor_sw128(base + kATile);
+          const uint64_t whi = tc::sdesc_kmajor_sw128(base + 2 * kATile);
+          const uint64_t wlo = tc::sdesc_kmajor_sw128(base + 2 * kATile + kWTile);
+#pragma unroll
+          for (int k = 0; k < kBKe / kUmmaK; ++k) {
+            const uint64_t adv = uint64_t((k * kUmmaK * 2) >> 4);
+            const uint32_t first = (kb | k) != 0 ? 1u : 0u;
+            tc::mma_f16(d0, ahi + adv, whi + adv, id, first);
+            tc::mma_f16(d1, ahi + adv, wlo + adv, id, first);
+            tc::mma_f16(d1, alo + adv, whi + adv, id, 1u);
+          }
+          tc::mma_commit(&empty[s]);
+        }
+        tc::mma_commit(&tfull);
+      }
+    }
+  } else {  // epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32)
+    const int q = warp & 3;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      int mb, nb;
+      tile_coords(tile, n_m, n_n, mb, nb);
+      mbar_wait(&tfull, it & 1u);
+      tc::fence_after_sync();
+      const int row = mb * kBM + q * 32 + lane;
+      const float rsc = row < M ? rs[row] : 0.0f;
+      const bool vec_ok = (N % 4) == 0;
+#pragma unroll 1
+      for (int cc = 0; cc < kBN / 32; ++cc) {
+        uint32_t a[32], c[32];
+        const uint32_t lane_off = uint32_t(q * 32) << 16;
+        tc::tmem_ld32(tmem + lane_off + uint32_t(cc * 32), a);
+        tc::tmem_ld32(tmem + lane_off + uint32_t(kBN + cc * 32), c);
+        tc::tmem_ld_wait();
+        const int n0 = nb * kBN + cc * 32;
+        if (row < M) {
+          float* o = out + int64_t(row) * N + n0;
+          if (vec_ok && n0 + 32 <= N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 v;
+              v.x = fmaf(__uint_as_float(c[j + 0]), kLoUnscale, __uint_as_float(a[j + 0])) * rsc * cs[n0 + j + 0];
+              v.y = fmaf(__uint_as_float(c[j + 1]), kLoUnscale, __uint_as_float(a[j + 1])) * rsc * cs[n0 + j + 1];
+              v.z = fmaf(__uint_as_float(c[j + 2]), kLoUnscale, __uint_as_float(a[j + 2])) * rsc * cs[n0 + j + 2];
+              v.w = fmaf(__uint_as_float(c[j + 3]), kLoUnscale, __uint_as_float(a[j + 3])) * rsc * cs[n0 + j + 3];
+              *reinterpret_cast<float4*>(o + j) = v;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < N)
+                o[j] = fmaf(__uint_as_float(c[j]), kLoUnscale, __uint_as_float(a[j])) * rsc * cs[n0 + j];
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+inline size_t workspace_bytes(int B, int I, int O, int C) { return layout(B, I, O, C).total; }
+
+// Full op with a caller workspace of workspace_bytes() bytes (no initialisation needed).
+inline int run(const float* x, const float* grid, const float* wb, const float* sw, const float* sc, int32_t G,
+               int32_t K, int32_t B, int32_t I, int32_t O, float* out, void* workspace, size_t ws_bytes,
+               cudaStream_t stream) {
+  if (B < 0 || I < 0 || O < 0 || G < 1 || K < 0) return kInvalidArgument;
+  const int C = G + K;
+  if (C + K + 1 > kMaxKnots) return kUnsupported;
+  if (B == 0 || O == 0) return kOk;
+  if (x == nullptr || grid == nullptr || wb == nullptr || sw == nullptr || sc == nullptr || out == nullptr)
+    return kInvalidArgument;
+  if (I == 0) {
+    cudaMemsetAsync(out, 0, size_t(B) * O * 4, stream);
+    return launch_status();
+  }
+  const Layout L = layout(B, I, O, C);
+  if (workspace == nullptr || ws_bytes < L.total) return kWorkspaceTooSmall;
+  char* w = static_cast<char*>(workspace);
+  __half* a_hi = reinterpret_cast<__half*>(w + L.a_hi);
+  __half* a_lo = reinterpret_cast<__half*>(w + L.a_lo);
+  __half* w_hi = reinterpret_cast<__half*>(w + L.w_hi);
+  __half* w_lo = reinterpret_cast<__half*>(w + L.w_lo);
+  float* rs = reinterpret_cast<float*>(w + L.rs);
+  float* cs = reinterpret_cast<float*>(w + L.cs);
+  const int64_t kp = padded_k(I, C);
+  prep_w_kernel<<<O, 256, 0, stream>>>(wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
+  prep_a_kernel<<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  CUtensorMap m_ahi, m_alo, m_whi, m_wlo;
+  if (!tc::make_map_sw128(&m_ahi, a_hi, uint64_t(B), uint64_t(kp), 2, kBM) ||
+      !tc::make_map_sw128(&m_alo, a_lo, uint64_t(B), uint64_t(kp), 2, kBM) ||
+      !tc::make_map_sw128(&m_whi, w_hi, uint64_t(O), uint64_t(kp), 2, kBN) ||
+      !tc::make_map_sw128(&m_wlo, w_lo, uint64_t(O), uint64_t(kp), 2, kBN))
+    return kUnsupported;
+  if (!ensure_dyn_smem(gemm_kernel, kSmem)) return kCudaError;
+  const int n_tiles = ((B + kBM - 1) / kBM) * ((O + kBN - 1) / kBN);
+  const int grid_ctas = n_tiles < sm_count() ? n_tiles : sm_count();
+  gemm_kernel<<<grid_ctas, kThreads, kSmem, stream>>>(m_ahi, m_alo, m_whi, m_wlo, B, O, kp, rs, cs, out);
+  return launch_status();
+}
+
+}  // namespace kan
+}  // namespace b200

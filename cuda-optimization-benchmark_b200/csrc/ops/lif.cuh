@@ -9,15 +9,20 @@
 // const float* threshold, int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem)`
 // (tasks/leaky/tests/task.json:3; expert launcher reference/leaky/solution.cu:106-138).
 //
-// B200 design: the membrane state lives in registers for the whole time loop; a thread owns 4
-// consecutive neurons of the flattened (B*H) neuron axis (one 128-bit load of x[t] and one
-// 128-bit streaming store of spikes[t] per step, coalesced across the warp), and keeps kDepth
-// future time steps of x in flight in a register ring, so each SM always has loads outstanding.
-// Unaligned pointers or B*H not a multiple of 4 take the one-neuron-per-thread form of the same
-// loop.  8 bytes of HBM traffic per neuron-step (read x, write spike).
+// B200 design: the membrane state lives in registers for the whole time loop.  Each CTA owns a
+// contiguous slab of S neurons of the flattened (B*H) neuron axis (S ~ B*H / #SMs, one CTA per
+// SM), one thread per 4 neurons, and moves whole time-step slices of its slab with cp.async.bulk:
+// one thread keeps kDepth future x[t] slices (S*4 bytes each) in flight into a shared-memory
+// ring, the threads read their 4 neurons with one 128-bit shared load, write their 4 spikes into
+// a shared staging ring, and after one CTA barrier per step the same thread writes the slice of
+// spikes back with one bulk store.  DRAM sees S*4-byte contiguous transfers instead of
+// per-warp 512-byte pieces scattered over many time slices.  8 bytes of HBM traffic per
+// neuron-step (read x, write spike).  Shapes whose neuron count is not a multiple of 4, or
+// unaligned pointers, take the one-neuron-per-thread form of the same loop.
 #pragma once
 
 #include "../common/b200_common.cuh"
+#include "../common/bulk.cuh"
 
 namespace b200 {
 namespace lif {
@@ -33,45 +38,75 @@ __device__ __forceinline__ float step(float& mem, float x, float beta, float th)
   return mem >= th ? 1.0f : 0.0f;
 }
 
-// Vector form: thread owns neurons [4v, 4v+4) of the flattened neuron axis (NB = B*H, NB % 4 == 0).
-__global__ void __launch_bounds__(kThreads) lif_vec_kernel(const float* __restrict__ x, const float* __restrict__ mem0,
-                                                           const float* __restrict__ beta,
-                                                           const float* __restrict__ th, int T, int64_t NB, int H,
-                                                           float* __restrict__ spikes, float* __restrict__ final_mem) {
-  const int64_t v = int64_t(blockIdx.x) * kThreads + threadIdx.x;
-  if (v * 4 >= NB) return;
-  const int64_t i0 = v * 4;
-  float4 m = *reinterpret_cast<const float4*>(mem0 + i0);
-  float bq[4], tq[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int h = int((i0 + j) % H);
-    bq[j] = clamp01(beta[h]);
-    tq[j] = th[h];
+constexpr int kMaxDepth = 16;  // x slices in flight per CTA
+constexpr int kOut = 4;        // spike slices being written back per CTA
+constexpr int kSmemBudget = 160 * 1024;
+
+// Slab form (NB % 4 == 0, 16-byte aligned pointers): CTA c owns neurons [c*S, c*S + cnt).
+__global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restrict__ x, const float* __restrict__ mem0,
+                                                          const float* __restrict__ beta,
+                                                          const float* __restrict__ th, int T, int64_t NB, int H,
+                                                          int S, int depth, float* __restrict__ spikes,
+                                                          float* __restrict__ final_mem) {
+  extern __shared__ __align__(128) float sm[];
+  __shared__ uint64_t full[kMaxDepth];
+  float* xr = sm;                  // depth slices of S floats
+  float* so = sm + int64_t(depth) * S;  // kOut slices of S floats
+  const int64_t n0 = int64_t(blockIdx.x) * S;
+  const int cnt = int(NB - n0 < S ? NB - n0 : S);
+  const uint32_t bytes = uint32_t(cnt) * 4u;
+  const int tid = threadIdx.x;
+  const bool mine = 4 * tid < cnt;
+  if (tid == 0) {
+    for (int d = 0; d < depth; ++d) mbar_init(&full[d], 1);
+    fence_barrier_init();
   }
-  const float* xp = x + i0;
-  float* sp = spikes + i0;
-  float4 ring[kDepth];
+  __syncthreads();
+  if (tid == 0) {
+    for (int t = 0; t < depth && t < T; ++t) {
+      mbar_arrive_expect_tx(&full[t], bytes);
+      bulk_g2s(xr + int64_t(t) * S, x + int64_t(t) * NB + n0, bytes, &full[t]);
+    }
+  }
+  float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
+  float bq[4] = {0.f, 0.f, 0.f, 0.f}, tq[4] = {0.f, 0.f, 0.f, 0.f};
+  if (mine) {
+    m = *reinterpret_cast<const float4*>(mem0 + n0 + 4 * tid);
 #pragma unroll
-  for (int d = 0; d < kDepth; ++d)
-    if (d < T) ring[d] = ld_stream_f4(xp + int64_t(d) * NB);
-  for (int t0 = 0; t0 < T; t0 += kDepth) {
-#pragma unroll
-    for (int d = 0; d < kDepth; ++d) {
-      const int t = t0 + d;
-      if (t < T) {
-        const float4 xv = ring[d];
-        if (t + kDepth < T) ring[d] = ld_stream_f4(xp + int64_t(t + kDepth) * NB);
-        float4 s;
-        s.x = step(m.x, xv.x, bq[0], tq[0]);
-        s.y = step(m.y, xv.y, bq[1], tq[1]);
-        s.z = step(m.z, xv.z, bq[2], tq[2]);
-        s.w = step(m.w, xv.w, bq[3], tq[3]);
-        st_stream_f4(sp + int64_t(t) * NB, s);
+    for (int j = 0; j < 4; ++j) {
+      const int h = int((n0 + 4 * tid + j) % H);
+      bq[j] = clamp01(beta[h]);
+      tq[j] = th[h];
+    }
+  }
+  for (int t = 0; t < T; ++t) {
+    const int d = t % depth;
+    mbar_wait(&full[d], uint32_t(t / depth) & 1u);
+    if (mine) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + int64_t(d) * S + 4 * tid);
+      float4 sp;
+      sp.x = step(m.x, xv.x, bq[0], tq[0]);
+      sp.y = step(m.y, xv.y, bq[1], tq[1]);
+      sp.z = step(m.z, xv.z, bq[2], tq[2]);
+      sp.w = step(m.w, xv.w, bq[3], tq[3]);
+      *reinterpret_cast<float4*>(so + int64_t(t % kOut) * S + 4 * tid) = sp;
+    }
+    // Before anyone writes staging slot (t+1) % kOut in the next step, the bulk store that last
+    // read it (step t+1-kOut) must be done: at most kOut-2 older stores may still be reading.
+    if (tid == 0) bulk_wait_read<kOut - 2>();
+    __syncthreads();
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      bulk_s2g(spikes + int64_t(t) * NB + n0, so + int64_t(t % kOut) * S, bytes);
+      bulk_commit();
+      if (t + depth < T) {
+        mbar_arrive_expect_tx(&full[d], bytes);
+        bulk_g2s(xr + int64_t(d) * S, x + int64_t(t + depth) * NB + n0, bytes, &full[d]);
       }
     }
   }
-  *reinterpret_cast<float4*>(final_mem + i0) = m;
+  if (mine) *reinterpret_cast<float4*>(final_mem + n0 + 4 * tid) = m;
+  if (tid == 0) bulk_wait_all();
 }
 
 // Scalar form: one neuron per thread, same per-neuron arithmetic.
@@ -112,11 +147,22 @@ inline int run(const float* x, const float* mem0, const float* beta, const float
   if (NB == 0) return kOk;
   if (mem0 == nullptr || beta == nullptr || th == nullptr || final_mem == nullptr) return kInvalidArgument;
   if (T > 0 && (x == nullptr || spikes == nullptr)) return kInvalidArgument;
-  const bool vec = (NB % 4 == 0) && aligned16(mem0) && aligned16(final_mem) && (T == 0 || (aligned16(x) && aligned16(spikes)));
-  if (vec) {
-    const int64_t threads = NB / 4;
-    const int64_t grid = (threads + kThreads - 1) / kThreads;
-    lif_vec_kernel<<<unsigned(grid), kThreads, 0, stream>>>(x, mem0, beta, th, T, NB, H, spikes, final_mem);
+  const bool slab = T > 0 && (NB % 4 == 0) && aligned16(mem0) && aligned16(final_mem) && aligned16(x) &&
+                    aligned16(spikes);
+  if (slab) {
+    // Slab of S neurons per CTA: about one CTA per SM, S a multiple of 128 (whole warps).
+    const int sms = sm_count();
+    int64_t S = (NB + sms - 1) / sms;
+    S = (S + 127) / 128 * 128;
+    if (S > 4096) S = 4096;
+    const int64_t grid = (NB + S - 1) / S;
+    int depth = int(kSmemBudget / (S * 4)) - kOut;
+    if (depth > kMaxDepth) depth = kMaxDepth;
+    if (depth < 2) depth = 2;
+    const size_t smem = size_t(depth + kOut) * size_t(S) * 4;
+    if (!ensure_dyn_smem(lif_slab_kernel, int(smem))) return kCudaError;
+    lif_slab_kernel<<<unsigned(grid), unsigned(S / 4), smem, stream>>>(x, mem0, beta, th, T, NB, H, int(S), depth,
+                                                                       spikes, final_mem);
   } else {
     const int64_t grid = (NB + kThreads - 1) / kThreads;
     lif_scalar_kernel<<<unsigned(grid), kThreads, 0, stream>>>(x, mem0, beta, th, T, NB, H, spikes, final_mem);

@@ -12,8 +12,8 @@
 // Per element (lw = cur - old):
 //   ratio r = exp(lw); clipped = lw < log1p(-eps) or lw > log1p(eps);
 //   gain = min(r*adv, exp(clamp(lw))*adv)  (exp(clamp(lw)) is 1-eps / 1+eps when clipped, else r)
-//   kl   = (r - 1) - lw
-// Reductions: sum gain, count clipped, sum kl, sum r, sum r^2, max r, [sum entropy].
+//   kl   = (r - 1) - lw, whose mean is (sum r - sum lw) / N - 1
+// Reductions: sum gain, count clipped, sum lw, sum r, sum r^2, max r, [sum entropy].
 // ESS = exp(2 lse(lw) - lse(2 lw)) / N = (sum r)^2 / (sum r^2) / N.
 //
 // B200 design.  12 (16 with entropy) bytes per element.  The element range is cut into fixed
@@ -38,8 +38,8 @@
 namespace b200 {
 namespace ppo {
 
-constexpr int kThreads = 256;                                       // consumer threads
-constexpr int kVecPerThread = 4;                                    // float4 per input per thread
+constexpr int kThreads = 512;                                       // consumer threads
+constexpr int kVecPerThread = 2;                                    // float4 per input per thread
 constexpr int64_t kChunk = int64_t(kThreads) * kVecPerThread * 4;  // 4096 elements per chunk
 constexpr int kPipeThreads = kThreads + 32;                         // + one producer warp
 constexpr uint32_t kRedBar = 1;                                     // named barrier of the consumers
@@ -56,7 +56,7 @@ struct Pipe {
 };
 
 struct __align__(16) Partial {
-  double gain, kl, r, r2, ent;
+  double gain, lw, r, r2, ent;
   float rmax;
   unsigned clipped;
 };
@@ -85,43 +85,55 @@ inline int64_t num_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
 inline size_t workspace_bytes(int64_t n) { return 256 + align256(size_t(num_chunks(n)) * sizeof(Partial)); }
 
 struct Acc {
-  float gain = 0.f, kl = 0.f, r = 0.f, r2 = 0.f, ent = 0.f, rmax = 0.f;
+  float gain = 0.f, lw = 0.f, r = 0.f, r2 = 0.f, ent = 0.f, rmax = 0.f;
   unsigned clipped = 0;
-  double big_gain = 0.0, big_kl = 0.0, big_r = 0.0, big_r2 = 0.0;  // lw > 30 only
+  double big_gain = 0.0, big_lw = 0.0, big_r = 0.0, big_r2 = 0.0;  // lw > 30 only
 };
+
+// Rare elements (within 1e-6 of a clip boundary, or lw > 30) leave the fast path: the clip
+// decision is re-taken in fp64 and, for lw > 30, the element is accumulated in fp64.
+__device__ __forceinline__ void add_element_slow(Acc& acc, float cur, float old, float adv, const Clip& c) {
+  const double lwd = double(cur) - double(old);
+  const bool below = lwd < c.lo_d;
+  const bool clipped = below || lwd > c.hi_d;
+  acc.clipped += clipped ? 1u : 0u;
+  const float lw = __fsub_rn(cur, old);
+  if (lw <= 30.0f) {
+    const float r = __expf(lw);
+    const float rc = clipped ? (below ? c.down : c.up) : r;
+    acc.gain = __fadd_rn(acc.gain, fminf(__fmul_rn(r, adv), __fmul_rn(rc, adv)));
+    acc.lw = __fadd_rn(acc.lw, lw);
+    acc.r = __fadd_rn(acc.r, r);
+    acc.r2 = __fmaf_rn(r, r, acc.r2);
+    acc.rmax = fmaxf(acc.rmax, r);
+  } else {
+    const double r = exp(lwd);
+    const double rc = exp(c.hi_d);
+    acc.big_gain += fmin(r * double(adv), rc * double(adv));
+    acc.big_lw += lwd;
+    acc.big_r += r;
+    acc.big_r2 += r * r;
+    acc.rmax = fmaxf(acc.rmax, float(r));
+  }
+}
 
 __device__ __forceinline__ void add_element(Acc& acc, float cur, float old, float adv, const Clip& c) {
   const float lw = __fsub_rn(cur, old);
   const float dm = __fsub_rn(lw, c.mid);
   const float adm = fabsf(dm);
-  bool clipped = adm > c.hw;
-  bool below = dm < 0.0f;
-  // Within 1e-6 of a boundary the fp32 decision may differ from the fp64 one: take it in fp64.
-  if (fabsf(__fsub_rn(adm, c.hw)) < 1e-6f) {
-    const double lwd = double(cur) - double(old);
-    below = lwd < c.lo_d;
-    clipped = below || lwd > c.hi_d;
+  if (fabsf(__fsub_rn(adm, c.hw)) < 1e-6f || lw > 30.0f) {
+    add_element_slow(acc, cur, old, adv, c);
+    return;
   }
+  const bool clipped = adm > c.hw;
   acc.clipped += clipped ? 1u : 0u;
-  if (lw <= 30.0f) {
-    const float r = __expf(lw);
-    const float rc = clipped ? (below ? c.down : c.up) : r;
-    const float g = fminf(__fmul_rn(r, adv), __fmul_rn(rc, adv));
-    acc.gain = __fadd_rn(acc.gain, g);
-    acc.kl = __fadd_rn(acc.kl, __fsub_rn(__fsub_rn(r, 1.0f), lw));
-    acc.r = __fadd_rn(acc.r, r);
-    acc.r2 = __fmaf_rn(r, r, acc.r2);
-    acc.rmax = fmaxf(acc.rmax, r);
-  } else {
-    const double lwd = double(cur) - double(old);
-    const double r = exp(lwd);
-    const double rc = exp(c.hi_d);
-    acc.big_gain += fmin(r * double(adv), rc * double(adv));
-    acc.big_kl += (r - 1.0) - lwd;
-    acc.big_r += r;
-    acc.big_r2 += r * r;
-    acc.rmax = fmaxf(acc.rmax, float(r));
-  }
+  const float r = __expf(lw);
+  const float rc = clipped ? (dm < 0.0f ? c.down : c.up) : r;
+  acc.gain = __fadd_rn(acc.gain, fminf(__fmul_rn(r, adv), __fmul_rn(rc, adv)));
+  acc.lw = __fadd_rn(acc.lw, lw);
+  acc.r = __fadd_rn(acc.r, r);
+  acc.r2 = __fmaf_rn(r, r, acc.r2);
+  acc.rmax = fmaxf(acc.rmax, r);
 }
 
 template <bool kEnt>
@@ -180,7 +192,7 @@ __device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
   __shared__ double s_d[5][kThreads / 32];
   __shared__ float s_max[kThreads / 32];
   __shared__ unsigned s_cnt[kThreads / 32];
-  double v[5] = {double(acc.gain) + acc.big_gain, double(acc.kl) + acc.big_kl, double(acc.r) + acc.big_r,
+  double v[5] = {double(acc.gain) + acc.big_gain, double(acc.lw) + acc.big_lw, double(acc.r) + acc.big_r,
                  double(acc.r2) + acc.big_r2, double(acc.ent)};
 #pragma unroll
   for (int q = 0; q < 5; ++q) v[q] = warp_sum(v[q]);
@@ -196,13 +208,13 @@ __device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
   named_sync(kRedBar, kThreads);
   Partial p{};
   if (threadIdx.x == 0) {
-    p.gain = p.kl = p.r = p.r2 = p.ent = 0.0;
+    p.gain = p.lw = p.r = p.r2 = p.ent = 0.0;
     p.rmax = 0.f;
     p.clipped = 0;
 #pragma unroll
     for (int i = 0; i < kThreads / 32; ++i) {
       p.gain += s_d[0][i];
-      p.kl += s_d[1][i];
+      p.lw += s_d[1][i];
       p.r += s_d[2][i];
       p.r2 += s_d[3][i];
       p.ent += s_d[4][i];
@@ -256,7 +268,7 @@ __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, in
     const double N = double(n_total);
     out[0] = float(-t[0] / N);
     out[1] = float(double(c) / N);
-    out[2] = float(t[1] / N);
+    out[2] = float((t[2] - t[1]) / N - 1.0);
     out[3] = float((t[2] / N) * (t[2] / t[3]));
     out[4] = n_total > 0 ? mx : __int_as_float(0x7fc00000);
     out[5] = float(t[2] / N);

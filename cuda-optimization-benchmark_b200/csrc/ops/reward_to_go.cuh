@@ -36,45 +36,9 @@ constexpr int kWarps = 4;                    // warps (rows in flight) per CTA
 constexpr int kThreads = 32 * kWarps;
 // Per-warp shared memory: kSeg floats (+16 B phase slack) and kSeg done bytes (+16 B slack).
 constexpr int kRewardBytes = ((kSeg * 4 + 16) + 15) / 16 * 16;
-constexpr int kDoneBytes = ((kSeg + 16) + 15) / 16 * 16;
+constexpr int kDoneBytes = ((kSeg + 16 + 16) + 15) / 16 * 16;  // + 16: done_mask reads 40-byte windows
 constexpr int kWarpSmem = kRewardBytes + kDoneBytes;
-constexpr int kSmemBytes = kWarps * kWarpSmem;
-
-// Stage src[0..len) (floats) into shared memory at sdst[phase .. phase+len), where phase is the
-// float offset of src within its 16-byte group (so the 16-byte aligned interior of the range maps
-// to 16-byte aligned shared addresses).  Lane 0 moves the aligned interior with one bulk copy
-// counted on `bar`; the lanes load the ragged head and tail (< 4 elements each) themselves.
-// Returns the number of bytes the bulk copy will deliver (0 when there is no interior).
-__device__ __forceinline__ uint32_t stage_floats(const float* __restrict__ src, int len, float* sdst, int phase,
-                                                 uint64_t* bar, int lane) {
-  const int ea = (4 - phase) & 3;                       // first element on a 16-byte boundary
-  const int eb = len > ea ? ea + ((len - ea) & ~3) : ea;  // end of the aligned interior
-  const uint32_t bytes = len > ea ? uint32_t(eb - ea) * 4u : 0u;
-  if (lane == 0 && bytes) bulk_g2s(sdst + phase + ea, src + ea, bytes, bar);
-  const int head = len < ea ? len : ea;
-  if (lane < head) sdst[phase + lane] = ld_stream_f1(src + lane);
-  if (lane < len - eb && eb < len) sdst[phase + eb + lane] = ld_stream_f1(src + eb + lane);
-  return bytes;
-}
-
-__device__ __forceinline__ unsigned char ld_stream_u8(const unsigned char* p) {
-  unsigned short v;
-  asm volatile("ld.global.nc.L1::no_allocate.u8 %0, [%1];" : "=h"(v) : "l"(p));
-  return (unsigned char)v;
-}
-
-// Same for bytes (16-byte phase; head and tail up to 15 bytes each).
-__device__ __forceinline__ uint32_t stage_bytes(const unsigned char* __restrict__ src, int len, unsigned char* sdst,
-                                                int phase, uint64_t* bar, int lane) {
-  const int ea = (16 - phase) & 15;
-  const int eb = len > ea ? ea + ((len - ea) & ~15) : ea;
-  const uint32_t bytes = len > ea ? uint32_t(eb - ea) : 0u;
-  if (lane == 0 && bytes) bulk_g2s(sdst + phase + ea, src + ea, bytes, bar);
-  const int head = len < ea ? len : ea;
-  if (lane < head) sdst[phase + lane] = ld_stream_u8(src + lane);
-  if (lane < len - eb && eb < len) sdst[phase + eb + lane] = ld_stream_u8(src + eb + lane);
-  return bytes;
-}
+constexpr int kSmemBytes = 2 * kWarps * kWarpSmem;  // two staging buffers per warp
 
 // Write sfrom[phase .. phase+len) to dst[0..len).  When dst has the same 16-byte phase as the
 // staged data, full groups go out as 128-bit streaming stores; otherwise lane-strided scalars.
@@ -103,92 +67,205 @@ __device__ __forceinline__ void drain_floats(float* __restrict__ dst, int len, c
   }
 }
 
-// One warp, one row: walks [0, T) from the end in passes of kSeg steps.  `bar` is this warp's
-// mbarrier and `uses` counts its completed phases (carried across rows).
-__device__ __forceinline__ void scan_row(const float* __restrict__ rrow, const unsigned char* __restrict__ drow,
-                                         float* __restrict__ orow, int T, double gamma, float gamma_f, float* s_r,
-                                         unsigned char* s_d, uint64_t* bar, uint32_t& uses, int lane) {
-  double carry = 0.0;  // value of out[t1] for the pass [t0, t1); 0 past the row end
-  for (int t1 = T; t1 > 0; t1 -= kSeg) {
-    const int t0 = t1 > kSeg ? t1 - kSeg : 0;
-    const int len = t1 - t0;
-    const float* rs = rrow + t0;
-    const unsigned char* ds = drow + t0;
-    const int pr = int((reinterpret_cast<uintptr_t>(rs) >> 2) & 3);
-    const int pd = int(reinterpret_cast<uintptr_t>(ds) & 15);
-    // Shared memory written by the previous pass through ordinary stores is about to be
-    // overwritten by the bulk-copy engine: order the two.
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncwarp();
-    // Byte counts are known before either copy is issued, so the expect_tx arrive goes first.
-    const int ear = (4 - pr) & 3, ead = (16 - pd) & 15;
-    const uint32_t rb = len > ear ? uint32_t((len - ear) & ~3) * 4u : 0u;
-    const uint32_t db = len > ead ? uint32_t((len - ead) & ~15) : 0u;
-    if (lane == 0) mbar_arrive_expect_tx(bar, rb + db);
-    stage_floats(rs, len, s_r, pr, bar, lane);
-    stage_bytes(ds, len, s_d, pd, bar, lane);
-    mbar_wait(bar, uses & 1u);
-    ++uses;
-    __syncwarp();
-
-    // Lane l owns steps [l*kLane, min((l+1)*kLane, len)) of the pass.
-    const int lo = lane * kLane;
-    const int hi = min(lo + kLane, len);
-    double A = 1.0, Bv = 0.0;
-    unsigned long long dmask = 0;  // bit (e - lo) set when done[t0 + e]
-    for (int e = hi - 1; e >= lo; --e) {
-      const bool d = s_d[pd + e] != 0;
-      dmask |= (unsigned long long)d << (e - lo);
-      const double a = d ? 0.0 : gamma;
-      Bv = fma(a, Bv, double(s_r[pr + e]));
-      A *= a;
-    }
-    // Inclusive suffix composition over lanes: lane l gets f_l o f_{l+1} o ... o f_31.
+// Bit e (e < cnt) set when byte sd[at + e] is non-zero.  Reads the ten aligned 32-bit words that
+// cover [at, at + 40) and folds each word's four "byte is non-zero" bits into a nibble.
+__device__ __forceinline__ unsigned long long done_mask(const unsigned char* sd, int at, int cnt) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(sd) + (at >> 2);
+  unsigned long long m = 0;
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const double A2 = __shfl_down_sync(0xffffffffu, A, d);
-      const double B2 = __shfl_down_sync(0xffffffffu, Bv, d);
-      if (lane + d < 32) {
-        Bv = fma(A, B2, Bv);
-        A *= A2;
-      }
-    }
-    const double start = fma(A, carry, Bv);                  // out[t0 + lo]
-    double yin = __shfl_down_sync(0xffffffffu, start, 1);    // out[t0 + hi] for lanes < 31
-    if (lane == 31) yin = carry;
-    const double next_carry = __shfl_sync(0xffffffffu, start, 0);
-    // Second pass from the exact incoming value, in fp32: at most kLane roundings per output.
-    float y = float(yin);
-    for (int e = hi - 1; e >= lo; --e) {
-      const float a = (dmask >> (e - lo)) & 1ull ? 0.0f : gamma_f;
-      y = __fmaf_rn(a, y, s_r[pr + e]);
-      s_r[pr + e] = y;
-    }
-    __syncwarp();
-    drain_floats(orow + t0, len, s_r, pr, lane);
-    __syncwarp();
-    carry = next_carry;
+  for (int i = 0; i < 10; ++i) {
+    const uint32_t v = w[i];
+    const uint32_t hi = (((v & 0x7f7f7f7fu) + 0x7f7f7f7fu) | v) & 0x80808080u;  // 0x80 per non-zero byte
+    const uint32_t nib = (hi >> 7 | hi >> 14 | hi >> 21 | hi >> 28) & 0xfu;      // bytes 0..3 -> bits 0..3
+    m |= (unsigned long long)nib << (4 * i);
   }
+  m >>= (at & 3);
+  return cnt >= 64 ? m : (m & ((1ull << cnt) - 1ull));
 }
 
+// Ragged-edge values a lane loaded for a prefetched pass; written to shared memory when the
+// pass's bulk copy has landed, so issuing a pass never waits on its own plain loads.
+struct Edges {
+  float rh, rt;
+  uint32_t dh, dt;
+};
+
+// Geometry of the pass [t0, t0 + len) of one row: 16-byte phases and aligned interiors.
+struct Pass {
+  const float* rs;
+  const unsigned char* ds;
+  int len, pr, pd, ear, ebr, ead, ebd;
+};
+
+__device__ __forceinline__ Pass make_pass(const float* rrow, const unsigned char* drow, int t0, int len) {
+  Pass p;
+  p.rs = rrow + t0;
+  p.ds = drow + t0;
+  p.len = len;
+  p.pr = int((reinterpret_cast<uintptr_t>(p.rs) >> 2) & 3);
+  p.pd = int(reinterpret_cast<uintptr_t>(p.ds) & 15);
+  p.ear = (4 - p.pr) & 3;
+  p.ebr = len > p.ear ? p.ear + ((len - p.ear) & ~3) : p.ear;
+  p.ead = (16 - p.pd) & 15;
+  p.ebd = len > p.ead ? p.ead + ((len - p.ead) & ~15) : p.ead;
+  return p;
+}
+
+__device__ __forceinline__ unsigned char ld_u8(const unsigned char* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u8 %0, [%1];" : "=h"(v) : "l"(p));
+  return (unsigned char)v;
+}
+
+// Start moving a pass into a staging buffer: lane 0 arms the buffer's barrier and issues one bulk
+// copy per stream for the aligned interiors; every lane issues its ragged-edge loads.
+__device__ __forceinline__ Edges issue_pass(const Pass& p, float* s_r, unsigned char* s_d, uint64_t* bar, int lane) {
+  fence_proxy_async_smem();  // earlier ordinary accesses of this buffer come before the copy
+  __syncwarp();
+  const uint32_t rb = uint32_t(p.ebr - p.ear) * 4u * (p.len > p.ear);
+  const uint32_t db = uint32_t(p.ebd - p.ead) * (p.len > p.ead);
+  if (lane == 0) {
+    mbar_arrive_expect_tx(bar, rb + db);
+    if (rb) bulk_g2s(s_r + p.pr + p.ear, p.rs + p.ear, rb, bar);
+    if (db) bulk_g2s(s_d + p.pd + p.ead, p.ds + p.ead, db, bar);
+  }
+  Edges e{0.f, 0.f, 0u, 0u};
+  const int hr = min(p.len, p.ear), tr = p.len - p.ebr;
+  const int hd = min(p.len, p.ead), td = p.len - p.ebd;
+  if (lane < hr) e.rh = ld_stream_f1(p.rs + lane);
+  if (lane < tr) e.rt = ld_stream_f1(p.rs + p.ebr + lane);
+  if (lane < hd) e.dh = ld_u8(p.ds + lane);
+  if (lane < td) e.dt = ld_u8(p.ds + p.ebd + lane);
+  return e;
+}
+
+// Finish staging a pass: write the ragged edges, wait for the bulk copies (phase `parity`).
+__device__ __forceinline__ void land_pass(const Pass& p, const Edges& e, float* s_r, unsigned char* s_d,
+                                          uint64_t* bar, uint32_t parity, int lane) {
+  const int hr = min(p.len, p.ear), tr = p.len - p.ebr;
+  const int hd = min(p.len, p.ead), td = p.len - p.ebd;
+  if (lane < hr) s_r[p.pr + lane] = e.rh;
+  if (lane < tr) s_r[p.pr + p.ebr + lane] = e.rt;
+  if (lane < hd) s_d[p.pd + lane] = (unsigned char)e.dh;
+  if (lane < td) s_d[p.pd + p.ebd + lane] = (unsigned char)e.dt;
+  mbar_wait(bar, parity);
+  __syncwarp();
+}
+
+// Scan one staged pass given the value entering it from the right (`carry`); writes the outputs
+// into the staging buffer and returns the value at the pass's first step.
+__device__ __forceinline__ double scan_pass(const Pass& p, float* s_r, const unsigned char* s_d, double carry,
+                                            double gamma, float gamma_f, int lane) {
+  // Lane l owns steps [l*kLane, l*kLane + cnt) of the pass, cnt <= kLane.
+  const int lo = lane * kLane;
+  const int cnt = max(0, min(kLane, p.len - lo));
+  const unsigned long long dmask = done_mask(s_d, p.pd + lo, cnt);  // bit e: done at step lo + e
+  float* rl = s_r + p.pr + lo;
+  double Bv = 0.0;
+#pragma unroll
+  for (int e = kLane - 1; e >= 0; --e) {
+    if (e < cnt) {
+      const double rv = double(rl[e]);
+      Bv = ((dmask >> e) & 1ull) ? rv : fma(gamma, Bv, rv);
+    }
+  }
+  double A = 0.0;  // product of the run's factors: 0 if any done, else gamma^cnt
+  if (dmask == 0) {
+    double q = gamma;
+    A = 1.0;
+#pragma unroll
+    for (int b = 0; b < 6; ++b) {
+      if ((cnt >> b) & 1) A *= q;
+      q *= q;
+    }
+  }
+  // Inclusive suffix composition over lanes: lane l gets f_l o f_{l+1} o ... o f_31.
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const double A2 = __shfl_down_sync(0xffffffffu, A, d);
+    const double B2 = __shfl_down_sync(0xffffffffu, Bv, d);
+    if (lane + d < 32) {
+      Bv = fma(A, B2, Bv);
+      A *= A2;
+    }
+  }
+  const double start = fma(A, carry, Bv);                // value at this lane's first step
+  double yin = __shfl_down_sync(0xffffffffu, start, 1);  // value entering this lane's run
+  if (lane == 31) yin = carry;
+  const double first = __shfl_sync(0xffffffffu, start, 0);
+  // Second pass from the exact incoming value, in fp32: at most kLane roundings per output.
+  float y = float(yin);
+#pragma unroll
+  for (int e = kLane - 1; e >= 0; --e) {
+    if (e < cnt) {
+      const float rv = rl[e];
+      y = ((dmask >> e) & 1ull) ? rv : __fmaf_rn(gamma_f, y, rv);
+      rl[e] = y;
+    }
+  }
+  __syncwarp();
+  return first;
+}
+
+// Each warp streams its rows (row = warp id, + total warps, ...) pass by pass, from the end of a
+// row to its start, through two staging buffers: the next pass is in flight while the current
+// one is scanned and written out.
 __global__ void __launch_bounds__(kThreads) rtg_kernel(const float* __restrict__ reward,
                                                        const unsigned char* __restrict__ done, float gamma,
                                                        int B, int T, float* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ uint64_t bars[kWarps];
+  __shared__ uint64_t bars[kWarps][2];  // one barrier per staging buffer
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* s_r = reinterpret_cast<float*>(smem + warp * kWarpSmem);
-  unsigned char* s_d = smem + warp * kWarpSmem + kRewardBytes;
+  unsigned char* wbase = smem + warp * 2 * kWarpSmem;  // buffer b at wbase + b * kWarpSmem
+  auto s_rb = [&](uint32_t b) { return reinterpret_cast<float*>(wbase + b * kWarpSmem); };
+  auto s_db = [&](uint32_t b) { return wbase + b * kWarpSmem + kRewardBytes; };
   if (lane == 0) {
-    mbar_init(&bars[warp], 1);
+    mbar_init(&bars[warp][0], 1);
+    mbar_init(&bars[warp][1], 1);
     fence_barrier_init();
   }
   __syncwarp();
-  uint32_t uses = 0;
   const double g = double(gamma);
-  for (int64_t row = int64_t(blockIdx.x) * kWarps + warp; row < B; row += int64_t(gridDim.x) * kWarps) {
-    const int64_t off = row * int64_t(T);
-    scan_row(reward + off, done + off, out + off, T, g, gamma, s_r, s_d, &bars[warp], uses, lane);
+  const int64_t stride = int64_t(gridDim.x) * kWarps;
+  int64_t row = int64_t(blockIdx.x) * kWarps + warp;
+  if (row >= B) return;
+  int t1 = T;
+  // Current pass and its staging state.
+  Pass cur = make_pass(reward + row * int64_t(T), done + row * int64_t(T), t1 > kSeg ? t1 - kSeg : 0,
+                       t1 > kSeg ? kSeg : t1);
+  Edges ecur = issue_pass(cur, s_rb(0), s_db(0), &bars[warp][0], lane);
+  uint32_t k = 0;
+  double carry = 0.0;
+  for (;;) {
+    // Work out and prefetch the next pass (next pass of this row, or the last pass of the next row).
+    int64_t nrow = row;
+    int nt1 = t1 - kSeg;
+    if (nt1 <= 0) {
+      nrow = row + stride;
+      nt1 = T;
+    }
+    const bool has_next = nrow < B;
+    Pass nxt{};
+    Edges enxt{0.f, 0.f, 0u, 0u};
+    const uint32_t nb = (k + 1) & 1u;
+    if (has_next) {
+      const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
+      nxt = make_pass(reward + nrow * int64_t(T), done + nrow * int64_t(T), nt0, nt1 - nt0);
+      enxt = issue_pass(nxt, s_rb(nb), s_db(nb), &bars[warp][nb], lane);
+    }
+    const uint32_t cb = k & 1u;
+    land_pass(cur, ecur, s_rb(cb), s_db(cb), &bars[warp][cb], (k >> 1) & 1u, lane);
+    const double first = scan_pass(cur, s_rb(cb), s_db(cb), carry, g, gamma, lane);
+    const int t0 = t1 > kSeg ? t1 - kSeg : 0;
+    drain_floats(out + row * int64_t(T) + t0, cur.len, s_rb(cb), cur.pr, lane);
+    __syncwarp();
+    if (!has_next) break;
+    carry = (nrow == row) ? first : 0.0;
+    row = nrow;
+    t1 = nt1;
+    cur = nxt;
+    ecur = enxt;
+    ++k;
   }
 }
 
@@ -197,8 +274,10 @@ inline int run(const float* reward, const unsigned char* done, float gamma, int3
   if (B < 0 || T < 0) return kInvalidArgument;
   if (B == 0 || T == 0) return kOk;
   if (reward == nullptr || done == nullptr || out == nullptr) return kInvalidArgument;
+  // About 8 warps per SM, each streaming several rows: loads of one row overlap the scan of the
+  // previous one.
   const int64_t ctas_needed = (int64_t(B) + kWarps - 1) / kWarps;
-  const int64_t cap = int64_t(sm_count()) * resident_ctas_per_sm(rtg_kernel, kThreads, kSmemBytes);
+  const int64_t cap = int64_t(sm_count()) * 2;
   const int grid = int(ctas_needed < cap ? ctas_needed : cap);
   rtg_kernel<<<grid, kThreads, kSmemBytes, stream>>>(reward, done, gamma, B, T, out);
   return launch_status();

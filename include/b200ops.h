@@ -126,6 +126,25 @@ int b200_leaky_async(const float* input_current, const float* mem0, const float*
                      int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * KAN linear layer (task efficient_kan): out[B, O] = silu(x) . base_weight^T + bases(x) .
+ * (spline_weight * spline_scaler)^T, with the G + K B-spline bases of order K on each input's
+ * knot grid[I, G + 2K + 1].
+ * Replaces `void reference(const float* x, const float* grid, const float* base_weight,
+ * const float* spline_weight, const float* spline_scaler, int32_t grid_size, int32_t spline_order,
+ * int32_t B, int32_t I, int32_t O, float* out)`: tasks/efficient_kan/tests/task.json:3,
+ * reference/efficient_kan/solution.cu:177.
+ * ------------------------------------------------------------------------------------------- */
+void b200_efficient_kan(const float* x, const float* grid, const float* base_weight, const float* spline_weight,
+                        const float* spline_scaler, int32_t grid_size, int32_t spline_order, int32_t B, int32_t I,
+                        int32_t O, float* out);
+/* Stream form; workspace: b200_efficient_kan_workspace_bytes(...) bytes (no initialisation). */
+size_t b200_efficient_kan_workspace_bytes(int32_t grid_size, int32_t spline_order, int32_t B, int32_t I, int32_t O);
+int b200_efficient_kan_async(const float* x, const float* grid, const float* base_weight, const float* spline_weight,
+                             const float* spline_scaler, int32_t grid_size, int32_t spline_order, int32_t B,
+                             int32_t I, int32_t O, float* out, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * FP8 E4M3 linear layer (task fp8_linear): output[M, N] (bf16) =
  * (x_fp8[M, K] . w_fp8[N, K]^T) / (scale_x * scale_w) + bias[N].
  * Replaces `void reference(const int32_t M, const int32_t K, const int32_t N,
