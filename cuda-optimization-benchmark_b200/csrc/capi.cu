@@ -7,12 +7,12 @@
 #include <cuda_runtime.h>
 
 #include "../../include/b200ops.h"
-#include "ops/fp8_linear.cuh"
-#include "ops/kan.cuh"
-#include "ops/lif.cuh"
-#include "ops/ppo_clip.cuh"
-#include "ops/reward_to_go.cuh"
-#include "ops/robust_l1.cuh"
+#include "dropin/efficient_kan.cuh"
+#include "dropin/fp8_linear.cuh"
+#include "dropin/leaky.cuh"
+#include "dropin/pow_abs_sqrt_mean.cuh"
+#include "dropin/ppo_clip.cuh"
+#include "dropin/reward_to_go.cuh"
 
 namespace {
 thread_local int g_last_status = 0;
@@ -39,13 +39,7 @@ int b200_device_fault(void) {
 // ---------------------------------------------------------------------------------- robust-L1
 void b200_pow_abs_sqrt_mean(const float* inp, const float* target, int64_t batch_size, int64_t height,
                             int64_t width, float* output) {
-  const int64_t n = b200::robust_l1::abi_count(batch_size, height, width);
-  if (n < 0) return record(b200::kInvalidArgument);
-  int st = 0;
-  const size_t ws = b200::robust_l1::workspace_bytes(n);
-  void* w = b200::arena_get(ws, nullptr, &st);
-  if (st != 0) return record(st);
-  record(b200::robust_l1::run(inp, target, n, output, w, ws, nullptr));
+  record(b200::dropin::pow_abs_sqrt_mean(inp, target, batch_size, height, width, output));
 }
 
 size_t b200_robust_l1_workspace_bytes(int64_t n) { return n < 0 ? 0 : b200::robust_l1::workspace_bytes(n); }
@@ -68,27 +62,16 @@ int b200_robust_l1_finish(const double* partials, int64_t n_partials, int64_t n_
 }
 
 // ---------------------------------------------------------------------------------------- PPO
-static void ppo_dropin(int32_t B, int32_t T, int32_t H, const float* cur, const float* old, const float* adv,
-                       const float* ent, float eps, float* out) {
-  const int64_t n = b200::ppo::abi_count(B, T, H);
-  if (n < 0) return record(b200::kInvalidArgument);
-  int st = 0;
-  const size_t ws = b200::ppo::workspace_bytes(n);
-  void* w = b200::arena_get(ws, nullptr, &st);
-  if (st != 0) return record(st);
-  record(b200::ppo::run(cur, old, adv, ent, n, eps, out, w, ws, nullptr));
-}
-
 void b200_ppo_clip(const int32_t B, const int32_t T, const int32_t H, const float* current_log_prob,
                    const float* old_log_prob, const float* advantage, const float clip_epsilon, float* output) {
-  ppo_dropin(B, T, H, current_log_prob, old_log_prob, advantage, nullptr, clip_epsilon, output);
+  record(b200::dropin::ppo_clip(B, T, H, current_log_prob, old_log_prob, advantage, nullptr, clip_epsilon, output));
 }
 
 void b200_ppo_clip_ext(const int32_t B, const int32_t T, const int32_t H, const float* current_log_prob,
                        const float* old_log_prob, const float* advantage, const float* entropy,
                        const float clip_epsilon, float* output) {
   if (entropy == nullptr) return record(b200::kInvalidArgument);
-  ppo_dropin(B, T, H, current_log_prob, old_log_prob, advantage, entropy, clip_epsilon, output);
+  record(b200::dropin::ppo_clip(B, T, H, current_log_prob, old_log_prob, advantage, entropy, clip_epsilon, output));
 }
 
 size_t b200_ppo_workspace_bytes(int64_t n) { return n < 0 ? 0 : b200::ppo::workspace_bytes(n); }
@@ -117,7 +100,7 @@ int b200_ppo_finish(const void* partials, int64_t n_partials, int64_t n_total, i
 
 // ------------------------------------------------------------------------------- reward-to-go
 void b200_reward_to_go(const float* reward, const bool* done, float gamma, int32_t B, int32_t T, float* output) {
-  record(b200::rtg::run(reward, reinterpret_cast<const unsigned char*>(done), gamma, B, T, output, nullptr));
+  record(b200::dropin::reward_to_go(reward, done, gamma, B, T, output));
 }
 
 int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
@@ -128,7 +111,7 @@ int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamm
 // ---------------------------------------------------------------------------------------- LIF
 void b200_leaky(const float* input_current, const float* mem0, const float* beta, const float* threshold,
                 int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem) {
-  record(b200::lif::run(input_current, mem0, beta, threshold, T, B, H, spikes, final_mem, nullptr));
+  record(b200::dropin::leaky(input_current, mem0, beta, threshold, T, B, H, spikes, final_mem));
 }
 
 int b200_leaky_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
@@ -139,7 +122,7 @@ int b200_leaky_async(const float* input_current, const float* mem0, const float*
 // --------------------------------------------------------------------------------- FP8 linear
 void b200_fp8_linear(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8, float scale_x,
                      const uint8_t* w_fp8, float scale_w, const uint16_t* bias, uint16_t* output) {
-  record(b200::fp8::run(M, K, N, x_fp8, scale_x, w_fp8, scale_w, bias, output, nullptr));
+  record(b200::dropin::fp8_linear(M, K, N, x_fp8, scale_x, w_fp8, scale_w, bias, output));
 }
 
 int b200_fp8_linear_async(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8, float scale_x,
@@ -164,13 +147,8 @@ int b200_fp8_linear_plan(const int32_t M, const int32_t K, const int32_t N, cons
 void b200_efficient_kan(const float* x, const float* grid, const float* base_weight, const float* spline_weight,
                         const float* spline_scaler, int32_t grid_size, int32_t spline_order, int32_t B, int32_t I,
                         int32_t O, float* out) {
-  if (B < 0 || I < 0 || O < 0 || grid_size < 1 || spline_order < 0) return record(b200::kInvalidArgument);
-  int st = 0;
-  const size_t ws = b200::kan::workspace_bytes(B, I, O, grid_size + spline_order);
-  void* w = b200::arena_get(ws, nullptr, &st);
-  if (st != 0) return record(st);
-  record(b200::kan::run(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, B, I, O, out, w,
-                        ws, nullptr));
+  record(b200::dropin::efficient_kan(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, B,
+                                     I, O, out));
 }
 
 size_t b200_efficient_kan_workspace_bytes(int32_t grid_size, int32_t spline_order, int32_t B, int32_t I, int32_t O) {

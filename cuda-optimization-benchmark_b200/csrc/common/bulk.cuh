@@ -17,7 +17,8 @@ namespace b200 {
 __device__ unsigned int g_b200_fault;
 
 enum FaultBits : unsigned {
-  kFaultWaitTimeout = 1u,  // a bounded mbarrier / flag wait gave up
+  kFaultWaitTimeout = 1u,   // a bounded mbarrier / flag wait gave up
+  kFaultNoTensorCore = 2u,  // a tensor-core kernel ran from code built without sm_100a features
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s

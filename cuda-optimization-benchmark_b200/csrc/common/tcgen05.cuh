@@ -15,6 +15,16 @@
 
 #include "bulk.cuh"
 
+// tcgen05 instructions exist only in the architecture-specific sm_100a target.  A build such as
+// `nvcc -arch=sm_100a` also emits generic compute_100 PTX for the same source; in that pass the
+// wrappers below compile to nothing and the tensor-core kernels only record kFaultNoTensorCore.
+// On a B200 the driver runs the sm_100a code, never that PTX.
+#if defined(__CUDA_ARCH__) && !defined(__CUDA_ARCH_FEAT_SM100_ALL)
+#define B200_TCGEN05 0
+#else
+#define B200_TCGEN05 1
+#endif
+
 namespace b200 {
 namespace tc {
 
@@ -41,53 +51,72 @@ __host__ __device__ constexpr uint32_t idesc(int M, int N, uint32_t ab_fmt) {
 // Warp-wide: allocate `ncols` (power of two >= 32) TMEM columns; the base address is written to
 // *smem_dst.
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+#if B200_TCGEN05
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(smem_dst)),
                "r"(ncols)
                : "memory");
+#endif
 }
 __device__ __forceinline__ void tmem_relinquish() {
+#if B200_TCGEN05
   asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+#endif
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+#if B200_TCGEN05
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+#endif
 }
 
 __device__ __forceinline__ void fence_before_sync() {
+#if B200_TCGEN05
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+#endif
 }
-__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() {
+#if B200_TCGEN05
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#endif
+}
 
 // --------------------------------------------------------------------------------------- MMA
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, issued by one thread.
 __device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t id,
                                        uint32_t accumulate) {
+#if B200_TCGEN05
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(id), "r"(accumulate)
       : "memory");
+#endif
 }
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t id,
                                         uint32_t accumulate) {
+#if B200_TCGEN05
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(id), "r"(accumulate)
       : "memory");
+#endif
 }
 
 // Arrive on `bar` once every MMA previously issued by this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
+#if B200_TCGEN05
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_addr(bar))
                : "memory");
+#endif
 }
 
 // ------------------------------------------------------------------------------ TMEM -> regs
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane (base lane + i).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+#if B200_TCGEN05
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -97,8 +126,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+#endif
 }
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld_wait() {
+#if B200_TCGEN05
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#endif
+}
 
 // ---------------------------------------------------------------------------------------- TMA
 // 2-D tiled load of the box at (c0 = innermost coordinate, c1) into shared memory, completing on

@@ -6,9 +6,11 @@
 // is never freed before process exit; after the first call at a given size a call performs no
 // allocation.  Fresh memory is zero-filled on the caller's stream before first use.
 //
-// Calls that share the arena must not overlap on the GPU: issue them on one stream, or order
-// them with events.  The stream forms in the C ABI that take a caller workspace have no such
-// restriction beyond the usual one for the workspace they are given.
+// Each op has its own slot (ArenaClient), because ops keep state in their scratch between calls
+// (the reductions' completion counter must stay zero between calls).  Calls of one op that share
+// its slot must not overlap on the GPU: issue them on one stream, or order them with events.
+// The stream forms in the C ABI that take a caller workspace have no such restriction beyond the
+// usual one for the workspace they are given.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -29,21 +31,24 @@ inline std::mutex& arena_mutex() {
   return m;
 }
 
+enum ArenaClient : int { kArenaRobustL1 = 0, kArenaPpo = 1, kArenaKan = 2, kArenaClients = 3 };
+
 inline ArenaSlot* arena_slots() {
-  static ArenaSlot slots[64];
+  static ArenaSlot slots[64 * kArenaClients];
   return slots;
 }
 
 // Returns a zero-initialised-at-allocation device buffer of at least `bytes` bytes for the
-// current device, or nullptr with *status set.  Contents persist between calls.
-inline void* arena_get(size_t bytes, cudaStream_t stream, int* status) {
+// current device and the given client, or nullptr with *status set.  Contents persist between
+// calls.
+inline void* arena_get(ArenaClient client, size_t bytes, cudaStream_t stream, int* status) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     *status = kCudaError;
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(arena_mutex());
-  ArenaSlot& slot = arena_slots()[dev];
+  ArenaSlot& slot = arena_slots()[dev * kArenaClients + client];
   if (slot.bytes >= bytes && slot.ptr != nullptr) {
     *status = kOk;
     return slot.ptr;

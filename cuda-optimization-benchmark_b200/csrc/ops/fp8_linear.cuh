@@ -102,6 +102,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float scale, const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int vec_ok) {
   using C = Cfg<BN>;
   constexpr int S = C::kStages;
+#if !B200_TCGEN05
+  if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
+  return;
+#else
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[S], empty[S], tfull[2], tempty[2];
   __shared__ uint32_t tmem_base_s;
@@ -203,6 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, C::kTmemCols);
   }
+#endif
 }
 
 // ------------------------------------------------------------------------ CUDA-core fallback

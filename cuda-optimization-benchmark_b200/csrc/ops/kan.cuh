@@ -15,13 +15,16 @@
 // v is split into fp16 v_hi = fp16(v) and v_lo = fp16((v - v_hi) * 2^11) (22 significant bits
 // together), and the tensor cores form
 //   D0 = A_hi . W_hi^T      D1 = A_hi . W_lo^T + A_lo . W_hi^T      out = D0 + D1 * 2^-11
-// in two fp32 TMEM accumulators (the dropped A_lo . W_lo term is 2^-22 relative).  Rows of A and
-// of W' are scaled by powers of two so every value fits fp16; the epilogue undoes them.
+// in fp32 TMEM accumulators (the dropped A_lo . W_lo term is 2^-22 relative).  The tensor cores'
+// fp32 accumulation is not round-to-nearest, so its error grows with the number of chained MMAs;
+// D0 is therefore spread round-robin by k-block over three accumulators (a third of the chain
+// each) and summed in the epilogue, which keeps K' = 9216 well inside 1e-5.  Rows of A and of W'
+// are scaled by powers of two so every value fits fp16; the epilogue undoes them.
 //   1. prep_w_kernel: W' hi/lo planes (one CTA per output row);
 //   2. prep_a_kernel: silu + Cox-de Boor bases of x in fp32, hi/lo planes (one CTA per batch row);
-//   3. gemm_kernel: persistent warp-specialised tcgen05 GEMM (kind::f16, 128 x 256 tiles,
-//      128-byte-swizzled TMA loads of the four planes, 12 MMAs per stage), fused combine/rescale
-//      epilogue writing fp32 rows.
+//   3. gemm_kernel: persistent warp-specialised tcgen05 GEMM (kind::f16, 128 x 128 tiles, TMEM
+//      = [D0a | D0b | D0c | D1], 128-byte-swizzled TMA loads of the four planes in a 3-stage ring,
+//      12 MMAs per stage), fused combine/rescale epilogue writing fp32 rows.
 // Planes are K-padded to a multiple of 64 with zeros so every TMA row pitch is 16-byte aligned.
 #pragma once
 
@@ -38,7 +41,7 @@ namespace kan {
 
 constexpr int kMaxKnots = 64;  // G + 2K + 1 knots per input at most
 constexpr int kBM = 128;
-constexpr int kBN = 256;
+constexpr int kBN = 128;
 constexpr int kBKe = 64;       // fp16 elements of K per stage (one 128-byte swizzle row)
 constexpr int kUmmaK = 16;     // K per tcgen05.mma for 16-bit operands
 constexpr int kThreads = 192;  // warp 0 loads, warp 1 issues MMAs, warps 2-5 epilogue
@@ -48,11 +51,12 @@ constexpr float kLoUnscale = 1.0f / 2048.0f;
 constexpr float kFp16Safe = 16384.0f;    // rows are scaled so |value| < 2^14
 
 constexpr int kATile = kBM * kBKe * 2;   // 16 KB per A plane per stage
-constexpr int kWTile = kBN * kBKe * 2;   // 32 KB per W plane per stage
-constexpr int kStage = 2 * kATile + 2 * kWTile;  // 96 KB
-constexpr int kStages = 2;
+constexpr int kWTile = kBN * kBKe * 2;   // 16 KB per W plane per stage
+constexpr int kStage = 2 * kATile + 2 * kWTile;  // 64 KB
+constexpr int kStages = 3;
 constexpr int kSmem = kStages * kStage + 1024;
-constexpr int kTmemCols = 2 * kBN;       // D0 and D1
+constexpr int kD0Parts = 3;               // D0 accumulators (k-block round-robin)
+constexpr int kTmemCols = 4 * kBN;       // D0a, D0b, D0c, D1
 
 inline int64_t padded_k(int I, int C) { return (int64_t(I) * (1 + C) + kBKe - 1) / kBKe * kBKe; }
 
@@ -203,6 +207,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                 const __grid_constant__ CUtensorMap tm_whi, const __grid_constant__ CUtensorMap tm_wlo, int M, int N,
                 int64_t kp, const float* __restrict__ rs, const float* __restrict__ cs, float* __restrict__ out) {
+#if !B200_TCGEN05
+  if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
+  return;
+#else
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[kStages], empty[kStages], tfull, tempty;
   __shared__ uint32_t tmem_base_s;
@@ -258,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t id = tc::idesc(kBM, kBN, 0);  // F16 x F16 -> F32
       uint32_t kb_all = 0, it = 0;
-      const uint32_t d0 = tmem, d1 = tmem + kBN;
+      const uint32_t d1 = tmem + kD0Parts * kBN;
       for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         mbar_wait(&tempty, (it & 1u) ^ 1u);
         tc::fence_after_sync();
@@ -271,12 +279,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t alo = tc::sdesc_kmajor_sw128(base + kATile);
           const uint64_t whi = tc::sdesc_kmajor_sw128(base + 2 * kATile);
           const uint64_t wlo = tc::sdesc_kmajor_sw128(base + 2 * kATile + kWTile);
+          const uint32_t d0 = tmem + uint32_t(kb % kD0Parts) * kBN;
 #pragma unroll
           for (int k = 0; k < kBKe / kUmmaK; ++k) {
             const uint64_t adv = uint64_t((k * kUmmaK * 2) >> 4);
-            const uint32_t first = (kb | k) != 0 ? 1u : 0u;
-            tc::mma_f16(d0, ahi + adv, whi + adv, id, first);
-            tc::mma_f16(d1, ahi + adv, wlo + adv, id, first);
+            tc::mma_f16(d0, ahi + adv, whi + adv, id, (kb >= kD0Parts || k != 0) ? 1u : 0u);
+            tc::mma_f16(d1, ahi + adv, wlo + adv, id, (kb | k) != 0 ? 1u : 0u);
             tc::mma_f16(d1, alo + adv, whi + adv, id, 1u);
           }
           tc::mma_commit(&empty[s]);
@@ -295,13 +303,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = mb * kBM + q * 32 + lane;
       const float rsc = row < M ? rs[row] : 0.0f;
       const bool vec_ok = (N % 4) == 0;
+      const int parts = nkb < kD0Parts ? nkb : kD0Parts;  // D0 accumulators written this tile
 #pragma unroll 1
       for (int cc = 0; cc < kBN / 32; ++cc) {
-        uint32_t a[32], c[32];
+        uint32_t a[32], c[32], t[32];
         const uint32_t lane_off = uint32_t(q * 32) << 16;
         tc::tmem_ld32(tmem + lane_off + uint32_t(cc * 32), a);
-        tc::tmem_ld32(tmem + lane_off + uint32_t(kBN + cc * 32), c);
+        tc::tmem_ld32(tmem + lane_off + uint32_t(kD0Parts * kBN + cc * 32), c);
         tc::tmem_ld_wait();
+        for (int p = 1; p < parts; ++p) {
+          tc::tmem_ld32(tmem + lane_off + uint32_t(p * kBN + cc * 32), t);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) a[j] = __float_as_uint(__uint_as_float(a[j]) + __uint_as_float(t[j]));
+        }
         const int n0 = nb * kBN + cc * 32;
         if (row < M) {
           float* o = out + int64_t(row) * N + n0;
@@ -333,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
+#endif
 }
 
 inline size_t workspace_bytes(int B, int I, int O, int C) { return layout(B, I, O, C).total; }

@@ -38,7 +38,7 @@ constexpr int kThreads = 32 * kWarps;
 constexpr int kRewardBytes = ((kSeg * 4 + 16) + 15) / 16 * 16;
 constexpr int kDoneBytes = ((kSeg + 16 + 16) + 15) / 16 * 16;  // + 16: done_mask reads 40-byte windows
 constexpr int kWarpSmem = kRewardBytes + kDoneBytes;
-constexpr int kSmemBytes = 2 * kWarps * kWarpSmem;  // two staging buffers per warp
+constexpr int kSmemPerBuffer = kWarps * kWarpSmem;  // one staging buffer per warp
 
 // Write sfrom[phase .. phase+len) to dst[0..len).  When dst has the same 16-byte phase as the
 // staged data, full groups go out as 128-bit streaming stores; otherwise lane-strided scalars.
@@ -208,15 +208,16 @@ __device__ __forceinline__ double scan_pass(const Pass& p, float* s_r, const uns
 }
 
 // Each warp streams its rows (row = warp id, + total warps, ...) pass by pass, from the end of a
-// row to its start, through two staging buffers: the next pass is in flight while the current
-// one is scanned and written out.
-__global__ void __launch_bounds__(kThreads) rtg_kernel(const float* __restrict__ reward,
+// row to its start.  With nbuf = 2 the next pass is in flight in the second staging buffer while
+// the current one is scanned and written out; with nbuf = 1 (every warp has a single pass, and the
+// smaller footprint lets 40 warps share an SM) passes are staged one after the other.
+__global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restrict__ reward,
                                                        const unsigned char* __restrict__ done, float gamma,
-                                                       int B, int T, float* __restrict__ out) {
+                                                       int B, int T, int nbuf, float* __restrict__ out) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint64_t bars[kWarps][2];  // one barrier per staging buffer
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned char* wbase = smem + warp * 2 * kWarpSmem;  // buffer b at wbase + b * kWarpSmem
+  unsigned char* wbase = smem + warp * nbuf * kWarpSmem;  // buffer b at wbase + b * kWarpSmem
   auto s_rb = [&](uint32_t b) { return reinterpret_cast<float*>(wbase + b * kWarpSmem); };
   auto s_db = [&](uint32_t b) { return wbase + b * kWarpSmem + kRewardBytes; };
   if (lane == 0) {
@@ -248,18 +249,24 @@ __global__ void __launch_bounds__(kThreads) rtg_kernel(const float* __restrict__
     Pass nxt{};
     Edges enxt{0.f, 0.f, 0u, 0u};
     const uint32_t nb = (k + 1) & 1u;
-    if (has_next) {
+    if (has_next && nbuf == 2) {
       const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
       nxt = make_pass(reward + nrow * int64_t(T), done + nrow * int64_t(T), nt0, nt1 - nt0);
       enxt = issue_pass(nxt, s_rb(nb), s_db(nb), &bars[warp][nb], lane);
     }
-    const uint32_t cb = k & 1u;
-    land_pass(cur, ecur, s_rb(cb), s_db(cb), &bars[warp][cb], (k >> 1) & 1u, lane);
+    const uint32_t cb = nbuf == 2 ? (k & 1u) : 0u;
+    const uint32_t par = nbuf == 2 ? ((k >> 1) & 1u) : (k & 1u);
+    land_pass(cur, ecur, s_rb(cb), s_db(cb), &bars[warp][cb], par, lane);
     const double first = scan_pass(cur, s_rb(cb), s_db(cb), carry, g, gamma, lane);
     const int t0 = t1 > kSeg ? t1 - kSeg : 0;
     drain_floats(out + row * int64_t(T) + t0, cur.len, s_rb(cb), cur.pr, lane);
     __syncwarp();
     if (!has_next) break;
+    if (nbuf == 1) {
+      const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
+      nxt = make_pass(reward + nrow * int64_t(T), done + nrow * int64_t(T), nt0, nt1 - nt0);
+      enxt = issue_pass(nxt, s_rb(0), s_db(0), &bars[warp][0], lane);
+    }
     carry = (nrow == row) ? first : 0.0;
     row = nrow;
     t1 = nt1;
@@ -274,12 +281,15 @@ inline int run(const float* reward, const unsigned char* done, float gamma, int3
   if (B < 0 || T < 0) return kInvalidArgument;
   if (B == 0 || T == 0) return kOk;
   if (reward == nullptr || done == nullptr || out == nullptr) return kInvalidArgument;
-  // About 8 warps per SM, each streaming several rows: loads of one row overlap the scan of the
-  // previous one.
+  // One row per warp in a single wave when the batch fits (10 CTAs = 40 warps per SM, one staging
+  // buffer each); otherwise about 8 warps per SM streaming several rows through two buffers.
   const int64_t ctas_needed = (int64_t(B) + kWarps - 1) / kWarps;
-  const int64_t cap = int64_t(sm_count()) * 2;
+  const int64_t one_wave = int64_t(sm_count()) * resident_ctas_per_sm(rtg_kernel, kThreads, kSmemPerBuffer);
+  const bool single = ctas_needed <= one_wave && T <= kSeg;
+  const int nbuf = single ? 1 : 2;
+  const int64_t cap = single ? one_wave : int64_t(sm_count()) * 2;
   const int grid = int(ctas_needed < cap ? ctas_needed : cap);
-  rtg_kernel<<<grid, kThreads, kSmemBytes, stream>>>(reward, done, gamma, B, T, out);
+  rtg_kernel<<<grid, kThreads, nbuf * kSmemPerBuffer, stream>>>(reward, done, gamma, B, T, nbuf, out);
   return launch_status();
 }
 
