@@ -58,5 +58,22 @@ def build_library(force=False, verbose=False):
     return LIB
 
 
+def build_grader_libs(verbose=False):
+    """Build every abi/<task>/solution.cu the way the reference grader does (in parallel)."""
+    import importlib.util
+    from concurrent.futures import ThreadPoolExecutor
+    spec = importlib.util.spec_from_file_location("b200_amalgamate", PKG / "abi" / "amalgamate.py")
+    am = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(am)
+    if am.main(check=True) != 0:
+        raise RuntimeError("abi/*/solution.cu are stale: run abi/amalgamate.py")
+    with ThreadPoolExecutor(max_workers=6) as ex:
+        paths = list(ex.map(lambda t: am.build_grader_lib(t, nvcc()), list(am.TASKS)))
+    if verbose:
+        for p in paths:
+            print(p, flush=True)
+    return paths
+
+
 if __name__ == "__main__":
     print(build_library(force="--force" in sys.argv, verbose=True))

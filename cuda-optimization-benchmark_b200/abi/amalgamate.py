@@ -48,6 +48,45 @@ TASKS = {
 }
 
 INCLUDE = re.compile(r'^\s*#\s*include\s+"([^"]+)"')
+BUILD = ABI / "_build"
+# The reference grader's nvcc flags (graders/grade.py:40,104-107), arch for B200.
+GRADER_FLAGS = ["-arch=sm_100a", "-O3", "-shared", "-Xcompiler", "-fPIC", "-cudart", "shared", "-Xlinker",
+                "-Bsymbolic"]
+
+
+def params(task):
+    """[(c type, name)] of the task's `void reference(...)` signature."""
+    inner = TASKS[task][0].split("(", 1)[1].rsplit(")", 1)[0]
+    out = []
+    for p in inner.split(","):
+        p = " ".join(p.split())
+        name = re.findall(r"[A-Za-z_]\w*", p)[-1]
+        out.append((p[: p.rindex(name)].strip(), name))
+    return out
+
+
+def shim(task):
+    """A grader-style shim: includes solution.cu and exposes extern "C" grader_entry(void** a),
+    where a[i] is the address of argument i's value (the grader's calling protocol)."""
+    args = []
+    for i, (ctype, _) in enumerate(params(task)):
+        t = ctype if "*" in ctype else ctype.replace("const ", "", 1)
+        args.append(f"*({t}*)a[{i}]")
+    return '#include "solution.cu"\nextern "C" void grader_entry(void** a) { reference(' + ", ".join(args) + "); }\n"
+
+
+def build_grader_lib(task, nvcc="nvcc"):
+    """Compile abi/<task>/solution.cu with the grader's command line into abi/_build/<task>/kernel.so."""
+    import shutil
+    import subprocess
+    d = BUILD / task
+    d.mkdir(parents=True, exist_ok=True)
+    shutil.copyfile(ABI / task / "solution.cu", d / "solution.cu")
+    (d / "shim.cu").write_text(shim(task))
+    r = subprocess.run([nvcc, *GRADER_FLAGS, "-o", "kernel.so", "shim.cu"], cwd=d, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"grader-style build of {task} failed:\n{r.stderr[-3000:]}")
+    return d / "kernel.so"
 
 
 def inline(path, seen, out):

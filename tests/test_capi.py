@@ -68,3 +68,17 @@ def test_built_for_sm100a_only():
     b = pkg()._build
     assert b.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
     assert Path(b.LIB).exists()
+
+
+def test_amalgamations_are_current():
+    """abi/<task>/solution.cu (the grader drop-ins) match what abi/amalgamate.py generates now."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("b200_amalgamate_c", REPO / "cuda-optimization-benchmark_b200" /
+                                                  "abi" / "amalgamate.py")
+    am = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(am)
+    assert am.main(check=True) == 0
+    for task in am.TASKS:
+        text = (am.ABI / task / "solution.cu").read_text()
+        assert am.TASKS[task][0] + " {" in text      # the verbatim reference signature
+        assert "#include \"" not in text             # one self-contained translation unit
