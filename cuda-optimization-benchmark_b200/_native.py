@@ -26,6 +26,7 @@ SIGNATURES = {
     "b200_pow_abs_sqrt_mean": (None, [c_p, c_p, c_i64, c_i64, c_i64, c_p]),
     "b200_robust_l1_workspace_bytes": (c_sz, [c_i64]),
     "b200_robust_l1_async": (c_int, [c_p, c_p, c_i64, c_p, c_p, c_sz, c_p]),
+    "b200_pow_abs_sqrt_mean_noalloc": (c_int, [c_p, c_p, c_i64, c_i64, c_i64, c_p, c_p]),
     "b200_robust_l1_chunk_elems": (c_i64, []),
     "b200_robust_l1_shard_partials": (c_int, [c_p, c_p, c_i64, c_p, c_p]),
     "b200_robust_l1_finish": (c_int, [c_p, c_i64, c_i64, c_p, c_p]),

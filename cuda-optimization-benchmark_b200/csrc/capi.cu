@@ -165,3 +165,67 @@ int b200_efficient_kan_async(const float* x, const float* grid, const float* bas
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------- robust-L1 without allocating
+// b200_pow_abs_sqrt_mean_noalloc: the robust-L1 mean for callers that must not allocate device
+// memory at all.  Such callers exist: a serving engine or framework that reserves the whole GPU
+// for its own pool (a stray cudaMalloc then fails or fragments that pool), a plugin host whose
+// contract forbids plugins from allocating, or a latency-critical loop that cannot take the
+// implicit device synchronisation and unpredictable latency of cudaMalloc/cudaFree.  The regular
+// entry points take their scratch from an arena that cudaMalloc fills on first use; this one uses
+// a fixed array of device memory compiled into the library instead.
+//
+// The array is kNoAllocScratchBytes (131,328 bytes) per GPU: a 256-byte counter block plus one
+// fp64 partial per 8192-element chunk, enough for kNoAllocMaxElems = 2^27 elements; larger calls
+// are refused with B200_WORKSPACE_TOO_SMALL before anything is launched.  Every GPU that loads the
+// library holds the array until the process exits.  All calls on a device share it, so calls that
+// overlap on the GPU (different streams, no ordering) race on it; calls on one stream are safe.
+// The first call on each device looks up the array's device address (cudaGetSymbolAddress with
+// that device current) and caches it; make that first call before any stream capture begins.
+// Each call clears the counter block on its stream before launching, so a call never depends on
+// what an earlier call left there; the partials are fully rewritten by every call.
+namespace {
+constexpr int64_t kNoAllocMaxElems = int64_t(1) << 27;
+constexpr size_t kNoAllocScratchBytes =
+    256 + size_t(kNoAllocMaxElems / b200::robust_l1::kChunk) * sizeof(double);  // 131,328 bytes
+}  // namespace
+
+// In host code this name is only a stand-in for the array, not a device address: the kernel must
+// be given the address returned by cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+// Device address of g_noalloc_scratch on the current device (looked up once per device).
+void* noalloc_scratch(int* status) {
+  static void* addr[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = b200::kCudaError;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      *status = b200::kCudaError;
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  *status = b200::kOk;
+  return addr[dev];
+}
+}  // namespace
+
+extern "C" int b200_pow_abs_sqrt_mean_noalloc(const float* inp, const float* target, int64_t batch_size,
+                                              int64_t height, int64_t width, float* output, void* stream) {
+  const int64_t n = b200::robust_l1::abi_count(batch_size, height, width);
+  if (n < 0) return b200::kInvalidArgument;
+  if (n > kNoAllocMaxElems) return b200::kWorkspaceTooSmall;
+  int st = 0;
+  void* scratch = noalloc_scratch(&st);
+  if (st != b200::kOk) return st;
+  if (cudaMemsetAsync(scratch, 0, 256, as_stream(stream)) != cudaSuccess) return b200::kCudaError;
+  return b200::robust_l1::run(inp, target, n, output, scratch, kNoAllocScratchBytes, as_stream(stream));
+}

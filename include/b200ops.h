@@ -61,6 +61,19 @@ size_t b200_robust_l1_workspace_bytes(int64_t n);
 int b200_robust_l1_async(const float* inp, const float* target, int64_t n, float* output, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* Robust-L1 mean that allocates nothing, for callers that may not allocate device memory: a
+ * framework or serving engine that owns the whole GPU through its own memory pool, a plugin host
+ * whose contract forbids allocation, or a latency-critical loop that cannot take cudaMalloc's
+ * implicit synchronisation.  This entry point has no counterpart in the reference.  Scratch is a
+ * 131,328-byte device array inside the library, held by every GPU that loads it until exit, so a
+ * call may cover at most B200_NOALLOC_MAX_ELEMS elements (batch_size*4*height*width); larger calls
+ * return B200_WORKSPACE_TOO_SMALL without launching.  The first call on a device looks up the
+ * array's device address; make it before any stream capture begins.  All calls on a device share
+ * the array: calls that overlap on the GPU race, calls ordered on one stream do not. */
+#define B200_NOALLOC_MAX_ELEMS 134217728LL
+int b200_pow_abs_sqrt_mean_noalloc(const float* inp, const float* target, int64_t batch_size, int64_t height,
+                                   int64_t width, float* output, void* stream);
+
 /* Multi-GPU halves.  The global element range is cut into chunks of b200_robust_l1_chunk_elems();
  * a shard must start on a chunk boundary.  shard_partials writes one double per local chunk;
  * finish sums the gathered partials of all shards (in chunk order) and divides by n_total.  The
