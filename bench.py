@@ -439,6 +439,59 @@ def run_reference(args, world, rank):
             "e2e": {"value": v, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+PROFILE_FP8 = {"fp8_m16": (16, 4096, 4096), "fp8_m1024": (1024, 4096, 4096), "fp8_8192": (8192, 8192, 8192),
+               "fp8_16384": (16384, 28672, 8192), "fp8_ref_timed": (2048, 4096, 1024)}
+
+
+def run_profile(ops_list, reps):
+    """Run each listed op `reps` times at its BASELINE size on cuda:0 and print nothing but the
+    device fault word: the workload for `ncu` launch lists and captures (profiles/*.md)."""
+    from oracle import inputs
+    pkg = importlib.import_module("cuda-optimization-benchmark_b200")
+    lib = pkg.load()
+    ops = pkg.ops
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if "rtg" in ops_list or "ppo" in ops_list:
+        s = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs.baseline_inputs("rl_pipeline", 0).items()}
+        out = torch.empty(B, T, device=dev)
+        po = torch.empty(7, device=dev)
+        for _ in range(reps):
+            if "rtg" in ops_list:
+                ops.reward_to_go(s["reward"], s["done"], s["gamma"], out=out)
+            if "ppo" in ops_list:
+                ops.ppo_clip(s["current_log_prob"], s["old_log_prob"], s["advantage"], 0.2, s["entropy"], out=po)
+    if "lif" in ops_list:
+        s = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs.baseline_inputs("lif", 0).items()}
+        for _ in range(reps):
+            ops.leaky(s["input_current"], s["mem0"], s["beta"], s["threshold"])
+    if "robust_l1" in ops_list:
+        s = inputs.baseline_inputs("robust_l1", 0)
+        a, b = s["inp"].to(dev), s["target"].to(dev)
+        for _ in range(reps):
+            ops.robust_l1(a, b)
+    if "kan" in ops_list:
+        s = inputs.baseline_inputs("kan", 0)
+        t = {k: s[k].to(dev) for k in ["x", "grid", "base_weight", "spline_weight", "spline_scaler"]}
+        out = torch.empty(s["B"], s["O"], device=dev)
+        nb = lib.b200_efficient_kan_workspace_bytes(5, 3, s["B"], s["I"], s["O"])
+        ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+        for _ in range(reps):
+            lib.b200_efficient_kan_async(t["x"].data_ptr(), t["grid"].data_ptr(), t["base_weight"].data_ptr(),
+                                         t["spline_weight"].data_ptr(), t["spline_scaler"].data_ptr(), 5, 3, s["B"],
+                                         s["I"], s["O"], out.data_ptr(), ws.data_ptr(), nb, None)
+    for name in [x for x in ops_list if x in PROFILE_FP8]:
+        M, N, K = PROFILE_FP8[name]
+        s = inputs.baseline_inputs("fp8_linear", 0, shape=(M, N, K))
+        x, w, bb = s["x_fp8"].to(dev), s["w_fp8"].to(dev), s["bias"].to(dev)
+        o = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        for _ in range(reps):
+            lib.b200_fp8_linear_async(M, K, N, x.data_ptr(), s["scale_x"], w.data_ptr(), s["scale_w"], bb.data_ptr(),
+                                      o.data_ptr(), None)
+    torch.cuda.synchronize()
+    print("device fault word:", lib.b200_device_fault(), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -447,7 +500,13 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--profile", default=None,
+                    help="comma list of ops (rtg, ppo, lif, robust_l1, kan, fp8_m16, fp8_m1024, fp8_8192, fp8_16384, "
+                         "fp8_ref_timed): run each --steps times for ncu, no timing")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args.profile.split(","), args.steps)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -114,34 +114,40 @@ __device__ __forceinline__ float block_max(float v, float* s_red) {
 }
 
 // ---------------------------------------------------------------------------------- W' planes
-// One CTA per output row o.  w'(p=0, i) = W_base[o,i]; w'(p=1+c, i) = sw[o,i,c] * scaler[o,i]
-// (the fp32 product the reference forms, tasks/efficient_kan/reference.py:45).
+// One CTA per output row o, one thread per input i at a time (input-major, so each thread reads
+// its C contiguous spline weights and the warp's reads are contiguous).  w'(p=0, i) = W_base[o,i];
+// w'(p=1+c, i) = sw[o,i,c] * scaler[o,i] (the fp32 product the reference forms,
+// tasks/efficient_kan/reference.py:45).  Pass 1 finds the row's max |w'|, pass 2 writes the planes.
 __global__ void __launch_bounds__(256) prep_w_kernel(const float* __restrict__ wb, const float* __restrict__ sw,
                                                      const float* __restrict__ sc, int I, int O, int C, int64_t kp,
                                                      __half* __restrict__ w_hi, __half* __restrict__ w_lo,
                                                      float* __restrict__ cs) {
   __shared__ float s_red[33];
   const int o = blockIdx.x;
-  const int64_t kk = int64_t(I) * (1 + C);
+  const float* wbr = wb + int64_t(o) * I;
+  const float* swr = sw + int64_t(o) * I * C;
+  const float* scr = sc + int64_t(o) * I;
   float amax = 0.0f;
-  for (int64_t q = threadIdx.x; q < kk; q += blockDim.x) {
-    const int p = int(q / I), i = int(q - int64_t(p) * I);
-    const float v = p == 0 ? wb[int64_t(o) * I + i]
-                           : __fmul_rn(sw[(int64_t(o) * I + i) * C + (p - 1)], sc[int64_t(o) * I + i]);
-    amax = fmaxf(amax, fabsf(v));
+  for (int i = threadIdx.x; i < I; i += blockDim.x) {
+    amax = fmaxf(amax, fabsf(__ldg(wbr + i)));
+    const float sv = __ldg(scr + i);
+    for (int c = 0; c < C; ++c) amax = fmaxf(amax, fabsf(__fmul_rn(__ldg(swr + int64_t(i) * C + c), sv)));
   }
   const float f = fp16_row_factor(block_max(amax, s_red));
   if (threadIdx.x == 0) cs[o] = 1.0f / f;
   __half* hr = w_hi + int64_t(o) * kp;
   __half* lr = w_lo + int64_t(o) * kp;
-  for (int64_t q = threadIdx.x; q < kp; q += blockDim.x) {
-    float v = 0.0f;
-    if (q < kk) {
-      const int p = int(q / I), i = int(q - int64_t(p) * I);
-      v = p == 0 ? wb[int64_t(o) * I + i]
-                 : __fmul_rn(sw[(int64_t(o) * I + i) * C + (p - 1)], sc[int64_t(o) * I + i]);
-    }
-    split_store(v * f, hr + q, lr + q);
+  for (int i = threadIdx.x; i < I; i += blockDim.x) {
+    split_store(__ldg(wbr + i) * f, hr + i, lr + i);
+    const float sv = __ldg(scr + i);
+    for (int c = 0; c < C; ++c)
+      split_store(__fmul_rn(__ldg(swr + int64_t(i) * C + c), sv) * f, hr + int64_t(1 + c) * I + i,
+                  lr + int64_t(1 + c) * I + i);
+  }
+  const int64_t kk = int64_t(I) * (1 + C);
+  for (int64_t q = kk + threadIdx.x; q < kp; q += blockDim.x) {
+    hr[q] = __float2half_rn(0.0f);
+    lr[q] = __float2half_rn(0.0f);
   }
 }
 
@@ -162,13 +168,36 @@ __device__ __forceinline__ void bases_of(float x, const float* g, int nk, int K,
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
-// One CTA per batch row b; the grid is read per input (knots of input i at grid + i*nk).
+// Same recurrence with the knot count NK and order KO known at compile time: fully unrolled, the
+// knot and basis arrays stay in registers.
+template <int NK, int KO>
+__device__ __forceinline__ void bases_fixed(float x, const float* __restrict__ gsrc, float* b) {
+  float g[NK];
+#pragma unroll
+  for (int j = 0; j < NK; ++j) g[j] = __ldg(gsrc + j);
+#pragma unroll
+  for (int j = 0; j < NK - 1; ++j) b[j] = (x >= g[j] && x < g[j + 1]) ? 1.0f : 0.0f;
+#pragma unroll
+  for (int k = 1; k <= KO; ++k) {
+#pragma unroll
+    for (int j = 0; j < NK - 1 - k; ++j) {
+      const float l = __fdiv_rn(__fsub_rn(x, g[j]), __fsub_rn(g[j + k], g[j]));
+      const float r = __fdiv_rn(__fsub_rn(g[j + k + 1], x), __fsub_rn(g[j + k + 1], g[j + 1]));
+      b[j] = __fadd_rn(__fmul_rn(l, b[j]), __fmul_rn(r, b[j + 1]));
+    }
+  }
+}
+
+// One CTA per batch row b; the knots of input i are grid[i*nk .. i*nk + nk).  NK/KO > 0 select the
+// unrolled form for that (knot count, order); 0 selects the general loop.
+template <int NK, int KO>
 __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x, const float* __restrict__ grid,
                                                      int I, int C, int K, int64_t kp, __half* __restrict__ a_hi,
                                                      __half* __restrict__ a_lo, float* __restrict__ rs) {
   __shared__ float s_red[33];
   const int bi = blockIdx.x;
-  const int nk = C + K + 1;
+  const int nk = NK > 0 ? NK : C + K + 1;
+  const int nc = NK > 0 ? NK - KO - 1 : C;
   const float* xr = x + int64_t(bi) * I;
   float amax = 0.0f;
   for (int i = threadIdx.x; i < I; i += blockDim.x) amax = fmaxf(amax, fabsf(silu(xr[i])));
@@ -177,13 +206,21 @@ __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x
   if (threadIdx.x == 0) rs[bi] = 1.0f / f;
   __half* hr = a_hi + int64_t(bi) * kp;
   __half* lr = a_lo + int64_t(bi) * kp;
-  float g[kMaxKnots], b[kMaxKnots];
   for (int i = threadIdx.x; i < I; i += blockDim.x) {
     const float xv = xr[i];
-    for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
-    bases_of(xv, g, nk, K, b);
     split_store(silu(xv) * f, hr + i, lr + i);
-    for (int c = 0; c < C; ++c) split_store(b[c] * f, hr + int64_t(1 + c) * I + i, lr + int64_t(1 + c) * I + i);
+    if (NK > 0) {
+      float b[NK > 0 ? NK : 1];
+      bases_fixed<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, b);
+#pragma unroll
+      for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c)
+        split_store(b[c] * f, hr + int64_t(1 + c) * I + i, lr + int64_t(1 + c) * I + i);
+    } else {
+      float g[kMaxKnots], b[kMaxKnots];
+      for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
+      bases_of(xv, g, nk, K, b);
+      for (int c = 0; c < nc; ++c) split_store(b[c] * f, hr + int64_t(1 + c) * I + i, lr + int64_t(1 + c) * I + i);
+    }
   }
   const int64_t kk = int64_t(I) * (1 + C);
   for (int64_t q = kk + threadIdx.x; q < kp; q += blockDim.x) {
@@ -378,7 +415,9 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   float* cs = reinterpret_cast<float*>(w + L.cs);
   const int64_t kp = padded_k(I, C);
   prep_w_kernel<<<O, 256, 0, stream>>>(wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
-  prep_a_kernel<<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  if (G == 5 && K == 3) prep_a_kernel<12, 3><<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  else if (G == 8 && K == 3) prep_a_kernel<15, 3><<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  else prep_a_kernel<0, 0><<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
   CUtensorMap m_ahi, m_alo, m_whi, m_wlo;
   if (!tc::make_map_sw128(&m_ahi, a_hi, uint64_t(B), uint64_t(kp), 2, kBM) ||
       !tc::make_map_sw128(&m_alo, a_lo, uint64_t(B), uint64_t(kp), 2, kBM) ||

@@ -41,7 +41,7 @@ namespace ppo {
 constexpr int kThreads = 512;                                       // consumer threads
 constexpr int kVecPerThread = 2;                                    // float4 per input per thread
 constexpr int64_t kChunk = int64_t(kThreads) * kVecPerThread * 4;  // 4096 elements per chunk
-constexpr int kPipeThreads = kThreads + 32;                         // + one producer warp
+constexpr int kPipeThreads = kThreads + 64;                         // + producer and reducer warps
 constexpr uint32_t kRedBar = 1;                                     // named barrier of the consumers
 constexpr int kOutputs = 6;
 constexpr int kOutputsExt = 7;
@@ -186,42 +186,94 @@ __device__ __forceinline__ void thread_chunk_global(Acc& acc, const float* __res
   }
 }
 
-// Fixed-order reduction of the consumer threads' accumulators into one chunk partial (valid in
-// thread 0).  Uses a named barrier over the kThreads consumer threads only.
-__device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
-  __shared__ double s_d[5][kThreads / 32];
-  __shared__ float s_max[kThreads / 32];
-  __shared__ unsigned s_cnt[kThreads / 32];
-  double v[5] = {double(acc.gain) + acc.big_gain, double(acc.lw) + acc.big_lw, double(acc.r) + acc.big_r,
-                 double(acc.r2) + acc.big_r2, double(acc.ent)};
+// Warp-level record of one chunk (fp32 sums of the warp's 256 samples; the fp64 sums of the rare
+// lw > 30 samples).  The reducer warp combines a chunk's 16 records in a fixed order.
+struct WarpPart {
+  float gain, lw, r, r2, ent, rmax;
+  unsigned clipped, pad;
+  double big_gain, big_lw, big_r, big_r2;
+};
+constexpr int kSlots = 4;                       // chunks in flight between consumers and reducer
+constexpr int kConsumerWarps = kThreads / 32;   // 16
+
+__device__ __forceinline__ void warp_record(const Acc& acc, WarpPart* slot, int lane) {
+  float v[5] = {acc.gain, acc.lw, acc.r, acc.r2, acc.ent};
 #pragma unroll
-  for (int q = 0; q < 5; ++q) v[q] = warp_sum(v[q]);
+  for (int q = 0; q < 5; ++q)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(0xffffffffu, v[q], o);
   const float m = warp_max(acc.rmax);
   const unsigned cnt = warp_sum_u32(acc.clipped);
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) {
-#pragma unroll
-    for (int q = 0; q < 5; ++q) s_d[q][w] = v[q];
-    s_max[w] = m;
-    s_cnt[w] = cnt;
+  const bool any_big = __any_sync(0xffffffffu, acc.big_r != 0.0);
+  double bg = acc.big_gain, bl = acc.big_lw, br = acc.big_r, br2 = acc.big_r2;
+  if (any_big) {
+    bg = warp_sum(bg);
+    bl = warp_sum(bl);
+    br = warp_sum(br);
+    br2 = warp_sum(br2);
   }
+  if (lane == 0) {
+    WarpPart w;
+    w.gain = v[0];
+    w.lw = v[1];
+    w.r = v[2];
+    w.r2 = v[3];
+    w.ent = v[4];
+    w.rmax = m;
+    w.clipped = cnt;
+    w.pad = 0;
+    w.big_gain = any_big ? bg : 0.0;
+    w.big_lw = any_big ? bl : 0.0;
+    w.big_r = any_big ? br : 0.0;
+    w.big_r2 = any_big ? br2 : 0.0;
+    *slot = w;
+  }
+}
+
+// Combine a chunk's kConsumerWarps warp records (lane w holds record w) into the chunk partial,
+// valid in lane 0: fp64, fixed butterfly order.  Shared by every path, so all give the same bits.
+__device__ __forceinline__ Partial combine_records(const WarpPart* recs, int lane) {
+  double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+  float m = 0.f;
+  unsigned cnt = 0;
+  if (lane < kConsumerWarps) {
+    const WarpPart& w = recs[lane];
+    v[0] = double(w.gain);
+    v[1] = double(w.lw);
+    v[2] = double(w.r);
+    v[3] = double(w.r2);
+    v[4] = double(w.ent);
+    v[5] = w.big_gain;
+    v[6] = w.big_lw;
+    v[7] = w.big_r;
+    v[8] = w.big_r2;
+    m = w.rmax;
+    cnt = w.clipped;
+  }
+#pragma unroll
+  for (int q = 0; q < 9; ++q) v[q] = warp_sum(v[q]);
+  m = warp_max(m);
+  cnt = warp_sum_u32(cnt);
+  Partial p;
+  p.gain = v[0] + v[5];
+  p.lw = v[1] + v[6];
+  p.r = v[2] + v[7];
+  p.r2 = v[3] + v[8];
+  p.ent = v[4];
+  p.rmax = m;
+  p.clipped = cnt;
+  return p;
+}
+
+// Chunk partial of the kThreads consumer threads' accumulators (valid in thread 0), through the
+// same warp records and combine as the pipelined path.  Uses a named barrier over the consumers.
+__device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
+  __shared__ WarpPart s_rec[kConsumerWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  warp_record(acc, &s_rec[warp], lane);
   named_sync(kRedBar, kThreads);
   Partial p{};
-  if (threadIdx.x == 0) {
-    p.gain = p.lw = p.r = p.r2 = p.ent = 0.0;
-    p.rmax = 0.f;
-    p.clipped = 0;
-#pragma unroll
-    for (int i = 0; i < kThreads / 32; ++i) {
-      p.gain += s_d[0][i];
-      p.lw += s_d[1][i];
-      p.r += s_d[2][i];
-      p.r2 += s_d[3][i];
-      p.ent += s_d[4][i];
-      p.rmax = fmaxf(p.rmax, s_max[i]);
-      p.clipped += s_cnt[i];
-    }
-  }
+  if (warp == 0) p = combine_records(s_rec, lane);
   named_sync(kRedBar, kThreads);
   return p;
 }
@@ -294,9 +346,10 @@ __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict
   }
 }
 
-// Pipelined form (16-byte aligned inputs).  Warps 0-7 consume, warp 8 produces.  Full chunks go
-// through the bulk-copy ring; a trailing partial chunk is reduced from global memory by the CTA
-// that owns it, with the same element order.
+// Pipelined form (16-byte aligned inputs).  Warps 0-15 consume, warp 16 produces (bulk-copy ring),
+// warp 17 reduces (16 warp records -> one chunk partial, fixed order, fp64).  A trailing partial
+// chunk is read from global memory by the consumers of the CTA that owns it, in the same element
+// order, and reduced the same way.  No CTA-wide barrier inside the loop.
 template <bool kEnt, bool kFinish>
 __global__ void __launch_bounds__(kPipeThreads, 1)
     pipe_kernel(const float* __restrict__ cur, const float* __restrict__ old, const float* __restrict__ adv,
@@ -304,20 +357,26 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
                 unsigned* __restrict__ ticket, float* __restrict__ out) {
   using P = Pipe<kEnt>;
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t full[P::kStages], empty[P::kStages];
+  __shared__ uint64_t full[P::kStages], empty[P::kStages], rec_full[kSlots], rec_free[kSlots];
+  __shared__ WarpPart recs[kSlots][kConsumerWarps];
   const int64_t n_chunks = (n + kChunk - 1) / kChunk;
   const int64_t n_full = n / kChunk;
+  const bool own_tail = n_full < n_chunks && (n_chunks - 1) % gridDim.x == blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < P::kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kThreads / 32);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&rec_full[s], kConsumerWarps);
+      mbar_init(&rec_free[s], 1);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == kThreads / 32) {
+  if (warp == kConsumerWarps) {
     // Producer: one lane keeps the ring full.
     if (lane == 0) {
       const float* src[4] = {cur, old, adv, ent};
@@ -332,32 +391,56 @@ __global__ void __launch_bounds__(kPipeThreads, 1)
           bulk_g2s(dst + a * P::kArrayBytes, src[a] + c * kChunk, P::kArrayBytes, &full[s]);
       }
     }
+  } else if (warp == kConsumerWarps + 1) {
+    // Reducer: chunk i's 16 warp records, lane w holds record w; fixed-order fp64 tree.
+    uint32_t i = 0;
+    auto reduce_chunk = [&](int64_t c) {
+      const uint32_t s = i % kSlots, ph = (i / kSlots) & 1u;
+      mbar_wait(&rec_full[s], ph);
+      const Partial p = combine_records(recs[s], lane);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&rec_free[s]);
+        partials[c] = p;
+      }
+      ++i;
+    };
+    for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x) reduce_chunk(c);
+    if (own_tail) reduce_chunk(n_chunks - 1);
   } else {
     uint32_t i = 0;
-    for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x, ++i) {
-      const uint32_t s = i % P::kStages, ph = (i / P::kStages) & 1u;
+    auto record = [&](const Acc& acc) {
+      const uint32_t s = i % kSlots, ph = (i / kSlots) & 1u;
+      mbar_wait(&rec_free[s], ph ^ 1u);
+      warp_record(acc, &recs[s][warp], lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rec_full[s]);
+      ++i;
+    };
+    uint32_t k = 0;
+    for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x, ++k) {
+      const uint32_t s = k % P::kStages, ph = (k / P::kStages) & 1u;
       mbar_wait(&full[s], ph);
       const float* st = reinterpret_cast<const float*>(smem + s * P::kStageBytes);
       Acc acc;
 #pragma unroll
-      for (int k = 0; k < kVecPerThread; ++k) {
-        const int e = (k * kThreads + threadIdx.x) * 4;
+      for (int kk = 0; kk < kVecPerThread; ++kk) {
+        const int e = (kk * kThreads + threadIdx.x) * 4;
         const float4 c4 = *reinterpret_cast<const float4*>(st + e);
         const float4 o4 = *reinterpret_cast<const float4*>(st + kChunk + e);
         const float4 a4 = *reinterpret_cast<const float4*>(st + 2 * kChunk + e);
-        const float4 e4 = kEnt ? *reinterpret_cast<const float4*>(st + 3 * kChunk + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 e4 =
+            kEnt ? *reinterpret_cast<const float4*>(st + 3 * kChunk + e) : make_float4(0.f, 0.f, 0.f, 0.f);
         add4<kEnt>(acc, c4, o4, a4, e4, clip);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      const Partial p = cta_reduce(acc);
-      if (threadIdx.x == 0) partials[c] = p;
+      record(acc);
     }
-    if (n_full < n_chunks && (n_chunks - 1) % gridDim.x == blockIdx.x) {
+    if (own_tail) {
       Acc acc;
       thread_chunk_global<true, kEnt>(acc, cur, old, adv, ent, (n_chunks - 1) * kChunk, n, clip);
-      const Partial p = cta_reduce(acc);
-      if (threadIdx.x == 0) partials[n_chunks - 1] = p;
+      record(acc);
     }
   }
   if (kFinish) {
