@@ -4,11 +4,13 @@
 
 Headline workload ("RL loss pipeline"): per GPU a batch of
 B=4096 trajectories x T=1000 steps; one step = discounted reward-to-go over the batch plus the
-PPO clipped loss with its diagnostics and the mean entropy over the same 4,096,000 samples.
-`value` is samples (trajectory steps) per second over all GPUs, inputs resident in HBM; the
-per-op microseconds and roofline fractions that BASELINE.json's metric names are reported beside
-it.  With N > 1 each rank processes its own batch (weak scaling) and the PPO reduction is global:
-the ranks exchange their per-chunk partials with one NCCL all-gather and all finish identically.
+PPO clipped loss with its diagnostics and the mean entropy over the same 4,096,000 samples, both
+in one launch of the fused kernel (b200_rl_step_async).  `value` is samples (trajectory steps)
+per second over all GPUs, inputs resident in HBM; the per-op microseconds and roofline fractions
+that BASELINE.json's metric names are reported beside it (the two ops also timed as separate
+launches).  With N > 1 each rank processes its own batch (weak scaling) and the PPO reduction is
+global: the fused shard launch writes per-chunk partials, the ranks exchange them with one NCCL
+all-gather and all finish identically.
 
 Timing: W untimed warm-up steps, then exactly K steps between barriers and device syncs, timed
 with CUDA events on the launching stream, max over ranks.  Each step reads a different one of
@@ -135,6 +137,20 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------ inputs
+# ncu summaries under profiles/ that record dram__bytes_read.sum + dram__bytes_write.sum of one
+# launch of a kernel at this workload, as a line "traffic_bytes_per_launch: <bytes>".
+TRAFFIC_FILES = {"rl_step": "profiles/rl_step_B4096_T1000.txt"}
+
+
+def profiled_traffic(kernel):
+    import re
+    p = REPO / TRAFFIC_FILES[kernel]
+    if not p.exists():
+        return None
+    m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", p.read_text(), flags=re.M)
+    return int(m.group(1)) if m else None
+
+
 def make_sets(dev, rank, n_sets):
     from oracle import inputs  # seeded synthetic inputs of BASELINE.json configs[1]
     sets = []
@@ -163,41 +179,52 @@ def run_b200(args, world, rank, local):
         local_parts = torch.empty((n_parts, rec), dtype=torch.uint8, device=dev)
         all_parts = torch.empty((world * n_parts, rec), dtype=torch.uint8, device=dev)
 
-    # Pre-bound C-ABI argument tuples per input set: the timed loop is two ctypes calls per step.
+    # Pre-bound C-ABI argument tuples per input set: the timed loop is one ctypes call per step
+    # (N = 1), or the fused shard launch, the NCCL all-gather and the finish launch (N > 1).
     import ctypes
     P = ctypes.c_void_p
     cs = P(stream.cuda_stream)
     ws = ops.workspace("ppo", lib.b200_ppo_workspace_bytes(N_SAMPLES), dev)
-    rtg_args, ppo_args = [], []
+    step_args, rtg_args, ppo_args = [], [], []
     for s in sets:
-        rtg_args.append((P(s["reward"].data_ptr()), P(s["done"].data_ptr()), gamma, B, T, P(rtg_out.data_ptr()), cs))
-        ppo_args.append((P(s["current_log_prob"].data_ptr()), P(s["old_log_prob"].data_ptr()),
-                         P(s["advantage"].data_ptr()), P(s["entropy"].data_ptr()), N_SAMPLES, eps,
-                         P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), cs))
-    f_rtg, f_ppo = lib.b200_reward_to_go_async, lib.b200_ppo_async
-
-    def step(i, evs=None):
-        k = i % ROTATE
-        if evs is not None:
-            evs[0].record(stream)
-        f_rtg(*rtg_args[k])
-        if evs is not None:
-            evs[1].record(stream)
+        rtg_in = (P(s["reward"].data_ptr()), P(s["done"].data_ptr()), gamma, B, T, P(rtg_out.data_ptr()))
+        ppo_in = (P(s["current_log_prob"].data_ptr()), P(s["old_log_prob"].data_ptr()),
+                  P(s["advantage"].data_ptr()), P(s["entropy"].data_ptr()), N_SAMPLES, eps)
         if world == 1:
-            f_ppo(*ppo_args[k])
+            step_args.append(rtg_in + ppo_in + (P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), cs))
         else:
-            s = sets[k]
-            parts = ops.ppo_partials(s["current_log_prob"], s["old_log_prob"], s["advantage"], eps, s["entropy"])
-            local_parts.copy_(parts)
+            step_args.append(rtg_in + ppo_in + (P(local_parts.data_ptr()), cs))
+        rtg_args.append(rtg_in + (cs,))
+        ppo_args.append(ppo_in + (P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), cs))
+    f_rtg, f_ppo = lib.b200_reward_to_go_async, lib.b200_ppo_async
+    f_step = lib.b200_rl_step_async if world == 1 else lib.b200_rl_step_shard_async
+    f_finish = lib.b200_ppo_finish
+    if world > 1:
+        finish_args = (P(all_parts.data_ptr()), world * n_parts, world * N_SAMPLES, 1, P(ppo_out.data_ptr()), cs)
+    status = [0]
+
+    def step(i):
+        status[0] |= f_step(*step_args[i % ROTATE])
+        if world > 1:
             dist.all_gather_into_tensor(all_parts, local_parts)
-            ops.ppo_finish(all_parts, world * N_SAMPLES, True, out=ppo_out)
-        if evs is not None:
-            evs[2].record(stream)
+            status[0] |= f_finish(*finish_args)
+
+    def loop_ms(fn, k):
+        """Device ms per call of `fn` over k back-to-back calls between one pair of events."""
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(k):
+            fn(i)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / k
 
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if status[0] != 0:
+        raise RuntimeError(f"rl_step returned status {status[0]}")
     clocks = ClockSampler(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
@@ -205,14 +232,41 @@ def run_b200(args, world, rank, local):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for i in range(args.steps):
-        step(i, evs[i])
+        step(i)
     t1.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
     clk = clocks.stop()
+    if status[0] != 0:
+        raise RuntimeError(f"rl_step returned status {status[0]}")
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
-    rtg_ms = max_over_ranks(statistics.mean(e[0].elapsed_time(e[1]) for e in evs), world)
-    ppo_ms = max_over_ranks(statistics.mean(e[1].elapsed_time(e[2]) for e in evs), world)
+
+    # Average duration of the fused kernel alone (the roofline's kernel): at N = 1 the timed step is
+    # exactly one launch of it; at N > 1 its shard form is timed in its own back-to-back loop.
+    def fused_only(i):
+        status[0] |= f_step(*step_args[i % ROTATE])
+    fused_ms = ms if world == 1 else max_over_ranks(loop_ms(fused_only, args.steps), world)
+
+    # The two ops as separate launches on the same rotation (per-op breakdown, unfused step time).
+    for i in range(args.warmup):
+        f_rtg(*rtg_args[i % ROTATE])
+        f_ppo(*ppo_args[i % ROTATE])
+    torch.cuda.synchronize(dev)
+
+    def rtg_only(i):
+        status[0] |= f_rtg(*rtg_args[i % ROTATE])
+
+    def ppo_only(i):
+        status[0] |= f_ppo(*ppo_args[i % ROTATE])
+
+    def both(i):
+        rtg_only(i)
+        ppo_only(i)
+    rtg_ms = max_over_ranks(loop_ms(rtg_only, args.steps), world)
+    ppo_ms = max_over_ranks(loop_ms(ppo_only, args.steps), world)
+    unfused_ms = max_over_ranks(loop_ms(both, args.steps), world)
+    if status[0] != 0:
+        raise RuntimeError(f"reward_to_go / ppo returned status {status[0]}")
 
     # Same K steps replayed from a CUDA graph (one graph per input set), no events between kernels:
     # shows how much of the eager step time is host launch overhead.
@@ -224,8 +278,7 @@ def run_b200(args, world, rank, local):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=side):
                 cs_side = P(torch.cuda.current_stream(dev).cuda_stream)
-                f_rtg(*rtg_args[k][:-1], cs_side)
-                f_ppo(*ppo_args[k][:-1], cs_side)
+                f_step(*step_args[k][:-1], cs_side)
             graphs.append(g)
         for i in range(args.warmup):
             graphs[i % ROTATE].replay()
@@ -255,14 +308,12 @@ def run_b200(args, world, rank, local):
         h = host[i % 2]
         for k in names:
             dbuf[k].copy_(h[k], non_blocking=True)
-        ops.reward_to_go(dbuf["reward"], dbuf["done"], gamma, out=rtg_out)
         if world == 1:
-            ops.ppo_clip(dbuf["current_log_prob"], dbuf["old_log_prob"], dbuf["advantage"], eps, dbuf["entropy"],
-                         out=ppo_out)
+            ops.rl_step(dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"], dbuf["old_log_prob"],
+                        dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out, ppo_out=ppo_out)
         else:
-            parts = ops.ppo_partials(dbuf["current_log_prob"], dbuf["old_log_prob"], dbuf["advantage"], eps,
-                                     dbuf["entropy"])
-            local_parts.copy_(parts)
+            ops.rl_step_shard(dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"], dbuf["old_log_prob"],
+                              dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out, partials_out=local_parts)
             dist.all_gather_into_tensor(all_parts, local_parts)
             ops.ppo_finish(all_parts, world * N_SAMPLES, True, out=ppo_out)
         rtg_host.copy_(rtg_out, non_blocking=True)
@@ -288,11 +339,9 @@ def run_b200(args, world, rank, local):
         extra = other_ops(ops, dev, world, rank)
 
     peak, peak_kind = peaks()
-    dominant = "ppo_clip_ext" if ppo_ms >= rtg_ms else "reward_to_go"
-    dom_bytes = PPO_BYTES if ppo_ms >= rtg_ms else RTG_BYTES
-    dom_ms = max(ppo_ms, rtg_ms)
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-    per_step_launches = 2 if world == 1 else 3
+    step_bytes = RTG_BYTES + PPO_BYTES
+    achieved = step_bytes / (fused_ms * 1e-3) / 1e9
+    per_step_launches = 1 if world == 1 else 2
     line = {
         "metric": METRIC,
         "value": world * N_SAMPLES / (ms * 1e-3),
@@ -303,6 +352,7 @@ def run_b200(args, world, rank, local):
         "ms_per_step": ms,
         "us_per_step": ms * 1e3,
         "graph_us_per_step": graph_ms * 1e3 if graph_ms is not None else None,
+        "unfused_us_per_step": unfused_ms * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -312,9 +362,12 @@ def run_b200(args, world, rank, local):
                    "samples_per_gpu": N_SAMPLES, "gamma": 0.99, "done_p": 0.01, "clip_epsilon": 0.2,
                    "l2": f"rotating {ROTATE} input sets of {(RTG_BYTES - 4 * N_SAMPLES + PPO_BYTES) / 1e6:.0f} MB "
                          f"(> 126 MB L2)",
-                   "parallelism": f"dp{world}: rows sharded, PPO partials all-gathered (NCCL)" if world > 1
-                   else "1 GPU"},
+                   "parallelism": f"dp{world}: one batch per rank, PPO chunk partials all-gathered (NCCL)"
+                   if world > 1 else "1 GPU"},
         "per_op": {
+            "rl_step (fused)": {"us": fused_ms * 1e3, "bytes": step_bytes,
+                                "gbs": achieved, "frac_of_hbm": achieved / peak},
+            "note": "each op timed alone, back to back on the same input rotation",
             "reward_to_go": {"us": rtg_ms * 1e3, "bytes": RTG_BYTES,
                              "gbs": RTG_BYTES / (rtg_ms * 1e-3) / 1e9,
                              "frac_of_hbm": RTG_BYTES / (rtg_ms * 1e-3) / 1e9 / peak},
@@ -322,10 +375,13 @@ def run_b200(args, world, rank, local):
                              "gbs": PPO_BYTES / (ppo_ms * 1e-3) / 1e9,
                              "frac_of_hbm": PPO_BYTES / (ppo_ms * 1e-3) / 1e9 / peak},
         },
-        "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+        "roofline": {"bound": "hbm", "kernel": "rl::step_kernel (reward_to_go + ppo_clip_ext, one launch)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "algorithmic_bytes": step_bytes,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6650 GB/s",
-                     "traffic": None},
+                     "traffic": profiled_traffic("rl_step"),
+                     "traffic_source": TRAFFIC_FILES["rl_step"]},
         "e2e": {"value": world * N_SAMPLES / (e2e_ms * 1e-3), "unit": "samples/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": per_step_launches * args.steps,
@@ -452,8 +508,17 @@ def run_profile(ops_list, reps):
     ops = pkg.ops
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if "rl_step" in ops_list:
+        s = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v)
+             for k, v in inputs.baseline_inputs("rl_pipeline", 0).items()}
+        out = torch.empty(B, T, device=dev)
+        po = torch.empty(7, device=dev)
+        for _ in range(reps):
+            ops.rl_step(s["reward"], s["done"], s["gamma"], s["current_log_prob"], s["old_log_prob"], s["advantage"],
+                        0.2, s["entropy"], rtg_out=out, ppo_out=po)
     if "rtg" in ops_list or "ppo" in ops_list:
-        s = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs.baseline_inputs("rl_pipeline", 0).items()}
+        s = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v)
+             for k, v in inputs.baseline_inputs("rl_pipeline", 0).items()}
         out = torch.empty(B, T, device=dev)
         po = torch.empty(7, device=dev)
         for _ in range(reps):
@@ -501,7 +566,7 @@ def main():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile", default=None,
-                    help="comma list of ops (rtg, ppo, lif, robust_l1, kan, fp8_m16, fp8_m1024, fp8_8192, fp8_16384, "
+                    help="comma list of ops (rl_step, rtg, ppo, lif, robust_l1, kan, fp8_m16, fp8_m1024, fp8_8192, fp8_16384, "
                          "fp8_ref_timed): run each --steps times for ncu, no timing")
     args = ap.parse_args()
     if args.profile:

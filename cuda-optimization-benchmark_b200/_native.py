@@ -42,6 +42,11 @@ SIGNATURES = {
     # reward-to-go
     "b200_reward_to_go": (None, [c_p, c_p, c_f, c_i32, c_i32, c_p]),
     "b200_reward_to_go_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p]),
+    # fused RL step (reward-to-go + PPO in one launch)
+    "b200_rl_step_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p, c_sz,
+                                   c_p]),
+    "b200_rl_step_shard_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p,
+                                         c_p]),
     # LIF
     "b200_leaky": (None, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p]),
     "b200_leaky_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_p]),

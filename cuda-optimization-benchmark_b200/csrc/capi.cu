@@ -13,6 +13,7 @@
 #include "dropin/pow_abs_sqrt_mean.cuh"
 #include "dropin/ppo_clip.cuh"
 #include "dropin/reward_to_go.cuh"
+#include "ops/rl_step.cuh"
 
 namespace {
 thread_local int g_last_status = 0;
@@ -106,6 +107,23 @@ void b200_reward_to_go(const float* reward, const bool* done, float gamma, int32
 int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
                             float* output, void* stream) {
   return b200::rtg::run(reward, done, gamma, B, T, output, as_stream(stream));
+}
+
+// ------------------------------------------------------------------------------ fused RL step
+int b200_rl_step_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T, float* rtg_out,
+                       const float* current_log_prob, const float* old_log_prob, const float* advantage,
+                       const float* entropy, int64_t n, float clip_epsilon, float* ppo_out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return b200::rl::run(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy, n,
+                       clip_epsilon, ppo_out, workspace, workspace_bytes, true, nullptr, as_stream(stream));
+}
+
+int b200_rl_step_shard_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                             float* rtg_out, const float* current_log_prob, const float* old_log_prob,
+                             const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
+                             void* partials, void* stream) {
+  return b200::rl::run(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy, n,
+                       clip_epsilon, nullptr, nullptr, 0, false, partials, as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------------------- LIF

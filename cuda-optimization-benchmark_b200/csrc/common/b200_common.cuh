@@ -186,6 +186,25 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 __device__ __forceinline__ unsigned warp_sum_u32(unsigned v) { return __reduce_add_sync(0xffffffffu, v); }
 
+// Completion counting by amounts: a CTA that completed `add` of `total` work items (after writing
+// their results) adds them to the counter once; returns true in the one CTA whose add reaches
+// `total`, which then sees every other CTA's writes and resets the counter to zero.
+__device__ __forceinline__ bool elect_last_add(unsigned* ticket, unsigned add, unsigned total) {
+  __shared__ bool s_last_add;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(ticket, add);
+    s_last_add = (prev + add == total);
+    if (s_last_add) {
+      __threadfence();
+      *reinterpret_cast<volatile unsigned*>(ticket) = 0u;
+    }
+  }
+  __syncthreads();
+  return s_last_add;
+}
+
 // Last-CTA election for single-launch grid reductions.  Every CTA calls this once after
 // writing its partial results; it returns true in exactly one CTA (the last to arrive), which
 // then sees every other CTA's writes.  The winner resets the counter to zero, so the counter

@@ -63,6 +63,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep (up to `hint_ns`) until the phase
+// completes instead of returning at once, so a waiting warp takes no issue slots from the warps
+// that have work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that sleeps between polls (see mbar_try_wait_sleep); for warps whose wait overlaps
+// other warps' work.  Returns false (and records kFaultWaitTimeout) after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) {
+  constexpr uint32_t kHintNs = 1000000u;  // 1 ms; the hardware wakes the thread when the phase completes
+  if (mbar_try_wait_sleep(bar, parity, kHintNs)) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, kHintNs)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&g_b200_fault, kFaultWaitTimeout);
+      return false;
+    }
+  }
+}
+
 // Wait until the barrier phase with the given parity has completed.  Returns false (and records
 // kFaultWaitTimeout) after kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {

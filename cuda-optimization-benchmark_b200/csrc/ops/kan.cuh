@@ -188,6 +188,61 @@ __device__ __forceinline__ void bases_fixed(float x, const float* __restrict__ g
   }
 }
 
+// Only the non-zero bases, for strictly increasing knots g[0..NK): if g[j0] <= x < g[j0+1], the
+// order-k bases that can be non-zero are j0-k .. j0, and each is formed by the same two-term
+// expression as in the full recurrence (the terms skipped are exact zeros), so the values equal
+// the full recurrence's.  out[0..NK-KO-1) receives every order-KO basis (zero outside j0-KO..j0).
+// Returns false (out untouched) when the knots are not strictly increasing.
+template <int NK, int KO>
+__device__ __forceinline__ bool bases_local(float x, const float* __restrict__ gsrc, float* out) {
+  constexpr int C = NK - KO - 1;
+  float g[NK];
+#pragma unroll
+  for (int j = 0; j < NK; ++j) g[j] = __ldg(gsrc + j);
+  bool inc = true;
+  int j0 = -1;
+#pragma unroll
+  for (int j = 0; j < NK - 1; ++j) {
+    inc = inc && (g[j] < g[j + 1]);
+    if (x >= g[j] && x < g[j + 1]) j0 = j;
+  }
+  if (!inc) return false;
+#pragma unroll
+  for (int c = 0; c < C; ++c) out[c] = 0.0f;
+  if (j0 < 0) return true;
+  float nb[KO + 1];  // nb[m]: basis j0-k+m of the current order k
+  nb[0] = 1.0f;
+#pragma unroll
+  for (int k = 1; k <= KO; ++k) {
+    float nn[KO + 1];
+#pragma unroll
+    for (int m = 0; m <= k; ++m) {
+      const int j = j0 - k + m;
+      float v = 0.0f;
+      if (j >= 0 && j <= NK - 2 - k) {
+        // b_k[j] = L * b_{k-1}[j] + R * b_{k-1}[j+1]; b_{k-1}[j] is nb[m-1], b_{k-1}[j+1] is nb[m].
+        const float lt = m >= 1 ? __fmul_rn(__fdiv_rn(__fsub_rn(x, g[j]), __fsub_rn(g[j + k], g[j])), nb[m - 1])
+                                : 0.0f;
+        const float rt = m <= k - 1 ? __fmul_rn(__fdiv_rn(__fsub_rn(g[j + k + 1], x), __fsub_rn(g[j + k + 1], g[j + 1])),
+                                                nb[m])
+                                    : 0.0f;
+        v = __fadd_rn(lt, rt);
+      }
+      nn[m] = v;
+    }
+#pragma unroll
+    for (int m = 0; m <= k; ++m) nb[m] = nn[m];
+  }
+#pragma unroll
+  for (int m = 0; m <= KO; ++m) {
+    const int j = j0 - KO + m;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+      if (c == j) out[c] = nb[m];
+  }
+  return true;
+}
+
 // One CTA per batch row b; the knots of input i are grid[i*nk .. i*nk + nk).  NK/KO > 0 select the
 // unrolled form for that (knot count, order); 0 selects the general loop.
 template <int NK, int KO>
@@ -211,7 +266,8 @@ __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x
     split_store(silu(xv) * f, hr + i, lr + i);
     if (NK > 0) {
       float b[NK > 0 ? NK : 1];
-      bases_fixed<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, b);
+      if (!bases_local<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, b))
+        bases_fixed<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, b);
 #pragma unroll
       for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c)
         split_store(b[c] * f, hr + int64_t(1 + c) * I + i, lr + int64_t(1 + c) * I + i);

@@ -17,16 +17,17 @@
 // ESS = exp(2 lse(lw) - lse(2 lw)) / N = (sum r)^2 / (sum r^2) / N.
 //
 // B200 design.  12 (16 with entropy) bytes per element.  The element range is cut into fixed
-// chunks of kChunk elements, each reduced by one CTA in a fixed order into a 48-byte partial
-// (fp32 per thread, fp64 above), and the last CTA to finish combines the partials in chunk order:
-// the result is bit-identical for any grid, any pointer alignment, and any chunk-aligned split of
-// the range across GPUs (the multi-GPU path gathers the same partials and runs the same finish).
-// Aligned inputs stream through a TMA bulk-copy pipeline: a producer warp keeps kStages chunks
-// (48-64 KB each) in flight into shared memory with cp.async.bulk while 8 consumer warps reduce
-// the resident chunk, so loads never wait for compute.  The clip decision matches the fp64
-// oracle exactly: it is taken in fp32 and re-taken in fp64 for elements within 1e-6 of a clip
-// boundary.  Elements with lw > 30 (outside the reference's stated input range, where r^2 could
-// overflow fp32 sums) take an fp64 path.
+// chunks of kChunk = 4096 samples, each reduced by one 256-thread CTA in a fixed order: each
+// thread streams 4 float4 of every input (one of each at a time, 64 registers, 4 CTAs per SM)
+// with 128-bit non-allocating loads, accumulates in fp32,
+// each warp folds its lanes into one fp32 record, and the 8 records are combined in fp64 into a
+// 48-byte chunk partial; the last CTA to finish combines the partials in chunk order.  The result
+// is bit-identical for any grid, any pointer alignment, and any chunk-aligned split of the range
+// across GPUs (the multi-GPU path gathers the same partials and runs the same finish), and the
+// fused reward-to-go + PPO step kernel reuses the same per-chunk routine.  The clip decision
+// matches the fp64 oracle exactly: it is taken in fp32 and re-taken in fp64 for elements within
+// a few ulps of a clip boundary (Clip::margin).  Elements with lw > 30 (outside the reference's stated input range,
+// where r^2 could overflow fp32 sums) take an fp64 path.
 #pragma once
 
 #include <math.h>
@@ -38,22 +39,12 @@
 namespace b200 {
 namespace ppo {
 
-constexpr int kThreads = 512;                                       // consumer threads
-constexpr int kVecPerThread = 2;                                    // float4 per input per thread
+constexpr int kThreads = 256;                                       // threads per chunk
+constexpr int kVecPerThread = 4;                                    // float4 per input per thread
 constexpr int64_t kChunk = int64_t(kThreads) * kVecPerThread * 4;  // 4096 elements per chunk
-constexpr int kPipeThreads = kThreads + 64;                         // + producer and reducer warps
-constexpr uint32_t kRedBar = 1;                                     // named barrier of the consumers
+constexpr uint32_t kRedBar = 1;                                     // named barrier of a chunk's threads
 constexpr int kOutputs = 6;
 constexpr int kOutputsExt = 7;
-
-template <bool kEnt>
-struct Pipe {
-  static constexpr int kArrays = kEnt ? 4 : 3;
-  static constexpr int kArrayBytes = int(kChunk) * 4;
-  static constexpr int kStageBytes = kArrays * kArrayBytes;
-  static constexpr int kStages = kEnt ? 3 : 4;
-  static constexpr int kSmem = kStages * kStageBytes;
-};
 
 struct __align__(16) Partial {
   double gain, lw, r, r2, ent;
@@ -67,6 +58,7 @@ struct Clip {
   double lo_d, hi_d;   // log1p(-eps), log1p(eps)
   float mid, hw;       // centre and half-width of [lo, hi] in fp32 (fast decision)
   float down, up;      // exp(log1p(-eps)), exp(log1p(eps)) rounded to fp32
+  float margin;        // |adm - hw| below which the fp32 decision may differ from the fp64 one
 };
 
 inline Clip make_clip(float eps) {
@@ -78,10 +70,16 @@ inline Clip make_clip(float eps) {
   c.hw = float(0.5 * (c.hi_d - c.lo_d));
   c.down = float(exp(c.lo_d));
   c.up = float(exp(c.hi_d));
+  // The fp32 test |fl(lw - mid)| > hw can disagree with the exact lw < lo or lw > hi only when
+  // |lw - mid| is within the roundings of mid, hw and lw - mid of hw (lw itself is exact, or off by
+  // at most half an ulp of |lw|, near a bound): a few ulps of hw + |mid|.  Eight ulps leave room;
+  // samples inside the margin take the fp64 decision.
+  const float span = c.hw + fabsf(c.mid);
+  c.margin = 8.0f * (nextafterf(span, INFINITY) - span);
   return c;
 }
 
-inline int64_t num_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
+__host__ __device__ inline int64_t num_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
 inline size_t workspace_bytes(int64_t n) { return 256 + align256(size_t(num_chunks(n)) * sizeof(Partial)); }
 
 struct Acc {
@@ -90,7 +88,7 @@ struct Acc {
   double big_gain = 0.0, big_lw = 0.0, big_r = 0.0, big_r2 = 0.0;  // lw > 30 only
 };
 
-// Rare elements (within 1e-6 of a clip boundary, or lw > 30) leave the fast path: the clip
+// Rare elements (within Clip::margin of a clip boundary, or lw > 30) leave the fast path: the clip
 // decision is re-taken in fp64 and, for lw > 30, the element is accumulated in fp64.
 __device__ __forceinline__ void add_element_slow(Acc& acc, float cur, float old, float adv, const Clip& c) {
   const double lwd = double(cur) - double(old);
@@ -121,7 +119,7 @@ __device__ __forceinline__ void add_element(Acc& acc, float cur, float old, floa
   const float lw = __fsub_rn(cur, old);
   const float dm = __fsub_rn(lw, c.mid);
   const float adm = fabsf(dm);
-  if (fabsf(__fsub_rn(adm, c.hw)) < 1e-6f || lw > 30.0f) {
+  if (fabsf(__fsub_rn(adm, c.hw)) < c.margin || lw > 30.0f) {
     add_element_slow(acc, cur, old, adv, c);
     return;
   }
@@ -150,8 +148,46 @@ __device__ __forceinline__ void add4(Acc& acc, float4 c4, float4 o4, float4 a4, 
   }
 }
 
+// Fast form of add_element: no rare-case branch.  It tracks what the rare cases test (the smallest
+// |adm - hw| and the largest lw); when the tracked values show that some sample needed
+// add_element_slow, the caller discards the accumulator and recomputes the same samples with
+// add_element.  Otherwise every operation and its order equals add_element's, so the result has
+// the same bits either way.
+__device__ __forceinline__ void add_fast(Acc& acc, float cur, float old, float adv, const Clip& c, float& near,
+                                         float& lw_max) {
+  const float lw = __fsub_rn(cur, old);
+  const float dm = __fsub_rn(lw, c.mid);
+  const float adm = fabsf(dm);
+  near = fminf(near, fabsf(__fsub_rn(adm, c.hw)));
+  lw_max = fmaxf(lw_max, lw);
+  const bool clipped = adm > c.hw;
+  acc.clipped += clipped ? 1u : 0u;
+  const float r = __expf(lw);
+  const float rc = clipped ? (dm < 0.0f ? c.down : c.up) : r;
+  acc.gain = __fadd_rn(acc.gain, fminf(__fmul_rn(r, adv), __fmul_rn(rc, adv)));
+  acc.lw = __fadd_rn(acc.lw, lw);
+  acc.r = __fadd_rn(acc.r, r);
+  acc.r2 = __fmaf_rn(r, r, acc.r2);
+  acc.rmax = fmaxf(acc.rmax, r);
+}
+
+template <bool kEnt>
+__device__ __forceinline__ void add4_fast(Acc& acc, float4 c4, float4 o4, float4 a4, float4 e4, const Clip& c,
+                                          float& near, float& lw_max) {
+  add_fast(acc, c4.x, o4.x, a4.x, c, near, lw_max);
+  add_fast(acc, c4.y, o4.y, a4.y, c, near, lw_max);
+  add_fast(acc, c4.z, o4.z, a4.z, c, near, lw_max);
+  add_fast(acc, c4.w, o4.w, a4.w, c, near, lw_max);
+  if (kEnt) {
+    acc.ent = __fadd_rn(acc.ent, e4.x);
+    acc.ent = __fadd_rn(acc.ent, e4.y);
+    acc.ent = __fadd_rn(acc.ent, e4.z);
+    acc.ent = __fadd_rn(acc.ent, e4.w);
+  }
+}
+
 // Per-thread pass over elements (k*kThreads + t)*4 + j of one chunk straight from global memory
-// (k outer, j inner: the same order as the pipelined path), skipping elements past n.
+// (k outer, j inner), skipping elements past n; the vector and scalar forms give the same bits.
 template <bool kVec, bool kEnt>
 __device__ __forceinline__ void thread_chunk_global(Acc& acc, const float* __restrict__ cur,
                                                     const float* __restrict__ old, const float* __restrict__ adv,
@@ -159,17 +195,26 @@ __device__ __forceinline__ void thread_chunk_global(Acc& acc, const float* __res
                                                     const Clip& c) {
   const int t = threadIdx.x;
   if (kVec && base + kChunk <= n) {
-    float4 vc[kVecPerThread], vo[kVecPerThread], va[kVecPerThread], ve[kVecPerThread];
+    // One float4 of each stream at a time: few live registers, so more CTAs share an SM.
+    float near = __int_as_float(0x7f800000), lw_max = -__int_as_float(0x7f800000);
 #pragma unroll
     for (int k = 0; k < kVecPerThread; ++k) {
       const int64_t i = base + int64_t(k * kThreads + t) * 4;
-      vc[k] = ld_stream_f4(cur + i);
-      vo[k] = ld_stream_f4(old + i);
-      va[k] = ld_stream_f4(adv + i);
-      ve[k] = kEnt ? ld_stream_f4(ent + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 vc = ld_stream_f4(cur + i);
+      const float4 vo = ld_stream_f4(old + i);
+      const float4 va = ld_stream_f4(adv + i);
+      const float4 ve = kEnt ? ld_stream_f4(ent + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      add4_fast<kEnt>(acc, vc, vo, va, ve, c, near, lw_max);
     }
-#pragma unroll
-    for (int k = 0; k < kVecPerThread; ++k) add4<kEnt>(acc, vc[k], vo[k], va[k], ve[k], c);
+    if (near < c.margin || lw_max > 30.0f) {  // rare: some sample needs add_element_slow
+      acc = Acc();
+#pragma unroll 1
+      for (int k = 0; k < kVecPerThread; ++k) {
+        const int64_t i = base + int64_t(k * kThreads + t) * 4;
+        const float4 ve = kEnt ? ld_stream_f4(ent + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        add4<kEnt>(acc, ld_stream_f4(cur + i), ld_stream_f4(old + i), ld_stream_f4(adv + i), ve, c);
+      }
+    }
   } else {
 #pragma unroll 1
     for (int k = 0; k < kVecPerThread; ++k) {
@@ -186,96 +231,104 @@ __device__ __forceinline__ void thread_chunk_global(Acc& acc, const float* __res
   }
 }
 
-// Warp-level record of one chunk (fp32 sums of the warp's 256 samples; the fp64 sums of the rare
-// lw > 30 samples).  The reducer warp combines a chunk's 16 records in a fixed order.
-struct WarpPart {
-  float gain, lw, r, r2, ent, rmax;
-  unsigned clipped, pad;
-  double big_gain, big_lw, big_r, big_r2;
+constexpr int kConsumerWarps = kThreads / 32;   // 8
+
+// bar.red.or over the `count` threads of named barrier `id`: a barrier that also returns whether
+// any arriving thread passed true.
+__device__ __forceinline__ bool named_sync_or(uint32_t id, uint32_t count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "barrier.red.or.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
+// Shared scratch of one 256-thread reduction group.
+struct RedScratch {
+  float v[5][kThreads];  // per-thread gain, lw, r, r2, ent
+  float m[kThreads];     // per-thread max ratio
+  unsigned c[kThreads];  // per-thread clip count
+  double sum[5];
+  double big[kConsumerWarps][4];
+  float mx;
+  unsigned cnt;
 };
-constexpr int kSlots = 4;                       // chunks in flight between consumers and reducer
-constexpr int kConsumerWarps = kThreads / 32;   // 16
 
-__device__ __forceinline__ void warp_record(const Acc& acc, WarpPart* slot, int lane) {
-  float v[5] = {acc.gain, acc.lw, acc.r, acc.r2, acc.ent};
+// Chunk partial of a group's 256 accumulators (tid = thread index in the group, `bar` its named
+// barrier), valid in tid 0.  Each thread parks its fp32 sums in shared memory; warp q < 5 then
+// adds quantity q over the 256 threads in fp64 (lane l takes threads l, l+32, ..., l+224 in that
+// order, then a fixed butterfly), warp 5 takes the max and warp 6 the count.  The fp64 sums of the
+// rare lw > 30 samples are added per warp, then over warps in order, only when a thread has some.
+// Every path (one launch, fused step, multi-GPU shards) reduces a chunk through this routine, so all
+// give the same bits.
+__device__ __forceinline__ Partial group_reduce(const Acc& acc, RedScratch& s, int tid, uint32_t bar) {
+  s.v[0][tid] = acc.gain;
+  s.v[1][tid] = acc.lw;
+  s.v[2][tid] = acc.r;
+  s.v[3][tid] = acc.r2;
+  s.v[4][tid] = acc.ent;
+  s.m[tid] = acc.rmax;
+  s.c[tid] = acc.clipped;
+  const bool any_big = named_sync_or(bar, kThreads, acc.big_r != 0.0);
+  const int w = tid >> 5, lane = tid & 31;
+  if (w < 5) {
+    double x = 0.0;
 #pragma unroll
-  for (int q = 0; q < 5; ++q)
+    for (int j = 0; j < kConsumerWarps; ++j) x += double(s.v[w][lane + 32 * j]);
+    x = warp_sum(x);
+    if (lane == 0) s.sum[w] = x;
+  } else if (w == 5) {
+    float x = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v[q] += __shfl_xor_sync(0xffffffffu, v[q], o);
-  const float m = warp_max(acc.rmax);
-  const unsigned cnt = warp_sum_u32(acc.clipped);
-  const bool any_big = __any_sync(0xffffffffu, acc.big_r != 0.0);
-  double bg = acc.big_gain, bl = acc.big_lw, br = acc.big_r, br2 = acc.big_r2;
+    for (int j = 0; j < kConsumerWarps; ++j) x = fmaxf(x, s.m[lane + 32 * j]);
+    x = warp_max(x);
+    if (lane == 0) s.mx = x;
+  } else if (w == 6) {
+    unsigned x = 0;
+#pragma unroll
+    for (int j = 0; j < kConsumerWarps; ++j) x += s.c[lane + 32 * j];
+    x = warp_sum_u32(x);
+    if (lane == 0) s.cnt = x;
+  }
   if (any_big) {
-    bg = warp_sum(bg);
-    bl = warp_sum(bl);
-    br = warp_sum(br);
-    br2 = warp_sum(br2);
+    const double b0 = warp_sum(acc.big_gain), b1 = warp_sum(acc.big_lw);
+    const double b2 = warp_sum(acc.big_r), b3 = warp_sum(acc.big_r2);
+    if (lane == 0) {
+      s.big[w][0] = b0;
+      s.big[w][1] = b1;
+      s.big[w][2] = b2;
+      s.big[w][3] = b3;
+    }
   }
-  if (lane == 0) {
-    WarpPart w;
-    w.gain = v[0];
-    w.lw = v[1];
-    w.r = v[2];
-    w.r2 = v[3];
-    w.ent = v[4];
-    w.rmax = m;
-    w.clipped = cnt;
-    w.pad = 0;
-    w.big_gain = any_big ? bg : 0.0;
-    w.big_lw = any_big ? bl : 0.0;
-    w.big_r = any_big ? br : 0.0;
-    w.big_r2 = any_big ? br2 : 0.0;
-    *slot = w;
-  }
-}
-
-// Combine a chunk's kConsumerWarps warp records (lane w holds record w) into the chunk partial,
-// valid in lane 0: fp64, fixed butterfly order.  Shared by every path, so all give the same bits.
-__device__ __forceinline__ Partial combine_records(const WarpPart* recs, int lane) {
-  double v[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
-  float m = 0.f;
-  unsigned cnt = 0;
-  if (lane < kConsumerWarps) {
-    const WarpPart& w = recs[lane];
-    v[0] = double(w.gain);
-    v[1] = double(w.lw);
-    v[2] = double(w.r);
-    v[3] = double(w.r2);
-    v[4] = double(w.ent);
-    v[5] = w.big_gain;
-    v[6] = w.big_lw;
-    v[7] = w.big_r;
-    v[8] = w.big_r2;
-    m = w.rmax;
-    cnt = w.clipped;
-  }
-#pragma unroll
-  for (int q = 0; q < 9; ++q) v[q] = warp_sum(v[q]);
-  m = warp_max(m);
-  cnt = warp_sum_u32(cnt);
-  Partial p;
-  p.gain = v[0] + v[5];
-  p.lw = v[1] + v[6];
-  p.r = v[2] + v[7];
-  p.r2 = v[3] + v[8];
-  p.ent = v[4];
-  p.rmax = m;
-  p.clipped = cnt;
-  return p;
-}
-
-// Chunk partial of the kThreads consumer threads' accumulators (valid in thread 0), through the
-// same warp records and combine as the pipelined path.  Uses a named barrier over the consumers.
-__device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
-  __shared__ WarpPart s_rec[kConsumerWarps];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  warp_record(acc, &s_rec[warp], lane);
-  named_sync(kRedBar, kThreads);
+  named_sync(bar, kThreads);
   Partial p{};
-  if (warp == 0) p = combine_records(s_rec, lane);
-  named_sync(kRedBar, kThreads);
+  if (tid == 0) {
+    double bg[4] = {0.0, 0.0, 0.0, 0.0};
+    if (any_big) {
+      for (int i = 0; i < kConsumerWarps; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) bg[q] += s.big[i][q];
+    }
+    p.gain = s.sum[0] + bg[0];
+    p.lw = s.sum[1] + bg[1];
+    p.r = s.sum[2] + bg[2];
+    p.r2 = s.sum[3] + bg[3];
+    p.ent = s.sum[4];
+    p.rmax = s.mx;
+    p.clipped = s.cnt;
+  }
   return p;
+}
+
+// group_reduce over the kThreads threads of a chunk CTA (named barrier kRedBar).
+__device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
+  __shared__ RedScratch s_red;
+  return group_reduce(acc, s_red, threadIdx.x, kRedBar);
 }
 
 // Final combination of partials[0..n_parts) in a fixed order by the kThreads consumer threads;
@@ -287,12 +340,26 @@ __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, in
   double v[5] = {0, 0, 0, 0, 0};
   float m = 0.f;
   unsigned long long cnt = 0;
-  for (int64_t i = threadIdx.x; i < n_parts; i += kThreads) {
-    const double* pd = reinterpret_cast<const double*>(parts + i);
+  // Four partials per thread per round, loads issued before the adds (one L2 round trip a round).
+  for (int64_t i0 = threadIdx.x; i0 < n_parts; i0 += 4 * kThreads) {
+    double d[4][6];
 #pragma unroll
-    for (int q = 0; q < 5; ++q) v[q] += ld_cg_f64(pd + q);
-    m = fmaxf(m, ld_cg_f32(reinterpret_cast<const float*>(pd + 5)));
-    cnt += ld_cg_u32(reinterpret_cast<const unsigned*>(pd + 5) + 1);
+    for (int u = 0; u < 4; ++u) {
+      const int64_t i = i0 + int64_t(u) * kThreads;
+      const double* pd = reinterpret_cast<const double*>(parts + (i < n_parts ? i : 0));
+#pragma unroll
+      for (int q = 0; q < 6; ++q) d[u][q] = i < n_parts ? ld_cg_f64(pd + q) : 0.0;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (i0 + int64_t(u) * kThreads < n_parts) {
+#pragma unroll
+        for (int q = 0; q < 5; ++q) v[q] += d[u][q];
+        const unsigned long long w = __double_as_longlong(d[u][5]);
+        m = fmaxf(m, __uint_as_float(unsigned(w & 0xffffffffull)));
+        cnt += unsigned(w >> 32);
+      }
+    }
   }
 #pragma unroll
   for (int q = 0; q < 5; ++q) v[q] = warp_sum(v[q]);
@@ -328,124 +395,31 @@ __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, in
   }
 }
 
-// Direct form (unaligned inputs): CTA c handles chunks c, c + gridDim.x, ... from global memory.
-template <bool kVec, bool kEnt, bool kFinish>
-__global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict__ cur, const float* __restrict__ old,
-                                                         const float* __restrict__ adv, const float* __restrict__ ent,
-                                                         int64_t n, Clip clip, Partial* __restrict__ partials,
-                                                         unsigned* __restrict__ ticket, float* __restrict__ out) {
+// Chunk partials of chunks cta, cta + n_ctas, ... (all kThreads threads of the CTA take part).
+template <bool kVec, bool kEnt>
+__device__ __forceinline__ void chunk_partials(const float* __restrict__ cur, const float* __restrict__ old,
+                                               const float* __restrict__ adv, const float* __restrict__ ent, int64_t n,
+                                               const Clip& clip, Partial* __restrict__ partials, int64_t cta,
+                                               int64_t n_ctas) {
   const int64_t n_chunks = (n + kChunk - 1) / kChunk;
-  for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+  for (int64_t c = cta; c < n_chunks; c += n_ctas) {
     Acc acc;
     thread_chunk_global<kVec, kEnt>(acc, cur, old, adv, ent, c * kChunk, n, clip);
     const Partial p = cta_reduce(acc);
     if (threadIdx.x == 0) partials[c] = p;
   }
-  if (kFinish) {
-    if (elect_last_cta(ticket)) finish(partials, n_chunks, n, kEnt, out);
-  }
 }
 
-// Pipelined form (16-byte aligned inputs).  Warps 0-15 consume, warp 16 produces (bulk-copy ring),
-// warp 17 reduces (16 warp records -> one chunk partial, fixed order, fp64).  A trailing partial
-// chunk is read from global memory by the consumers of the CTA that owns it, in the same element
-// order, and reduced the same way.  No CTA-wide barrier inside the loop.
-template <bool kEnt, bool kFinish>
-__global__ void __launch_bounds__(kPipeThreads, 1)
-    pipe_kernel(const float* __restrict__ cur, const float* __restrict__ old, const float* __restrict__ adv,
-                const float* __restrict__ ent, int64_t n, Clip clip, Partial* __restrict__ partials,
-                unsigned* __restrict__ ticket, float* __restrict__ out) {
-  using P = Pipe<kEnt>;
-  extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t full[P::kStages], empty[P::kStages], rec_full[kSlots], rec_free[kSlots];
-  __shared__ WarpPart recs[kSlots][kConsumerWarps];
-  const int64_t n_chunks = (n + kChunk - 1) / kChunk;
-  const int64_t n_full = n / kChunk;
-  const bool own_tail = n_full < n_chunks && (n_chunks - 1) % gridDim.x == blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < P::kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    for (int s = 0; s < kSlots; ++s) {
-      mbar_init(&rec_full[s], kConsumerWarps);
-      mbar_init(&rec_free[s], 1);
-    }
-    fence_barrier_init();
-  }
-  __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    // Producer: one lane keeps the ring full.
-    if (lane == 0) {
-      const float* src[4] = {cur, old, adv, ent};
-      uint32_t i = 0;
-      for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x, ++i) {
-        const uint32_t s = i % P::kStages, ph = (i / P::kStages) & 1u;
-        mbar_wait(&empty[s], ph ^ 1u);
-        mbar_arrive_expect_tx(&full[s], P::kStageBytes);
-        unsigned char* dst = smem + s * P::kStageBytes;
-#pragma unroll
-        for (int a = 0; a < P::kArrays; ++a)
-          bulk_g2s(dst + a * P::kArrayBytes, src[a] + c * kChunk, P::kArrayBytes, &full[s]);
-      }
-    }
-  } else if (warp == kConsumerWarps + 1) {
-    // Reducer: chunk i's 16 warp records, lane w holds record w; fixed-order fp64 tree.
-    uint32_t i = 0;
-    auto reduce_chunk = [&](int64_t c) {
-      const uint32_t s = i % kSlots, ph = (i / kSlots) & 1u;
-      mbar_wait(&rec_full[s], ph);
-      const Partial p = combine_records(recs[s], lane);
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&rec_free[s]);
-        partials[c] = p;
-      }
-      ++i;
-    };
-    for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x) reduce_chunk(c);
-    if (own_tail) reduce_chunk(n_chunks - 1);
-  } else {
-    uint32_t i = 0;
-    auto record = [&](const Acc& acc) {
-      const uint32_t s = i % kSlots, ph = (i / kSlots) & 1u;
-      mbar_wait(&rec_free[s], ph ^ 1u);
-      warp_record(acc, &recs[s][warp], lane);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rec_full[s]);
-      ++i;
-    };
-    uint32_t k = 0;
-    for (int64_t c = blockIdx.x; c < n_full; c += gridDim.x, ++k) {
-      const uint32_t s = k % P::kStages, ph = (k / P::kStages) & 1u;
-      mbar_wait(&full[s], ph);
-      const float* st = reinterpret_cast<const float*>(smem + s * P::kStageBytes);
-      Acc acc;
-#pragma unroll
-      for (int kk = 0; kk < kVecPerThread; ++kk) {
-        const int e = (kk * kThreads + threadIdx.x) * 4;
-        const float4 c4 = *reinterpret_cast<const float4*>(st + e);
-        const float4 o4 = *reinterpret_cast<const float4*>(st + kChunk + e);
-        const float4 a4 = *reinterpret_cast<const float4*>(st + 2 * kChunk + e);
-        const float4 e4 =
-            kEnt ? *reinterpret_cast<const float4*>(st + 3 * kChunk + e) : make_float4(0.f, 0.f, 0.f, 0.f);
-        add4<kEnt>(acc, c4, o4, a4, e4, clip);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      record(acc);
-    }
-    if (own_tail) {
-      Acc acc;
-      thread_chunk_global<true, kEnt>(acc, cur, old, adv, ent, (n_chunks - 1) * kChunk, n, clip);
-      record(acc);
-    }
-  }
+// One launch: CTA c handles chunks c, c + gridDim.x, ...; with kFinish the last CTA to finish
+// combines every partial.  kVec: 128-bit loads for full chunks (16-byte aligned inputs).
+template <bool kVec, bool kEnt, bool kFinish>
+__global__ void __launch_bounds__(kThreads, 4) chunk_kernel(const float* __restrict__ cur, const float* __restrict__ old,
+                                                         const float* __restrict__ adv, const float* __restrict__ ent,
+                                                         int64_t n, Clip clip, Partial* __restrict__ partials,
+                                                         unsigned* __restrict__ ticket, float* __restrict__ out) {
+  chunk_partials<kVec, kEnt>(cur, old, adv, ent, n, clip, partials, blockIdx.x, gridDim.x);
   if (kFinish) {
-    const bool last = elect_last_cta(ticket);
-    if (last && threadIdx.x < kThreads) finish(partials, n_chunks, n, kEnt, out);
+    if (elect_last_cta(ticket)) finish(partials, (n + kChunk - 1) / kChunk, n, kEnt, out);
   }
 }
 
@@ -454,19 +428,10 @@ __global__ void __launch_bounds__(kThreads) finish_kernel(const Partial* __restr
   finish(partials, n_parts, n_total, ext != 0, out);
 }
 
-template <bool kEnt, bool kFinish>
-inline void launch_pipe(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
-                        const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
-  auto kern = pipe_kernel<kEnt, kFinish>;
-  ensure_dyn_smem(kern, Pipe<kEnt>::kSmem);
-  const int grid = balanced_grid(num_chunks(n), 1);
-  kern<<<grid, kPipeThreads, Pipe<kEnt>::kSmem, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, out);
-}
-
-template <bool kEnt, bool kFinish>
+template <bool kVec, bool kEnt, bool kFinish>
 inline void launch_direct(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
                           const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
-  auto kern = chunk_kernel<false, kEnt, kFinish>;
+  auto kern = chunk_kernel<kVec, kEnt, kFinish>;
   const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
   kern<<<grid, kThreads, 0, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, out);
 }
@@ -476,11 +441,11 @@ inline void launch_chunks(const float* cur, const float* old, const float* adv, 
                           const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
   const bool vec = aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
   if (ent != nullptr) {
-    if (vec) launch_pipe<true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-    else launch_direct<true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    if (vec) launch_direct<true, true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    else launch_direct<false, true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
   } else {
-    if (vec) launch_pipe<false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-    else launch_direct<false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    if (vec) launch_direct<true, false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
+    else launch_direct<false, false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
   }
 }
 

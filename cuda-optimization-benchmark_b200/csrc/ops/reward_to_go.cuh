@@ -10,15 +10,19 @@
 //
 // B200 design.  The recurrence is an affine map per step, y -> r[t] + a[t] * y with
 // a[t] = done[t] ? 0 : gamma, so a run of steps composes to y -> B + A * y.  One warp owns one row
-// at a time and walks it from the end in passes of kSeg = 32 * kLane elements:
+// at a time and walks it from the end in passes of at most kSeg = 32 * kLane elements:
 //   1. lane 0 moves the 16-byte aligned interior of the pass's rewards and done bytes into
-//      shared memory with one cp.async.bulk each (counted on the warp's mbarrier); the lanes
-//      load the ragged ends (the shared copy keeps the global 16-byte phase);
-//   2. lane l composes its contiguous run of kLane steps in fp64 (kLane is odd, so the 32 lanes'
-//      strided shared reads fall in 32 distinct banks);
-//   3. a 5-step warp suffix scan of the lanes' (A, B) maps, in fp64, gives every lane the exact
+//      shared memory with one cp.async.bulk each (counted on the warp's mbarrier, waited on with a
+//      sleeping try_wait so a waiting warp takes no issue slots); the lanes load the ragged ends;
+//   2. the pass is laid out right-aligned on a grid of 32 runs of kLane slots: lane l owns slots
+//      [l*kLane, (l+1)*kLane), and a pass shorter than kSeg leaves its unused slots at the front.
+//      Values flow only from later to earlier steps, so those slots (whatever they hold) reach no
+//      valid output, and every lane runs exactly kLane steps with no per-step bounds checks;
+//   3. lane l composes its run in fp64 (kLane is odd, so the 32 lanes' strided shared reads fall
+//      in 32 distinct banks); A is gamma^kLane, or 0 when the run holds a done flag;
+//   4. a 5-step warp suffix scan of the lanes' (A, B) maps, in fp64, gives every lane the exact
 //      value entering its run;
-//   4. lane l re-runs its steps from that value in fp32 (at most kLane roundings per output, no
+//   5. lane l re-runs its steps from that value in fp32 (at most kLane roundings per output, no
 //      error carried between runs) and writes the outputs over the rewards in shared memory,
 //      and the warp streams them out with 128-bit stores.
 // One warp per row and 40 warps per SM put every row of the BASELINE batch in flight at once.
@@ -34,11 +38,14 @@ constexpr int kLane = 33;                    // steps per lane per pass (odd: co
 constexpr int kSeg = 32 * kLane;             // steps per warp pass
 constexpr int kWarps = 4;                    // warps (rows in flight) per CTA
 constexpr int kThreads = 32 * kWarps;
-// Per-warp shared memory: kSeg floats (+16 B phase slack) and kSeg done bytes (+16 B slack).
-constexpr int kRewardBytes = ((kSeg * 4 + 16) + 15) / 16 * 16;
-constexpr int kDoneBytes = ((kSeg + 16 + 16) + 15) / 16 * 16;  // + 16: done_mask reads 40-byte windows
+// Per-warp staging buffer: the lane grid of kSeg floats starts at float 0..3 (so the copy keeps the
+// rows' 16-byte phase), the done grid at byte 0..15, and done_mask reads up to 40 bytes past the
+// start of a lane's 33-byte window.
+constexpr int kRewardBytes = (kSeg + 4) * 4;
+constexpr int kDoneBytes = ((kSeg + 16 + 40) + 15) / 16 * 16;
 constexpr int kWarpSmem = kRewardBytes + kDoneBytes;
 constexpr int kSmemPerBuffer = kWarps * kWarpSmem;  // one staging buffer per warp
+static_assert(kRewardBytes % 16 == 0 && kWarpSmem % 16 == 0, "staging buffers stay 16-byte aligned");
 
 // Write sfrom[phase .. phase+len) to dst[0..len).  When dst has the same 16-byte phase as the
 // staged data, full groups go out as 128-bit streaming stores; otherwise lane-strided scalars.
@@ -67,20 +74,22 @@ __device__ __forceinline__ void drain_floats(float* __restrict__ dst, int len, c
   }
 }
 
-// Bit e (e < cnt) set when byte sd[at + e] is non-zero.  Reads the ten aligned 32-bit words that
-// cover [at, at + 40) and folds each word's four "byte is non-zero" bits into a nibble.
-__device__ __forceinline__ unsigned long long done_mask(const unsigned char* sd, int at, int cnt) {
+// Bit e (e < kLane) set when byte sd[at + e] is non-zero.  Reads the ten aligned 32-bit words that
+// cover [at, at + 40) and folds each word's four "byte is non-zero" bits into a nibble: 0x80 marks
+// every non-zero byte, and one multiply gathers the four marks into the top nibble.
+__device__ __forceinline__ unsigned long long done_mask(const unsigned char* sd, int at) {
   const uint32_t* w = reinterpret_cast<const uint32_t*>(sd) + (at >> 2);
-  unsigned long long m = 0;
+  uint32_t lo = 0, hi = 0;
 #pragma unroll
   for (int i = 0; i < 10; ++i) {
     const uint32_t v = w[i];
-    const uint32_t hi = (((v & 0x7f7f7f7fu) + 0x7f7f7f7fu) | v) & 0x80808080u;  // 0x80 per non-zero byte
-    const uint32_t nib = (hi >> 7 | hi >> 14 | hi >> 21 | hi >> 28) & 0xfu;      // bytes 0..3 -> bits 0..3
-    m |= (unsigned long long)nib << (4 * i);
+    const uint32_t marks = (((v & 0x7f7f7f7fu) + 0x7f7f7f7fu) | v) & 0x80808080u;  // bit 7 of each byte
+    const uint32_t nib = (marks * 0x00204081u) >> 28;                              // bytes 0..3 -> bits 0..3
+    if (i < 8) lo |= nib << (4 * i);
+    else hi |= nib << (4 * (i - 8));
   }
-  m >>= (at & 3);
-  return cnt >= 64 ? m : (m & ((1ull << cnt) - 1ull));
+  const unsigned long long m = ((unsigned long long)hi << 32 | lo) >> (at & 3);
+  return m & ((1ull << kLane) - 1ull);
 }
 
 // Ragged-edge values a lane loaded for a prefetched pass; written to shared memory when the
@@ -90,11 +99,14 @@ struct Edges {
   uint32_t dh, dt;
 };
 
-// Geometry of the pass [t0, t0 + len) of one row: 16-byte phases and aligned interiors.
+// Geometry of the pass [t0, t0 + len) of one row (1 <= len <= kSeg).  Element i sits at float
+// sr + i of the reward buffer and byte sd + i of the done buffer; the lane grid starts gr floats
+// and gd bytes into them (sr = gr + kSeg - len).  gr and gd are chosen so that the aligned
+// interiors [ear, ebr) and [ead, ebd) land on 16-byte boundaries, as cp.async.bulk requires.
 struct Pass {
   const float* rs;
   const unsigned char* ds;
-  int len, pr, pd, ear, ebr, ead, ebd;
+  int len, pr, gr, gd, sr, sd, ear, ebr, ead, ebd;
 };
 
 __device__ __forceinline__ Pass make_pass(const float* rrow, const unsigned char* drow, int t0, int len) {
@@ -102,11 +114,16 @@ __device__ __forceinline__ Pass make_pass(const float* rrow, const unsigned char
   p.rs = rrow + t0;
   p.ds = drow + t0;
   p.len = len;
+  const int pad = kSeg - len;
   p.pr = int((reinterpret_cast<uintptr_t>(p.rs) >> 2) & 3);
-  p.pd = int(reinterpret_cast<uintptr_t>(p.ds) & 15);
+  const int pd = int(reinterpret_cast<uintptr_t>(p.ds) & 15);
+  p.gr = (p.pr - pad) & 3;
+  p.gd = (pd - pad) & 15;
+  p.sr = p.gr + pad;
+  p.sd = p.gd + pad;
   p.ear = (4 - p.pr) & 3;
   p.ebr = len > p.ear ? p.ear + ((len - p.ear) & ~3) : p.ear;
-  p.ead = (16 - p.pd) & 15;
+  p.ead = (16 - pd) & 15;
   p.ebd = len > p.ead ? p.ead + ((len - p.ead) & ~15) : p.ead;
   return p;
 }
@@ -126,8 +143,8 @@ __device__ __forceinline__ Edges issue_pass(const Pass& p, float* s_r, unsigned 
   const uint32_t db = uint32_t(p.ebd - p.ead) * (p.len > p.ead);
   if (lane == 0) {
     mbar_arrive_expect_tx(bar, rb + db);
-    if (rb) bulk_g2s(s_r + p.pr + p.ear, p.rs + p.ear, rb, bar);
-    if (db) bulk_g2s(s_d + p.pd + p.ead, p.ds + p.ead, db, bar);
+    if (rb) bulk_g2s(s_r + p.sr + p.ear, p.rs + p.ear, rb, bar);
+    if (db) bulk_g2s(s_d + p.sd + p.ead, p.ds + p.ead, db, bar);
   }
   Edges e{0.f, 0.f, 0u, 0u};
   const int hr = min(p.len, p.ear), tr = p.len - p.ebr;
@@ -144,41 +161,43 @@ __device__ __forceinline__ void land_pass(const Pass& p, const Edges& e, float* 
                                           uint64_t* bar, uint32_t parity, int lane) {
   const int hr = min(p.len, p.ear), tr = p.len - p.ebr;
   const int hd = min(p.len, p.ead), td = p.len - p.ebd;
-  if (lane < hr) s_r[p.pr + lane] = e.rh;
-  if (lane < tr) s_r[p.pr + p.ebr + lane] = e.rt;
-  if (lane < hd) s_d[p.pd + lane] = (unsigned char)e.dh;
-  if (lane < td) s_d[p.pd + p.ebd + lane] = (unsigned char)e.dt;
-  mbar_wait(bar, parity);
+  if (lane < hr) s_r[p.sr + lane] = e.rh;
+  if (lane < tr) s_r[p.sr + p.ebr + lane] = e.rt;
+  if (lane < hd) s_d[p.sd + lane] = (unsigned char)e.dh;
+  if (lane < td) s_d[p.sd + p.ebd + lane] = (unsigned char)e.dt;
+  mbar_wait_sleep(bar, parity);
   __syncwarp();
 }
 
+// gamma^kLane in fp64 (the composed factor of a run of kLane steps without a done flag).
+__device__ __forceinline__ double gamma_run(double gamma) {
+  double a = 1.0, q = gamma;
+#pragma unroll
+  for (int b = 0; b < 6; ++b) {
+    if ((kLane >> b) & 1) a *= q;
+    q *= q;
+  }
+  return a;
+}
+
 // Scan one staged pass given the value entering it from the right (`carry`); writes the outputs
-// into the staging buffer and returns the value at the pass's first step.
+// into the staging buffer and returns the value at the pass's first step (meaningful only for a
+// full pass, len == kSeg: a shorter pass is the first of its row, whose value is not needed).
+// gamma is the fp32 discount widened to fp64; g_run = gamma_run(gamma).
 __device__ __forceinline__ double scan_pass(const Pass& p, float* s_r, const unsigned char* s_d, double carry,
-                                            double gamma, float gamma_f, int lane) {
-  // Lane l owns steps [l*kLane, l*kLane + cnt) of the pass, cnt <= kLane.
+                                            double gamma, double g_run, float gamma_f, int lane) {
   const int lo = lane * kLane;
-  const int cnt = max(0, min(kLane, p.len - lo));
-  const unsigned long long dmask = done_mask(s_d, p.pd + lo, cnt);  // bit e: done at step lo + e
-  float* rl = s_r + p.pr + lo;
+  const unsigned long long dmask = done_mask(s_d, p.gd + lo);  // bit e: done at slot lo + e
+  float* rl = s_r + p.gr + lo;
+  // Composition of the run in fp64: y -> Bv + A*y (the factor of slot e is 0 at a done flag, else
+  // gamma; Bv stays finite, so 0 * Bv is an exact zero).
   double Bv = 0.0;
 #pragma unroll
   for (int e = kLane - 1; e >= 0; --e) {
-    if (e < cnt) {
-      const double rv = double(rl[e]);
-      Bv = ((dmask >> e) & 1ull) ? rv : fma(gamma, Bv, rv);
-    }
+    const double a = ((dmask >> e) & 1ull) ? 0.0 : gamma;
+    Bv = fma(a, Bv, double(rl[e]));
   }
-  double A = 0.0;  // product of the run's factors: 0 if any done, else gamma^cnt
-  if (dmask == 0) {
-    double q = gamma;
-    A = 1.0;
-#pragma unroll
-    for (int b = 0; b < 6; ++b) {
-      if ((cnt >> b) & 1) A *= q;
-      q *= q;
-    }
-  }
+  double A = dmask == 0 ? g_run : 0.0;
   // Inclusive suffix composition over lanes: lane l gets f_l o f_{l+1} o ... o f_31.
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
@@ -189,7 +208,7 @@ __device__ __forceinline__ double scan_pass(const Pass& p, float* s_r, const uns
       A *= A2;
     }
   }
-  const double start = fma(A, carry, Bv);                // value at this lane's first step
+  const double start = fma(A, carry, Bv);                // value at this lane's first slot
   double yin = __shfl_down_sync(0xffffffffu, start, 1);  // value entering this lane's run
   if (lane == 31) yin = carry;
   const double first = __shfl_sync(0xffffffffu, start, 0);
@@ -197,44 +216,39 @@ __device__ __forceinline__ double scan_pass(const Pass& p, float* s_r, const uns
   float y = float(yin);
 #pragma unroll
   for (int e = kLane - 1; e >= 0; --e) {
-    if (e < cnt) {
-      const float rv = rl[e];
-      y = ((dmask >> e) & 1ull) ? rv : __fmaf_rn(gamma_f, y, rv);
-      rl[e] = y;
-    }
+    const float rv = rl[e];
+    y = ((dmask >> e) & 1ull) ? rv : __fmaf_rn(gamma_f, y, rv);
+    rl[e] = y;
   }
   __syncwarp();
   return first;
 }
 
-// Each warp streams its rows (row = warp id, + total warps, ...) pass by pass, from the end of a
-// row to its start.  With nbuf = 2 the next pass is in flight in the second staging buffer while
-// the current one is scanned and written out; with nbuf = 1 (every warp has a single pass, and the
-// smaller footprint lets 40 warps share an SM) passes are staged one after the other.
-__global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restrict__ reward,
-                                                       const unsigned char* __restrict__ done, float gamma,
-                                                       int B, int T, int nbuf, float* __restrict__ out) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ uint64_t bars[kWarps][2];  // one barrier per staging buffer
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned char* wbase = smem + warp * nbuf * kWarpSmem;  // buffer b at wbase + b * kWarpSmem
+// One warp streams rows first_row, first_row + row_stride, ... pass by pass, from the end of a row
+// to its start.  wbase: the warp's staging memory (nbuf buffers of kWarpSmem bytes); bars: its two
+// mbarriers (initialised here).  With nbuf = 2 the next pass is in flight in the second buffer
+// while the current one is scanned and written out; with nbuf = 1 passes are staged one after the
+// other (a smaller footprint, so more warps share an SM).
+__device__ __forceinline__ void warp_rows(const float* __restrict__ reward, const unsigned char* __restrict__ done,
+                                          float gamma, int64_t B, int T, float* __restrict__ out, int64_t first_row,
+                                          int64_t row_stride, unsigned char* wbase, uint64_t* bars, int nbuf,
+                                          int lane) {
   auto s_rb = [&](uint32_t b) { return reinterpret_cast<float*>(wbase + b * kWarpSmem); };
   auto s_db = [&](uint32_t b) { return wbase + b * kWarpSmem + kRewardBytes; };
   if (lane == 0) {
-    mbar_init(&bars[warp][0], 1);
-    mbar_init(&bars[warp][1], 1);
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
     fence_barrier_init();
   }
   __syncwarp();
-  const double g = double(gamma);
-  const int64_t stride = int64_t(gridDim.x) * kWarps;
-  int64_t row = int64_t(blockIdx.x) * kWarps + warp;
+  const double g = double(gamma), g_run = gamma_run(g);
+  int64_t row = first_row;
   if (row >= B) return;
   int t1 = T;
   // Current pass and its staging state.
   Pass cur = make_pass(reward + row * int64_t(T), done + row * int64_t(T), t1 > kSeg ? t1 - kSeg : 0,
                        t1 > kSeg ? kSeg : t1);
-  Edges ecur = issue_pass(cur, s_rb(0), s_db(0), &bars[warp][0], lane);
+  Edges ecur = issue_pass(cur, s_rb(0), s_db(0), &bars[0], lane);
   uint32_t k = 0;
   double carry = 0.0;
   for (;;) {
@@ -242,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restric
     int64_t nrow = row;
     int nt1 = t1 - kSeg;
     if (nt1 <= 0) {
-      nrow = row + stride;
+      nrow = row + row_stride;
       nt1 = T;
     }
     const bool has_next = nrow < B;
@@ -252,20 +266,20 @@ __global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restric
     if (has_next && nbuf == 2) {
       const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
       nxt = make_pass(reward + nrow * int64_t(T), done + nrow * int64_t(T), nt0, nt1 - nt0);
-      enxt = issue_pass(nxt, s_rb(nb), s_db(nb), &bars[warp][nb], lane);
+      enxt = issue_pass(nxt, s_rb(nb), s_db(nb), &bars[nb], lane);
     }
     const uint32_t cb = nbuf == 2 ? (k & 1u) : 0u;
     const uint32_t par = nbuf == 2 ? ((k >> 1) & 1u) : (k & 1u);
-    land_pass(cur, ecur, s_rb(cb), s_db(cb), &bars[warp][cb], par, lane);
-    const double first = scan_pass(cur, s_rb(cb), s_db(cb), carry, g, gamma, lane);
+    land_pass(cur, ecur, s_rb(cb), s_db(cb), &bars[cb], par, lane);
+    const double first = scan_pass(cur, s_rb(cb), s_db(cb), carry, g, g_run, gamma, lane);
     const int t0 = t1 > kSeg ? t1 - kSeg : 0;
-    drain_floats(out + row * int64_t(T) + t0, cur.len, s_rb(cb), cur.pr, lane);
+    drain_floats(out + row * int64_t(T) + t0, cur.len, s_rb(cb) + (cur.sr - cur.pr), cur.pr, lane);
     __syncwarp();
     if (!has_next) break;
     if (nbuf == 1) {
       const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
       nxt = make_pass(reward + nrow * int64_t(T), done + nrow * int64_t(T), nt0, nt1 - nt0);
-      enxt = issue_pass(nxt, s_rb(0), s_db(0), &bars[warp][0], lane);
+      enxt = issue_pass(nxt, s_rb(0), s_db(0), &bars[0], lane);
     }
     carry = (nrow == row) ? first : 0.0;
     row = nrow;
@@ -274,6 +288,42 @@ __global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restric
     ecur = enxt;
     ++k;
   }
+}
+
+// One warp computes one whole row through one staging buffer (kWarpSmem bytes at wbase) and one
+// initialised mbarrier whose completed-phase count the caller keeps in `phase`.  Passes run from
+// the end of the row to its start, exactly as warp_rows with nbuf = 1 (same bits).
+__device__ __forceinline__ void one_row(const float* __restrict__ reward, const unsigned char* __restrict__ done,
+                                        float gamma, int T, float* __restrict__ out, int64_t row,
+                                        unsigned char* wbase, uint64_t* bar, uint32_t& phase, int lane) {
+  float* s_r = reinterpret_cast<float*>(wbase);
+  unsigned char* s_d = wbase + kRewardBytes;
+  const float* rrow = reward + row * int64_t(T);
+  const unsigned char* drow = done + row * int64_t(T);
+  float* orow = out + row * int64_t(T);
+  const double g = double(gamma), g_run = gamma_run(g);
+  double carry = 0.0;
+  for (int t1 = T; t1 > 0; t1 -= kSeg) {
+    const int t0 = t1 > kSeg ? t1 - kSeg : 0;
+    const Pass p = make_pass(rrow, drow, t0, t1 - t0);
+    const Edges e = issue_pass(p, s_r, s_d, bar, lane);
+    land_pass(p, e, s_r, s_d, bar, phase & 1u, lane);
+    ++phase;
+    carry = scan_pass(p, s_r, s_d, carry, g, g_run, gamma, lane);
+    drain_floats(orow + t0, p.len, s_r + (p.sr - p.pr), p.pr, lane);
+    __syncwarp();
+  }
+}
+
+// Warp w of CTA c handles rows c*kWarps + w, + gridDim.x*kWarps, ...
+__global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restrict__ reward,
+                                                       const unsigned char* __restrict__ done, float gamma,
+                                                       int B, int T, int nbuf, float* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint64_t bars[kWarps][2];  // one barrier per staging buffer
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  warp_rows(reward, done, gamma, B, T, out, int64_t(blockIdx.x) * kWarps + warp, int64_t(gridDim.x) * kWarps,
+            smem + warp * nbuf * kWarpSmem, bars[warp], nbuf, lane);
 }
 
 inline int run(const float* reward, const unsigned char* done, float gamma, int32_t B, int32_t T, float* out,

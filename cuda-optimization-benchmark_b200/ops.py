@@ -24,6 +24,15 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
 
 
+def _opt_ptr(t, stand_in):
+    """Pointer of an optional input stream: NULL when absent.  torch gives an empty tensor a NULL
+    data pointer, which the C ABI would read as "absent"; a present but empty stream passes a
+    valid stand-in address instead (never dereferenced: there are no elements)."""
+    if t is None:
+        return ctypes.c_void_p(0)
+    return ctypes.c_void_p(t.data_ptr() or stand_in.data_ptr())
+
+
 def _stream(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
@@ -107,8 +116,9 @@ def ppo_clip(cur, old, adv, clip_epsilon, entropy=None, out=None):
     out = torch.empty(k, dtype=torch.float32, device=cur.device) if out is None else out
     lib = _lib()
     ws = workspace("ppo", lib.b200_ppo_workspace_bytes(n), cur.device)
-    _native.check(lib.b200_ppo_async(_ptr(cur), _ptr(old), _ptr(adv), _ptr(entropy), n, float(clip_epsilon),
-                                     _ptr(out), _ptr(ws), ws.numel(), _stream(cur.device)), "ppo_clip")
+    _native.check(lib.b200_ppo_async(_ptr(cur), _ptr(old), _ptr(adv), _opt_ptr(entropy, out), n,
+                                     float(clip_epsilon), _ptr(out), _ptr(ws), ws.numel(), _stream(cur.device)),
+                  "ppo_clip")
     return out
 
 
@@ -119,7 +129,7 @@ def ppo_partials(cur, old, adv, clip_epsilon, entropy=None):
     chunk = lib.b200_ppo_chunk_elems()
     rec = lib.b200_ppo_partial_bytes()
     parts = torch.empty(((n + chunk - 1) // chunk, rec), dtype=torch.uint8, device=cur.device)
-    _native.check(lib.b200_ppo_shard_partials(_ptr(cur), _ptr(old), _ptr(adv), _ptr(entropy), n,
+    _native.check(lib.b200_ppo_shard_partials(_ptr(cur), _ptr(old), _ptr(adv), _opt_ptr(entropy, parts), n,
                                               float(clip_epsilon), _ptr(parts), _stream(cur.device)),
                   "ppo_partials")
     return parts
@@ -146,6 +156,65 @@ def reward_to_go(reward, done, gamma, out=None):
     return out
 
 
+# ---------------------------------------------------------------------------- fused RL loss step
+def rl_step(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_out=None, ppo_out=None):
+    """reward_to_go and ppo_clip on independent inputs in one launch; the same bits as the two
+    separate calls.  Returns (returns [B, T], PPO outputs [6] or [7])."""
+    _need(reward, "reward", torch.float32)
+    dev = reward.device
+    _need(done, "done", torch.bool, dev)
+    if reward.dim() != 2 or done.shape != reward.shape:
+        raise ValueError("reward and done must both be (B, T)")
+    for t, nm in ((cur, "current_log_prob"), (old, "old_log_prob"), (adv, "advantage")):
+        _need(t, nm, torch.float32, dev)
+    if entropy is not None:
+        _need(entropy, "entropy", torch.float32, dev)
+    n = cur.numel()
+    if old.numel() != n or adv.numel() != n or (entropy is not None and entropy.numel() != n):
+        raise ValueError("PPO inputs differ in size")
+    B, T = reward.shape
+    rtg_out = torch.empty_like(reward) if rtg_out is None else rtg_out
+    k = 7 if entropy is not None else 6
+    ppo_out = torch.empty(k, dtype=torch.float32, device=dev) if ppo_out is None else ppo_out
+    lib = _lib()
+    ws = workspace("ppo", lib.b200_ppo_workspace_bytes(n), dev)
+    _native.check(lib.b200_rl_step_async(_ptr(reward), _ptr(done), float(gamma), B, T, _ptr(rtg_out), _ptr(cur),
+                                         _ptr(old), _ptr(adv), _opt_ptr(entropy, ppo_out), n, float(clip_epsilon),
+                                         _ptr(ppo_out), _ptr(ws), ws.numel(), _stream(dev)), "rl_step")
+    return rtg_out, ppo_out
+
+
+def rl_step_shard(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_out=None, partials_out=None):
+    """The fused step of one shard: returns and the PPO per-chunk partial records (as
+    ppo_partials), for a cross-GPU gather and ppo_finish."""
+    _need(reward, "reward", torch.float32)
+    dev = reward.device
+    _need(done, "done", torch.bool, dev)
+    if reward.dim() != 2 or done.shape != reward.shape:
+        raise ValueError("reward and done must both be (B, T)")
+    for t, nm in ((cur, "current_log_prob"), (old, "old_log_prob"), (adv, "advantage")):
+        _need(t, nm, torch.float32, dev)
+    if entropy is not None:
+        _need(entropy, "entropy", torch.float32, dev)
+    n = cur.numel()
+    if old.numel() != n or adv.numel() != n or (entropy is not None and entropy.numel() != n):
+        raise ValueError("PPO inputs differ in size")
+    lib = _lib()
+    chunk = lib.b200_ppo_chunk_elems()
+    shape = ((n + chunk - 1) // chunk, lib.b200_ppo_partial_bytes())
+    if partials_out is None:
+        partials_out = torch.empty(shape, dtype=torch.uint8, device=dev)
+    elif tuple(partials_out.shape) != shape or partials_out.dtype != torch.uint8:
+        raise ValueError(f"partials_out must be uint8 {shape}")
+    B, T = reward.shape
+    rtg_out = torch.empty_like(reward) if rtg_out is None else rtg_out
+    _native.check(lib.b200_rl_step_shard_async(_ptr(reward), _ptr(done), float(gamma), B, T, _ptr(rtg_out),
+                                               _ptr(cur), _ptr(old), _ptr(adv), _opt_ptr(entropy, rtg_out), n,
+                                               float(clip_epsilon), _ptr(partials_out), _stream(dev)),
+                  "rl_step_shard")
+    return rtg_out, partials_out
+
+
 # ----------------------------------------------------------------------------------------- LIF
 def leaky(input_current, mem0, beta, threshold, spikes=None, final_mem=None):
     _need(input_current, "input_current", torch.float32)
@@ -158,6 +227,46 @@ def leaky(input_current, mem0, beta, threshold, spikes=None, final_mem=None):
     _native.check(_lib().b200_leaky_async(_ptr(input_current), _ptr(mem0), _ptr(beta), _ptr(threshold), T, B, H,
                                           _ptr(spikes), _ptr(final_mem), _stream(dev)), "leaky")
     return spikes, final_mem
+
+
+# ----------------------------------------------------------------------------------------- KAN
+def efficient_kan(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, out=None):
+    """KANLinear forward: out[B, O] = silu(x) base_weight^T + bases(x) (spline_weight * scaler)^T."""
+    _need(x, "x", torch.float32)
+    dev = x.device
+    for t, nm in ((grid, "grid"), (base_weight, "base_weight"), (spline_weight, "spline_weight"),
+                  (spline_scaler, "spline_scaler")):
+        _need(t, nm, torch.float32, dev)
+    B, I = x.shape
+    O = base_weight.shape[0]
+    G, K = int(grid_size), int(spline_order)
+    if grid.shape != (I, G + 2 * K + 1) or base_weight.shape != (O, I) or spline_weight.shape != (O, I, G + K) \
+            or spline_scaler.shape != (O, I):
+        raise ValueError("efficient_kan: inconsistent shapes")
+    out = torch.empty((B, O), dtype=torch.float32, device=dev) if out is None else out
+    lib = _lib()
+    ws = workspace("kan", lib.b200_efficient_kan_workspace_bytes(G, K, B, I, O), dev)
+    _native.check(lib.b200_efficient_kan_async(_ptr(x), _ptr(grid), _ptr(base_weight), _ptr(spline_weight),
+                                               _ptr(spline_scaler), G, K, B, I, O, _ptr(out), _ptr(ws),
+                                               ws.numel(), _stream(dev)), "efficient_kan")
+    return out
+
+
+# ---------------------------------------------------------------------------------- FP8 linear
+def fp8_linear(x_fp8, scale_x, w_fp8, scale_w, bias, out=None):
+    """bf16 (x_fp8 / scale_x) (w_fp8 / scale_w)^T + bias with E4M3 operands [M, K] and [N, K]."""
+    _need(x_fp8, "x_fp8", torch.float8_e4m3fn)
+    dev = x_fp8.device
+    _need(w_fp8, "w_fp8", torch.float8_e4m3fn, dev)
+    _need(bias, "bias", torch.bfloat16, dev)
+    M, K = x_fp8.shape
+    N = w_fp8.shape[0]
+    if w_fp8.shape[1] != K or bias.numel() != N:
+        raise ValueError("fp8_linear: inconsistent shapes")
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev) if out is None else out
+    _native.check(_lib().b200_fp8_linear_async(M, K, N, _ptr(x_fp8), float(scale_x), _ptr(w_fp8), float(scale_w),
+                                               _ptr(bias), _ptr(out), _stream(dev)), "fp8_linear")
+    return out
 
 
 # ------------------------------------------------------------------- reference-interface mirror
@@ -173,4 +282,9 @@ def reference(task, inp):
     if task == "leaky":
         s, m = leaky(inp["input_current"], inp["mem0"], inp["beta"], inp["threshold"])
         return {"spikes": s, "final_mem": m}
+    if task == "efficient_kan":
+        return {"out": efficient_kan(inp["x"], inp["grid"], inp["base_weight"], inp["spline_weight"],
+                                     inp["spline_scaler"], inp["grid_size"], inp["spline_order"])}
+    if task == "fp8_linear":
+        return {"output": fp8_linear(inp["x_fp8"], inp["scale_x"], inp["w_fp8"], inp["scale_w"], inp["bias"])}
     raise KeyError(f"unknown or not yet built task: {task}")

@@ -128,6 +128,24 @@ int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamm
                             float* output, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Fused RL loss step (no reference counterpart: the BASELINE RL pipeline, configs[1], runs
+ * reward_to_go and ppo_clip back to back on independent inputs).  One launch computes both;
+ * rtg_out is bit-identical to b200_reward_to_go_async and ppo_out to b200_ppo_async on the same
+ * inputs.  entropy may be NULL (6 PPO outputs) or a stream (7).  workspace as b200_ppo_async
+ * (b200_ppo_workspace_bytes(n), zero-filled once; the same buffer may serve both entry points).
+ * ------------------------------------------------------------------------------------------- */
+int b200_rl_step_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T, float* rtg_out,
+                       const float* current_log_prob, const float* old_log_prob, const float* advantage,
+                       const float* entropy, int64_t n, float clip_epsilon, float* ppo_out, void* workspace,
+                       size_t workspace_bytes, void* stream);
+/* Multi-GPU shard form: the PPO half writes its per-chunk partials (as b200_ppo_shard_partials)
+ * for a cross-GPU gather and b200_ppo_finish. */
+int b200_rl_step_shard_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                             float* rtg_out, const float* current_log_prob, const float* old_log_prob,
+                             const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
+                             void* partials, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Leaky integrate-and-fire layer (task leaky).
  * Replaces `void reference(const float* input_current, const float* mem0, const float* beta,
  * const float* threshold, int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem)`:
