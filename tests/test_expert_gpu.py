@@ -1,0 +1,207 @@
+"""GPU: the reference's own expert kernels (reference/<task>/solution.cu, compiled from their sources
+by oracle/ref_build.py into oracle/_ref/<task>/expert.so) beside the B200 drop-ins built the same
+way (abi/_build/<task>/kernel.so), both called through the grader's `grader_entry(void** a)`
+protocol (graders/child.py:85-97) on the same device buffers.
+
+- Checker: on the golden cases the expert's results meet the fp64 oracle's tolerance (spikes
+  bit-exact), which pins the oracle to the reference's own GPU implementation as well as to its
+  Python oracle.
+- Comparison: at every BASELINE.json size both sides are checked (against each other, or for FP8
+  against the fp64 oracle on the first rows, where the expert's TF32 multiply is recorded when it
+  falls outside the tolerance) and timed with the grader's rule
+  (graders/child.py:228-244: three warm-up calls, then the median over 10 batches of K
+  back-to-back calls, K chosen so a batch takes at least 1 ms; the same inputs every call, as the
+  grader does).  The table is printed at the end (run with -s) and written to the file named by
+  B200_EXPERT_TIMES when that is set.
+"""
+import ctypes
+import gc
+import importlib.util
+import json
+import os
+import statistics
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import REPO, golden_cases
+from oracle import exact, inputs, ref_build
+
+pytestmark = pytest.mark.gpu
+
+ABI = REPO / "cuda-optimization-benchmark_b200" / "abi"
+_spec = importlib.util.spec_from_file_location("b200_amalgamate_x", ABI / "amalgamate.py")
+am = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(am)
+
+SCALAR = {"int64_t": ctypes.c_int64, "int32_t": ctypes.c_int32, "float": ctypes.c_float}
+OUTPUTS = {"pow_abs_sqrt_mean": {"output": (torch.float32, lambda s: ())},
+           "ppo_clip": {"output": (torch.float32, lambda s: (6,))},
+           "reward_to_go": {"output": (torch.float32, lambda s: (s["B"], s["T"]))},
+           "leaky": {"spikes": (torch.float32, lambda s: (s["T"], s["B"], s["H"])),
+                     "final_mem": (torch.float32, lambda s: (s["B"], s["H"]))},
+           "efficient_kan": {"out": (torch.float32, lambda s: (s["B"], s["O"]))},
+           "fp8_linear": {"output": (torch.bfloat16, lambda s: (s["M"], s["N"]))}}
+TIMES = []
+
+
+def entry(path):
+    if not path.exists():
+        pytest.skip(f"{path} not built (run __graft_entry__.build() where the reference checkout exists)")
+    fn = ctypes.CDLL(str(path)).grader_entry
+    fn.argtypes = [ctypes.POINTER(ctypes.c_void_p)]
+    fn.restype = None
+    return fn
+
+
+def expert(task):
+    return entry(ref_build.library(task))
+
+
+def ours(task):
+    return entry(am.BUILD / task / "kernel.so")
+
+
+class Bound:
+    """One task's device inputs and outputs, and the grader-protocol argument array over them."""
+
+    def __init__(self, task, s):
+        self.dev = {k: v.cuda() for k, v in s.items() if isinstance(v, torch.Tensor)}
+        self.outs = {k: torch.empty(shp(s), dtype=dt, device="cuda") for k, (dt, shp) in OUTPUTS[task].items()}
+        self.keep = []
+        for ctype, name in am.params(task):
+            if "*" in ctype:
+                t = self.outs[name] if name in self.outs else self.dev[name]
+                self.keep.append(ctypes.c_void_p(t.data_ptr()))
+            else:
+                self.keep.append(SCALAR[ctype.replace("const ", "").strip()](s[name]))
+        self.arr = (ctypes.c_void_p * len(self.keep))(*[ctypes.addressof(v) for v in self.keep])
+
+    def call(self, fn):
+        for o in self.outs.values():
+            o.fill_(float("nan")) if o.is_floating_point() else o.zero_()
+        fn(self.arr)
+        torch.cuda.synchronize()
+        return {k: v.cpu() for k, v in self.outs.items()}
+
+
+def grader_ms(fn, min_ms=1.0, batches=10):
+    """Median ms per call under the grader's timing rule."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    fn()
+    e1.record()
+    e1.synchronize()
+    one = e0.elapsed_time(e1)
+    k = max(1, min(1000, int(min_ms / one) + 1)) if one > 0 else 1000
+    per = []
+    for _ in range(batches):
+        e0.record()
+        for _ in range(k):
+            fn()
+        e1.record()
+        e1.synchronize()
+        per.append(e0.elapsed_time(e1) / k)
+    return statistics.median(per)
+
+
+def check(task, got, ref):
+    atol, rtol = exact.TOLERANCE[task]
+    for k, v in got.items():
+        if task == "fp8_linear":
+            have = exact.bf16_bits_to_f64(v.view(torch.int16).numpy().view(np.uint16))
+            want = ref["output_f64"]
+        else:
+            have, want = v.double().numpy(), ref[k]
+        bad, worst = exact.within(have, want, atol, rtol)
+        assert bad == 0, (task, k, bad, worst)
+        if task == "leaky" and k == "spikes":
+            assert np.array_equal(v.numpy(), ref["spikes"]), "spikes not bit-exact"
+
+
+CASES = [(t, cid, rec) for t in OUTPUTS for cid, rec in golden_cases(t)[:3]]
+
+
+@pytest.mark.parametrize("task,cid,rec", CASES, ids=[f"{t}-{c}" for t, c, _ in CASES])
+def test_expert_meets_oracle(task, cid, rec):
+    """The reference's expert kernel on the golden cases, against the fp64 oracle."""
+    s = inputs.task_inputs(task, rec["case"], int(rec["case"]["seed"]))
+    check(task, Bound(task, s).call(expert(task)), exact.TASKS[task](s))
+
+
+def _baseline(name):
+    if name == "pow_abs_sqrt_mean":
+        return inputs.baseline_inputs("robust_l1", seed=0)
+    if name in ("ppo_clip", "reward_to_go"):
+        return inputs.baseline_inputs("rl_pipeline", seed=0)
+    if name == "leaky":
+        return inputs.baseline_inputs("lif", seed=0)
+    if name == "efficient_kan":
+        return inputs.baseline_inputs("kan", seed=0)
+    raise KeyError(name)
+
+
+SIZES = [("pow_abs_sqrt_mean", None), ("ppo_clip", None), ("reward_to_go", None), ("leaky", None),
+         ("efficient_kan", None)] + [("fp8_linear", shp) for shp in inputs.BASELINE_SHAPES["fp8_linear"]]
+
+
+@pytest.mark.parametrize("task,shape", SIZES, ids=[t if s is None else f"{t}-{s[0]}x{s[1]}x{s[2]}" for t, s in SIZES])
+def test_time_against_expert(task, shape):
+    """Both kernels at the BASELINE size, same buffers, the grader's timing rule."""
+    fe, fo = expert(task), ours(task)
+    s = inputs.baseline_inputs("fp8_linear", seed=0, shape=shape) if shape else _baseline(task)
+    b = Bound(task, s)
+    got = b.call(fo)
+    want = b.call(fe)
+    expert_bad = None
+    if task == "fp8_linear":
+        # Both against the fp64 oracle on the first rows.  The expert multiplies in TF32, whose
+        # error at this config's unscaled N(0, 1) weights can exceed the task tolerance; that is
+        # recorded, not asserted.  Ours must pass.
+        rows = slice(0, min(shape[0], 64))
+        ref = exact.fp8_linear(s, rows=rows)["output_f64"]
+        atol, rtol = exact.TOLERANCE[task]
+        have = {n: exact.bf16_bits_to_f64(v[rows].contiguous().view(torch.int16).numpy().view(np.uint16))
+                for n, v in (("ours", got["output"]), ("expert", want["output"]))}
+        bad_ours, worst = exact.within(have["ours"], ref, atol, rtol)
+        assert bad_ours == 0, ("ours outside the tolerance", worst)
+        expert_bad = int(exact.within(have["expert"], ref, atol, rtol)[0])
+    else:
+        # Both meet the oracle at the golden sizes; at this size they must agree within twice the
+        # task tolerance (spikes bit-exact).
+        for k in got:
+            if task == "leaky" and k == "spikes":
+                assert torch.equal(got[k], want[k])
+                continue
+            atol, rtol = exact.TOLERANCE[task]
+            g = got[k].reshape(-1)[: 1 << 22].double().numpy()   # the first 4M outputs at most
+            w = want[k].reshape(-1)[: 1 << 22].double().numpy()
+            ok = np.abs(g - w) <= 2 * (atol + rtol * np.abs(w))
+            bad = np.flatnonzero(~ok)
+            assert bad.size == 0, (task, k, int(bad.size), int(bad[0]), float(g[bad[0]]), float(w[bad[0]]))
+    t_expert = grader_ms(lambda: fe(b.arr))
+    t_ours = grader_ms(lambda: fo(b.arr))
+    label = task if shape is None else f"{task} M{shape[0]} N{shape[1]} K{shape[2]}"
+    TIMES.append({"op": label, "expert_us": t_expert * 1e3, "b200_us": t_ours * 1e3, "speedup": t_expert / t_ours,
+                  "expert_outside_tolerance": expert_bad})
+    del b, s
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
+def test_zz_report():
+    if not TIMES:
+        pytest.skip("no timings collected")
+    lines = [f"{'op':40s} {'expert us':>11s} {'B200 us':>10s} {'speedup':>8s}  expert outside tol (checked rows)"]
+    for r in TIMES:
+        eb = "" if r["expert_outside_tolerance"] is None else str(r["expert_outside_tolerance"])
+        lines.append(f"{r['op']:40s} {r['expert_us']:11.2f} {r['b200_us']:10.2f} {r['speedup']:7.2f}x  {eb}")
+    print("\n" + "\n".join(lines))
+    out = os.environ.get("B200_EXPERT_TIMES")
+    if out:
+        with open(out, "w") as f:
+            json.dump({"device": torch.cuda.get_device_name(), "rows": TIMES}, f, indent=1)
