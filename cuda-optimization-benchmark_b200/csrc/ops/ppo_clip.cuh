@@ -332,8 +332,10 @@ __device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
 }
 
 // Final combination of partials[0..n_parts) in a fixed order by the kThreads consumer threads;
-// writes 6 (or 7) outputs.  Every ratio is > 0, so 0 is the identity of the max.
-__device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, int64_t n_total, bool ext, float* out) {
+// writes 6 (or 7) outputs.  inv_n = 1 / n_total from the host (infinite for an empty batch, which
+// makes every mean NaN, as the mean of nothing is).  Every ratio is > 0, so 0 is the identity of the max.
+__device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, int64_t n_total, double inv_n, bool ext,
+                                       float* out) {
   __shared__ double s_d[5][kThreads / 32];
   __shared__ float s_max[kThreads / 32];
   __shared__ unsigned long long s_cnt[kThreads / 32];
@@ -384,14 +386,15 @@ __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, in
       mx = fmaxf(mx, s_max[i]);
       c += s_cnt[i];
     }
-    const double N = double(n_total);
-    out[0] = float(-t[0] / N);
-    out[1] = float(double(c) / N);
-    out[2] = float((t[2] - t[1]) / N - 1.0);
-    out[3] = float((t[2] / N) * (t[2] / t[3]));
+    // Means by the host's 1/N (an fp64 divide takes hundreds of cycles on this tail); the ESS ratio
+    // sum(r) / sum(r^2) by one correctly rounded fp32 divide (relative error ~1e-7).
+    out[0] = float(-t[0] * inv_n);
+    out[1] = float(double(c) * inv_n);
+    out[2] = float((t[2] - t[1]) * inv_n - 1.0);
+    out[3] = float((t[2] * inv_n) * double(__fdiv_rn(float(t[2]), float(t[3]))));
     out[4] = n_total > 0 ? mx : __int_as_float(0x7fc00000);
-    out[5] = float(t[2] / N);
-    if (ext) out[6] = float(t[4] / N);
+    out[5] = float(t[2] * inv_n);
+    if (ext) out[6] = float(t[4] * inv_n);
   }
 }
 
@@ -416,24 +419,28 @@ template <bool kVec, bool kEnt, bool kFinish>
 __global__ void __launch_bounds__(kThreads, 4) chunk_kernel(const float* __restrict__ cur, const float* __restrict__ old,
                                                          const float* __restrict__ adv, const float* __restrict__ ent,
                                                          int64_t n, Clip clip, Partial* __restrict__ partials,
-                                                         unsigned* __restrict__ ticket, float* __restrict__ out) {
+                                                         unsigned* __restrict__ ticket, double inv_n,
+                                                         float* __restrict__ out) {
   chunk_partials<kVec, kEnt>(cur, old, adv, ent, n, clip, partials, blockIdx.x, gridDim.x);
   if (kFinish) {
-    if (elect_last_cta(ticket)) finish(partials, (n + kChunk - 1) / kChunk, n, kEnt, out);
+    if (elect_last_cta(ticket)) finish(partials, (n + kChunk - 1) / kChunk, n, inv_n, kEnt, out);
   }
 }
 
 __global__ void __launch_bounds__(kThreads) finish_kernel(const Partial* __restrict__ partials, int64_t n_parts,
-                                                          int64_t n_total, int ext, float* __restrict__ out) {
-  finish(partials, n_parts, n_total, ext != 0, out);
+                                                          int64_t n_total, double inv_n, int ext,
+                                                          float* __restrict__ out) {
+  finish(partials, n_parts, n_total, inv_n, ext != 0, out);
 }
+
+inline double inv_count(int64_t n) { return 1.0 / double(n); }
 
 template <bool kVec, bool kEnt, bool kFinish>
 inline void launch_direct(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
                           const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
   auto kern = chunk_kernel<kVec, kEnt, kFinish>;
   const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
-  kern<<<grid, kThreads, 0, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, out);
+  kern<<<grid, kThreads, 0, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, inv_count(n), out);
 }
 
 template <bool kFinish>
@@ -474,7 +481,7 @@ inline int shard_partials(const float* cur, const float* old, const float* adv, 
 inline int shard_finish(const Partial* partials, int64_t n_parts, int64_t n_total, bool ext, float* out,
                         cudaStream_t stream) {
   if (n_parts < 0 || n_total < 0 || out == nullptr || (n_parts > 0 && partials == nullptr)) return kInvalidArgument;
-  finish_kernel<<<1, kThreads, 0, stream>>>(partials, n_parts, n_total, ext ? 1 : 0, out);
+  finish_kernel<<<1, kThreads, 0, stream>>>(partials, n_parts, n_total, inv_count(n_total), ext ? 1 : 0, out);
   return launch_status();
 }
 

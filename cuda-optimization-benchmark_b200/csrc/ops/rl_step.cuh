@@ -47,6 +47,7 @@ struct Args {
   ppo::Partial* partials;
   unsigned* ticket;
   float* ppo_out;
+  double inv_n;      // 1 / n for the PPO finish
   int64_t rtg_ctas;  // CTAs with the reward-to-go role (kRows rows each per round)
   int64_t ppo_ctas;  // CTAs with the PPO role
 };
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_kernel(const 
   ppo::chunk_partials<kVec, kEnt>(a.cur, a.old, a.adv, a.ent, a.n, a.clip, a.partials, pidx, a.ppo_ctas);
   if (kFinish) {
     if (elect_last_add(a.ticket, 1u, unsigned(a.ppo_ctas)))
-      ppo::finish(a.partials, ppo::num_chunks(a.n), a.n, kEnt, a.ppo_out);
+      ppo::finish(a.partials, ppo::num_chunks(a.n), a.n, a.inv_n, kEnt, a.ppo_out);
   }
 }
 
@@ -146,6 +147,7 @@ inline int run(const float* reward, const unsigned char* done, float gamma, int3
     a.partials = static_cast<ppo::Partial*>(partials_out);
   }
   a.ppo_out = ppo_out;
+  a.inv_n = ppo::inv_count(n);
   const int64_t slots = int64_t(sm_count()) * B200_RL_MIN_CTAS;
   split_roles(a.B, 9 * int64_t(T), ppo::num_chunks(n), (ent != nullptr ? 16 : 12) * ppo::kChunk, slots, finish,
               &a.rtg_ctas, &a.ppo_ctas);

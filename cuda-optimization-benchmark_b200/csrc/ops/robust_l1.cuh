@@ -88,21 +88,25 @@ __device__ __forceinline__ double cta_sum(double v) {
   return s;
 }
 
-// Sum of partials[0..n_parts) in a fixed order (strided per thread, then fixed CTA tree), divided
-// by n_total.  Shared by the single-launch finish and the multi-GPU finish kernel.
-__device__ __forceinline__ void finish(const double* partials, int64_t n_parts, int64_t n_total, float* out) {
+// Sum of partials[0..n_parts) in a fixed order (strided per thread, then fixed CTA tree), times
+// inv_n = 1 / n_total from the host (an fp64 divide would take hundreds of cycles on the kernel's
+// tail).  Shared by the single-launch finish and the multi-GPU finish kernel.
+__device__ __forceinline__ void finish(const double* partials, int64_t n_parts, double inv_n, float* out) {
   double s = 0.0;
   for (int64_t i = threadIdx.x; i < n_parts; i += kThreads) s += ld_cg_f64(partials + i);
   s = cta_sum(s);
-  if (threadIdx.x == 0) out[0] = float(s / double(n_total));   // n_total == 0 gives NaN, like mean([])
+  if (threadIdx.x == 0) out[0] = float(s * inv_n);   // n_total == 0: 0 * inf = NaN, like mean([])
 }
+
+inline double inv_count(int64_t n) { return 1.0 / double(n); }
 
 // Grid: CTA c handles chunks c, c + gridDim.x, ...  Chunk indices are local to this shard;
 // `partials` receives one value per local chunk.  With kFinish, the last CTA also finishes.
 template <bool kVec, bool kFinish>
 __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                                          int64_t n, double* __restrict__ partials,
-                                                         unsigned* __restrict__ ticket, float* __restrict__ out) {
+                                                         unsigned* __restrict__ ticket, double inv_n,
+                                                         float* __restrict__ out) {
   const int64_t n_chunks = (n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const float t = thread_chunk_sum<kVec>(a, b, c * kChunk, n);
@@ -110,13 +114,13 @@ __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict
     if (threadIdx.x == 0) partials[c] = s;
   }
   if (kFinish) {
-    if (elect_last_cta(ticket)) finish(partials, n_chunks, n, out);
+    if (elect_last_cta(ticket)) finish(partials, n_chunks, inv_n, out);
   }
 }
 
 __global__ void __launch_bounds__(kThreads) finish_kernel(const double* __restrict__ partials, int64_t n_parts,
-                                                          int64_t n_total, float* __restrict__ out) {
-  finish(partials, n_parts, n_total, out);
+                                                          double inv_n, float* __restrict__ out) {
+  finish(partials, n_parts, inv_n, out);
 }
 
 template <bool kVec, bool kFinish>
@@ -124,7 +128,7 @@ inline void launch_chunks(const float* a, const float* b, int64_t n, double* par
                           cudaStream_t stream) {
   auto kern = chunk_kernel<kVec, kFinish>;
   const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
-  kern<<<grid, kThreads, 0, stream>>>(a, b, n, partials, ticket, out);
+  kern<<<grid, kThreads, 0, stream>>>(a, b, n, partials, ticket, inv_count(n), out);
 }
 
 // Full op on one device with a caller workspace of workspace_bytes(n) bytes whose first 4 bytes
@@ -152,7 +156,7 @@ inline int shard_partials(const float* a, const float* b, int64_t n, double* par
 
 inline int shard_finish(const double* partials, int64_t n_parts, int64_t n_total, float* out, cudaStream_t stream) {
   if (n_parts < 0 || n_total < 0 || out == nullptr || (n_parts > 0 && partials == nullptr)) return kInvalidArgument;
-  finish_kernel<<<1, kThreads, 0, stream>>>(partials, n_parts, n_total, out);
+  finish_kernel<<<1, kThreads, 0, stream>>>(partials, n_parts, inv_count(n_total), out);
   return launch_status();
 }
 
