@@ -39,6 +39,7 @@ METRIC = "per-op µs and % of HBM or FP8-tensor roofline, 1–8 B200, vs CPU eag
 B, T = 4096, 1000
 N_SAMPLES = B * T
 ROTATE = 4
+READY = 1  # B200_STEP_INPUTS_READY (include/b200ops.h)
 # Algorithmic bytes per call (reads + writes of each op's inputs and outputs).
 RTG_BYTES = (4 + 1 + 4) * N_SAMPLES                 # reward f32 + done u8 -> output f32
 PPO_BYTES = 16 * N_SAMPLES + 7 * 4                  # cur, old, adv, entropy f32 -> 7 f32
@@ -171,6 +172,7 @@ def run_b200(args, world, rank, local):
     gamma, eps = sets[0]["gamma"], sets[0]["clip_epsilon"]
     rtg_out = torch.empty(B, T, device=dev)
     ppo_out = torch.empty(7, device=dev)
+    exchange = None
     if world > 1:
         import torch.distributed as dist
         chunk = lib.b200_ppo_chunk_elems()
@@ -178,6 +180,17 @@ def run_b200(args, world, rank, local):
         rec = lib.b200_ppo_partial_bytes()
         local_parts = torch.empty((n_parts, rec), dtype=torch.uint8, device=dev)
         all_parts = torch.empty((world * n_parts, rec), dtype=torch.uint8, device=dev)
+        # The fused step exchanges the PPO partials over NVLink peer memory inside the kernel; the
+        # NCCL all-gather (graph-replayed) is the fallback where CUDA IPC cannot be set up.
+        try:
+            exchange = ops.PeerExchange(world, rank, N_SAMPLES)
+        except Exception as e:  # noqa: BLE001 - any failure selects the fallback, reported below
+            print(f"rank {rank}: peer exchange unavailable ({e}); using the NCCL all-gather", file=sys.stderr)
+        ok = torch.tensor([1 if exchange is not None else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0 and exchange is not None:
+            exchange.close()
+            exchange = None
 
     # Pre-bound C-ABI argument tuples per input set: the timed loop is one ctypes call per step
     # (N = 1), or the fused shard launch, the NCCL all-gather and the finish launch (N > 1).
@@ -190,20 +203,30 @@ def run_b200(args, world, rank, local):
         rtg_in = (P(s["reward"].data_ptr()), P(s["done"].data_ptr()), gamma, B, T, P(rtg_out.data_ptr()))
         ppo_in = (P(s["current_log_prob"].data_ptr()), P(s["old_log_prob"].data_ptr()),
                   P(s["advantage"].data_ptr()), P(s["entropy"].data_ptr()), N_SAMPLES, eps)
+        # The timed steps run back to back over resident batches: no kernel writes their inputs,
+        # so each step declares them ready and reads them while the previous step finishes.
         if world == 1:
-            step_args.append(rtg_in + ppo_in + (P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), cs))
+            step_args.append(rtg_in + ppo_in + (P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), READY, cs))
+        elif exchange is not None:
+            step_args.append(rtg_in + ppo_in + (P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), exchange.handle))
         else:
             step_args.append(rtg_in + ppo_in + (P(local_parts.data_ptr()), cs))
         rtg_args.append(rtg_in + (cs,))
         ppo_args.append(ppo_in + (P(ppo_out.data_ptr()), P(ws.data_ptr()), ws.numel(), cs))
     f_rtg, f_ppo = lib.b200_reward_to_go_async, lib.b200_ppo_async
-    f_step = lib.b200_rl_step_async if world == 1 else lib.b200_rl_step_shard_async
+    f_step = lib.b200_rl_step_ex_async if world == 1 else lib.b200_rl_step_shard_async
     f_finish = lib.b200_ppo_finish
+    f_exchange, f_next_epoch = lib.b200_rl_step_exchange_async, lib.b200_peer_next_epoch
     if world > 1:
         finish_args = (P(all_parts.data_ptr()), world * n_parts, world * N_SAMPLES, 1, P(ppo_out.data_ptr()), cs)
     status = [0]
+    flags = [READY]  # the exchange step's flags (the one-GPU step carries them in step_args)
 
     def step(i):
+        if world > 1 and exchange is not None:
+            exchange.epoch = f_next_epoch(exchange.epoch)
+            status[0] |= f_exchange(*step_args[i % ROTATE], exchange.epoch, flags[0], cs)
+            return
         status[0] |= f_step(*step_args[i % ROTATE])
         if world > 1:
             dist.all_gather_into_tensor(all_parts, local_parts)
@@ -225,6 +248,28 @@ def run_b200(args, world, rank, local):
     torch.cuda.synchronize(dev)
     if status[0] != 0:
         raise RuntimeError(f"rl_step returned status {status[0]}")
+    # N > 1: each step (shard kernel -> NCCL all-gather of the chunk partials -> finish) is replayed
+    # from a CUDA graph, one per input set, so the host issues one launch per step instead of three
+    # (the Python cost of the collective call would otherwise exceed the step's device time).
+    step_graphs = []
+    if world > 1 and exchange is None:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        for k in range(ROTATE):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                cs_side = P(torch.cuda.current_stream(dev).cuda_stream)
+                status[0] |= f_step(*step_args[k][:-1], cs_side)
+                dist.all_gather_into_tensor(all_parts, local_parts)
+                status[0] |= f_finish(*finish_args[:-1], cs_side)
+            step_graphs.append(g)
+        torch.cuda.synchronize(dev)
+
+        def step(i):  # noqa: F811 (the graphed step replaces the eager one)
+            step_graphs[i % ROTATE].replay()
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize(dev)
     clocks = ClockSampler(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
@@ -240,12 +285,37 @@ def run_b200(args, world, rank, local):
     if status[0] != 0:
         raise RuntimeError(f"rl_step returned status {status[0]}")
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+    del step_graphs  # graphs holding NCCL work are released before the process group is destroyed
 
     # Average duration of the fused kernel alone (the roofline's kernel): at N = 1 the timed step is
     # exactly one launch of it; at N > 1 its shard form is timed in its own back-to-back loop.
     def fused_only(i):
         status[0] |= f_step(*step_args[i % ROTATE])
-    fused_ms = ms if world == 1 else max_over_ranks(loop_ms(fused_only, args.steps), world)
+    if world == 1 or exchange is not None:
+        fused_ms = ms  # the timed step is one launch of the fused kernel (exchange included at N > 1)
+    else:
+        fused_ms = max_over_ranks(loop_ms(fused_only, args.steps), world)
+
+    # The same steps without the inputs-ready declaration: each waits for the previous kernel
+    # before reading (the default of the API; only the launch latency overlaps).
+    waitfirst_ms = None
+    if world == 1 or exchange is not None:
+        wf_args = [a[:-2] + (0, cs) for a in step_args] if world == 1 else None
+
+        def waitfirst(i):
+            if world == 1:
+                status[0] |= f_step(*wf_args[i % ROTATE])
+            else:
+                flags[0] = 0
+                step(i)
+                flags[0] = READY
+        for i in range(args.warmup):
+            waitfirst(i)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        waitfirst_ms = max_over_ranks(loop_ms(waitfirst, args.steps), world)
+        if status[0] != 0:
+            raise RuntimeError(f"rl_step returned status {status[0]}")
 
     # The two ops as separate launches on the same rotation (per-op breakdown, unfused step time).
     for i in range(args.warmup):
@@ -311,6 +381,10 @@ def run_b200(args, world, rank, local):
         if world == 1:
             ops.rl_step(dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"], dbuf["old_log_prob"],
                         dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out, ppo_out=ppo_out)
+        elif exchange is not None:
+            ops.rl_step_exchange(exchange, dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"],
+                                 dbuf["old_log_prob"], dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out,
+                                 ppo_out=ppo_out)
         else:
             ops.rl_step_shard(dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"], dbuf["old_log_prob"],
                               dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out, partials_out=local_parts)
@@ -341,7 +415,7 @@ def run_b200(args, world, rank, local):
     peak, peak_kind = peaks()
     step_bytes = RTG_BYTES + PPO_BYTES
     achieved = step_bytes / (fused_ms * 1e-3) / 1e9
-    per_step_launches = 1 if world == 1 else 2
+    per_step_launches = 1 if (world == 1 or exchange is not None) else 2
     line = {
         "metric": METRIC,
         "value": world * N_SAMPLES / (ms * 1e-3),
@@ -360,13 +434,20 @@ def run_b200(args, world, rank, local):
         "data": "synthetic (seeded; BASELINE.json configs[1] distributions)",
         "config": {"workload": "rl_pipeline: reward_to_go + ppo_clip_ext", "B": B, "T": T, "H": 1,
                    "samples_per_gpu": N_SAMPLES, "gamma": 0.99, "done_p": 0.01, "clip_epsilon": 0.2,
+                   "launch": "programmatic dependent launch; back-to-back steps over resident batches declare "
+                             "their inputs ready (B200_STEP_INPUTS_READY)",
                    "l2": f"rotating {ROTATE} input sets of {(RTG_BYTES - 4 * N_SAMPLES + PPO_BYTES) / 1e6:.0f} MB "
                          f"(> 126 MB L2)",
-                   "parallelism": f"dp{world}: one batch per rank, PPO chunk partials all-gathered (NCCL)"
-                   if world > 1 else "1 GPU"},
+                   "parallelism": (f"dp{world}: one batch per rank; PPO chunk partials exchanged over NVLink "
+                                   f"peer memory inside the fused kernel" if exchange is not None else
+                                   f"dp{world}: one batch per rank, PPO chunk partials all-gathered (NCCL); "
+                                   f"each step replayed from a CUDA graph") if world > 1 else "1 GPU"},
         "per_op": {
             "rl_step (fused)": {"us": fused_ms * 1e3, "bytes": step_bytes,
                                 "gbs": achieved, "frac_of_hbm": achieved / peak},
+            "rl_step (fused, inputs not declared ready)": (
+                {"us": waitfirst_ms * 1e3, "gbs": step_bytes / (waitfirst_ms * 1e-3) / 1e9,
+                 "frac_of_hbm": step_bytes / (waitfirst_ms * 1e-3) / 1e9 / peak} if waitfirst_ms else None),
             "note": "each op timed alone, back to back on the same input rotation",
             "reward_to_go": {"us": rtg_ms * 1e3, "bytes": RTG_BYTES,
                              "gbs": RTG_BYTES / (rtg_ms * 1e-3) / 1e9,
@@ -392,6 +473,11 @@ def run_b200(args, world, rank, local):
         line["ops"] = extra
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args)
+    if exchange is not None:
+        torch.cuda.synchronize(dev)
+        barrier(world)  # no rank still stores into another's buffer
+        exchange.close()
+        barrier(world)
     return line
 
 
@@ -566,8 +652,8 @@ def main():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile", default=None,
-                    help="comma list of ops (rl_step, rtg, ppo, lif, robust_l1, kan, fp8_m16, fp8_m1024, fp8_8192, fp8_16384, "
-                         "fp8_ref_timed): run each --steps times for ncu, no timing")
+                    help="comma list of ops (rl_step, rtg, ppo, lif, robust_l1, kan, fp8_m16, fp8_m1024, fp8_8192, "
+                         "fp8_16384, fp8_ref_timed): run each --steps times for ncu, no timing")
     args = ap.parse_args()
     if args.profile:
         run_profile(args.profile.split(","), args.steps)

@@ -45,8 +45,19 @@ SIGNATURES = {
     # fused RL step (reward-to-go + PPO in one launch)
     "b200_rl_step_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p, c_sz,
                                    c_p]),
+    "b200_rl_step_ex_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p, c_sz,
+                                      ctypes.c_uint, c_p]),
     "b200_rl_step_shard_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p,
                                          c_p]),
+    # multi-GPU peer exchange
+    "b200_peer_handle_bytes": (c_sz, []),
+    "b200_rl_step_exchange_record_bytes": (c_sz, []),
+    "b200_peer_next_epoch": (ctypes.c_uint, [ctypes.c_uint]),
+    "b200_peer_exchange_create": (c_int, [c_int, c_int, c_i64, c_sz, c_p, c_p]),
+    "b200_peer_exchange_open": (c_int, [c_p, c_p]),
+    "b200_peer_exchange_destroy": (c_int, [c_p]),
+    "b200_rl_step_exchange_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p,
+                                            c_sz, c_p, ctypes.c_uint, ctypes.c_uint, c_p]),
     # LIF
     "b200_leaky": (None, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p]),
     "b200_leaky_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_p]),

@@ -114,8 +114,18 @@ int b200_rl_step_async(const float* reward, const uint8_t* done, float gamma, in
                        const float* current_log_prob, const float* old_log_prob, const float* advantage,
                        const float* entropy, int64_t n, float clip_epsilon, float* ppo_out, void* workspace,
                        size_t workspace_bytes, void* stream) {
+  return b200_rl_step_ex_async(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy,
+                               n, clip_epsilon, ppo_out, workspace, workspace_bytes, 0u, stream);
+}
+
+int b200_rl_step_ex_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                          float* rtg_out, const float* current_log_prob, const float* old_log_prob,
+                          const float* advantage, const float* entropy, int64_t n, float clip_epsilon, float* ppo_out,
+                          void* workspace, size_t workspace_bytes, unsigned flags, void* stream) {
+  if (flags & ~unsigned(B200_STEP_INPUTS_READY)) return b200::kInvalidArgument;
   return b200::rl::run(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy, n,
-                       clip_epsilon, ppo_out, workspace, workspace_bytes, true, nullptr, as_stream(stream));
+                       clip_epsilon, ppo_out, workspace, workspace_bytes, true, nullptr,
+                       (flags & B200_STEP_INPUTS_READY) != 0, as_stream(stream));
 }
 
 int b200_rl_step_shard_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
@@ -123,7 +133,38 @@ int b200_rl_step_shard_async(const float* reward, const uint8_t* done, float gam
                              const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
                              void* partials, void* stream) {
   return b200::rl::run(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy, n,
-                       clip_epsilon, nullptr, nullptr, 0, false, partials, as_stream(stream));
+                       clip_epsilon, nullptr, nullptr, 0, false, partials, false, as_stream(stream));
+}
+
+// ------------------------------------------------------------- multi-GPU peer exchange (NVLink)
+size_t b200_peer_handle_bytes(void) { return b200::kPeerHandleBytes; }
+size_t b200_rl_step_exchange_record_bytes(void) { return b200::rl::kExchangeRecordBytes; }
+unsigned b200_peer_next_epoch(unsigned epoch) { return b200::peer_next_epoch(epoch); }
+
+int b200_peer_exchange_create(int world, int rank, int64_t slots, size_t record_bytes, void** exchange,
+                              void* handle) {
+  b200::PeerExchange* x = nullptr;
+  const int st = b200::peer_create(world, rank, slots, record_bytes, &x, handle);
+  if (exchange) *exchange = x;
+  return st;
+}
+
+int b200_peer_exchange_open(void* exchange, const void* handles) {
+  return b200::peer_open(static_cast<b200::PeerExchange*>(exchange), handles);
+}
+
+int b200_peer_exchange_destroy(void* exchange) { return b200::peer_destroy(static_cast<b200::PeerExchange*>(exchange)); }
+
+int b200_rl_step_exchange_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                                float* rtg_out, const float* current_log_prob, const float* old_log_prob,
+                                const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
+                                float* ppo_out, void* workspace, size_t workspace_bytes, void* exchange,
+                                unsigned epoch, unsigned flags, void* stream) {
+  if (flags & ~unsigned(B200_STEP_INPUTS_READY)) return b200::kInvalidArgument;
+  return b200::rl::run_exchange(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy,
+                                n, clip_epsilon, ppo_out, workspace, workspace_bytes,
+                                static_cast<const b200::PeerExchange*>(exchange), epoch,
+                                (flags & B200_STEP_INPUTS_READY) != 0, as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------------------- LIF

@@ -40,6 +40,33 @@ inline int launch_status() {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched by launch_pdl may begin while the kernel
+// before it on the stream is still running, as soon as every CTA of that kernel has called
+// pdl_trigger() or exited.  Before its first global write (consecutive launches share output
+// buffers, partial slots and counters) each writing thread calls pdl_wait(), which returns once
+// the previous kernel has completed and its writes are visible.  Reads of inputs no kernel of the
+// sequence writes can go ahead before it.  Both are no-ops in a kernel launched without PDL.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                      const Args&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess ? kOk : kCudaError;
+}
+
+// ---------------------------------------------------------------------------------------------
 // Device properties, cached per device (the SM count sizes persistent grids).
 // ---------------------------------------------------------------------------------------------
 inline int sm_count() {

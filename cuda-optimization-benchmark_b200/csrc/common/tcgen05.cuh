@@ -6,7 +6,7 @@
 // descriptor: start>>4 at 0-13, leading byte offset>>4 at 16-29, stride byte offset>>4 at 32-45,
 // version 1 at 46-47, swizzle mode at 61-63).
 //
-// No TMA load here uses cluster multicast: every CTA loads its own tiles.
+// Every TMA load here is issued by the CTA that uses the tile, for itself alone.
 #pragma once
 
 #include <cuda.h>

@@ -12,7 +12,7 @@
 //   - one persistent CTA per SM walks output tiles of 128 x BN in grouped order (kGroupM row
 //     blocks share each sweep over column blocks, so both operands stay L2-resident);
 //   - warp 0: one thread issues 128-byte-swizzled TMA tile loads of x and w (both K-major) into a
-//     STAGES-deep shared-memory ring (no cluster multicast);
+//     STAGES-deep shared-memory ring (every CTA loads its own tiles);
 //   - warp 1: allocates 2*BN TMEM columns (two fp32 accumulators) and one thread issues
 //     tcgen05.mma kind::f8f6f4 (E4M3 x E4M3 -> fp32, 128 x BN x 32 per instruction), committing
 //     each stage back to the loader and each finished accumulator to the epilogue;

@@ -331,18 +331,25 @@ __device__ __forceinline__ Partial cta_reduce(const Acc& acc) {
   return group_reduce(acc, s_red, threadIdx.x, kRedBar);
 }
 
-// Final combination of partials[0..n_parts) in a fixed order by the kThreads consumer threads;
-// writes 6 (or 7) outputs.  inv_n = 1 / n_total from the host (infinite for an empty batch, which
-// makes every mean NaN, as the mean of nothing is).  Every ratio is > 0, so 0 is the identity of the max.
-__device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, int64_t n_total, double inv_n, bool ext,
-                                       float* out) {
+// Totals of a set of partials: the five sums, the ratio max and the clipped count.
+struct Sums {
+  double t[5];  // gain, lw, r, r2, ent
+  float mx;
+  unsigned long long c;
+};
+
+// Combination of partials[0..n_parts) in a fixed order by the kThreads threads of one CTA (thread
+// t adds partials t, t + kThreads, ... in order, then a warp butterfly, then warp 0..7 in order);
+// the totals are valid in thread 0.  Every ratio is > 0, so 0 is the identity of the max.
+__device__ __forceinline__ Sums reduce_partials(const Partial* parts, int64_t n_parts) {
   __shared__ double s_d[5][kThreads / 32];
   __shared__ float s_max[kThreads / 32];
   __shared__ unsigned long long s_cnt[kThreads / 32];
   double v[5] = {0, 0, 0, 0, 0};
   float m = 0.f;
   unsigned long long cnt = 0;
-  // Four partials per thread per round, loads issued before the adds (one L2 round trip a round).
+  // Four partials per thread per round, loads issued before the adds (one L2 round trip a round;
+  // ld.cg: other CTAs wrote them).
   for (int64_t i0 = threadIdx.x; i0 < n_parts; i0 += 4 * kThreads) {
     double d[4][6];
 #pragma unroll
@@ -376,41 +383,69 @@ __device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, in
     s_cnt[w] = cnt;
   }
   named_sync(kRedBar, kThreads);
+  Sums t{{0, 0, 0, 0, 0}, 0.f, 0ull};
   if (threadIdx.x == 0) {
-    double t[5] = {0, 0, 0, 0, 0};
-    float mx = 0.f;
-    unsigned long long c = 0;
     for (int i = 0; i < kThreads / 32; ++i) {
 #pragma unroll
-      for (int q = 0; q < 5; ++q) t[q] += s_d[q][i];
-      mx = fmaxf(mx, s_max[i]);
-      c += s_cnt[i];
+      for (int q = 0; q < 5; ++q) t.t[q] += s_d[q][i];
+      t.mx = fmaxf(t.mx, s_max[i]);
+      t.c += s_cnt[i];
     }
-    // Means by the host's 1/N (an fp64 divide takes hundreds of cycles on this tail); the ESS ratio
-    // sum(r) / sum(r^2) by one correctly rounded fp32 divide (relative error ~1e-7).
-    out[0] = float(-t[0] * inv_n);
-    out[1] = float(double(c) * inv_n);
-    out[2] = float((t[2] - t[1]) * inv_n - 1.0);
-    out[3] = float((t[2] * inv_n) * double(__fdiv_rn(float(t[2]), float(t[3]))));
-    out[4] = n_total > 0 ? mx : __int_as_float(0x7fc00000);
-    out[5] = float(t[2] * inv_n);
-    if (ext) out[6] = float(t[4] * inv_n);
   }
+  return t;
 }
 
-// Chunk partials of chunks cta, cta + n_ctas, ... (all kThreads threads of the CTA take part).
-template <bool kVec, bool kEnt>
-__device__ __forceinline__ void chunk_partials(const float* __restrict__ cur, const float* __restrict__ old,
-                                               const float* __restrict__ adv, const float* __restrict__ ent, int64_t n,
-                                               const Clip& clip, Partial* __restrict__ partials, int64_t cta,
-                                               int64_t n_ctas) {
+// The 6 (or 7) outputs from the totals over n_total samples (one thread).  inv_n = 1 / n_total
+// from the host (infinite for an empty batch, which makes every mean NaN, as the mean of nothing
+// is).  Means by that 1/N (an fp64 divide takes hundreds of cycles on this tail); the ESS ratio
+// sum(r) / sum(r^2) by one correctly rounded fp32 divide (relative error ~1e-7).
+__device__ __forceinline__ void write_outputs(const Sums& s, int64_t n_total, double inv_n, bool ext, float* out) {
+  out[0] = float(-s.t[0] * inv_n);
+  out[1] = float(double(s.c) * inv_n);
+  out[2] = float((s.t[2] - s.t[1]) * inv_n - 1.0);
+  out[3] = float((s.t[2] * inv_n) * double(__fdiv_rn(float(s.t[2]), float(s.t[3]))));
+  out[4] = n_total > 0 ? s.mx : __int_as_float(0x7fc00000);
+  out[5] = float(s.t[2] * inv_n);
+  if (ext) out[6] = float(s.t[4] * inv_n);
+}
+
+// Final combination of partials[0..n_parts) by the kThreads threads of one CTA; writes the outputs.
+__device__ __forceinline__ void finish(const Partial* parts, int64_t n_parts, int64_t n_total, double inv_n, bool ext,
+                                       float* out) {
+  const Sums s = reduce_partials(parts, n_parts);
+  if (threadIdx.x == 0) write_outputs(s, n_total, inv_n, ext, out);
+}
+
+// Chunk partials of chunks cta, cta + n_ctas, ... (all kThreads threads of the CTA take part);
+// thread 0 hands chunk c's partial to `store(c, p)`, the first time after pdl_wait().
+template <bool kVec, bool kEnt, class Store>
+__device__ __forceinline__ void chunk_partials_to(const float* __restrict__ cur, const float* __restrict__ old,
+                                                  const float* __restrict__ adv, const float* __restrict__ ent,
+                                                  int64_t n, const Clip& clip, const Store& store, int64_t cta,
+                                                  int64_t n_ctas) {
   const int64_t n_chunks = (n + kChunk - 1) / kChunk;
   for (int64_t c = cta; c < n_chunks; c += n_ctas) {
     Acc acc;
     thread_chunk_global<kVec, kEnt>(acc, cur, old, adv, ent, c * kChunk, n, clip);
     const Partial p = cta_reduce(acc);
-    if (threadIdx.x == 0) partials[c] = p;
+    if (threadIdx.x == 0) {
+      if (c == cta) pdl_wait();  // first global write of this CTA (no-op without PDL)
+      store(c, p);
+    }
   }
+}
+
+struct PlainStore {
+  Partial* partials;
+  __device__ __forceinline__ void operator()(int64_t c, const Partial& p) const { partials[c] = p; }
+};
+
+template <bool kVec, bool kEnt>
+__device__ __forceinline__ void chunk_partials(const float* __restrict__ cur, const float* __restrict__ old,
+                                               const float* __restrict__ adv, const float* __restrict__ ent, int64_t n,
+                                               const Clip& clip, Partial* __restrict__ partials, int64_t cta,
+                                               int64_t n_ctas) {
+  chunk_partials_to<kVec, kEnt>(cur, old, adv, ent, n, clip, PlainStore{partials}, cta, n_ctas);
 }
 
 // One launch: CTA c handles chunks c, c + gridDim.x, ...; with kFinish the last CTA to finish

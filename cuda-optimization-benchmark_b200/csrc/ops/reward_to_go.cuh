@@ -273,6 +273,7 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
     land_pass(cur, ecur, s_rb(cb), s_db(cb), &bars[cb], par, lane);
     const double first = scan_pass(cur, s_rb(cb), s_db(cb), carry, g, g_run, gamma, lane);
     const int t0 = t1 > kSeg ? t1 - kSeg : 0;
+    if (k == 0) pdl_wait();  // first global write of this warp (no-op without PDL)
     drain_floats(out + row * int64_t(T) + t0, cur.len, s_rb(cb) + (cur.sr - cur.pr), cur.pr, lane);
     __syncwarp();
     if (!has_next) break;

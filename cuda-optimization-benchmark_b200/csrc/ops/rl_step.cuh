@@ -16,6 +16,7 @@
 #pragma once
 
 #include "../common/b200_common.cuh"
+#include "../common/peer.cuh"
 #include "ppo_clip.cuh"
 #include "reward_to_go.cuh"
 
@@ -50,12 +51,22 @@ struct Args {
   double inv_n;      // 1 / n for the PPO finish
   int64_t rtg_ctas;  // CTAs with the reward-to-go role (kRows rows each per round)
   int64_t ppo_ctas;  // CTAs with the PPO role
+  bool early_reads;  // read the inputs before the previous kernel on the stream completes
 };
+
+// Under PDL the launch may begin before the previous kernel on the stream has finished.  Unless
+// the caller has declared that no kernel of the stream writes the inputs (early_reads), every
+// thread first waits for it, so only the launch latency overlaps; otherwise the loads go ahead and
+// each thread waits just before its first global write.
+__device__ __forceinline__ void step_prologue(const Args& a) {
+  if (!a.early_reads) pdl_wait();
+}
 
 template <bool kVec, bool kEnt, bool kFinish>
 __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_kernel(const Args a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint64_t bars[kRows][2];
+  step_prologue(a);
   const int64_t b = blockIdx.x, G = gridDim.x;
   const int64_t rtg_before = (b * a.rtg_ctas) / G;  // reward-to-go CTAs with a smaller index
   const bool is_rtg = ((b + 1) * a.rtg_ctas) / G > rtg_before;
@@ -68,8 +79,94 @@ __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_kernel(const 
   const int64_t pidx = b - rtg_before;  // index among the PPO CTAs
   ppo::chunk_partials<kVec, kEnt>(a.cur, a.old, a.adv, a.ent, a.n, a.clip, a.partials, pidx, a.ppo_ctas);
   if (kFinish) {
-    if (elect_last_add(a.ticket, 1u, unsigned(a.ppo_ctas)))
+    if (threadIdx.x == 0) pdl_wait();  // the ticket (also when this CTA had no chunk)
+    if (elect_last_add(a.ticket, 1u, unsigned(a.ppo_ctas))) {
+      pdl_trigger();  // the next launch may start while this CTA combines the partials
       ppo::finish(a.partials, ppo::num_chunks(a.n), a.n, a.inv_n, kEnt, a.ppo_out);
+    }
+  }
+}
+
+// The rank record of the multi-GPU step: this rank's PPO totals (ppo::Sums) as 14 words, each
+// stored with the epoch (LL form, 112 bytes).
+constexpr int kRankWords = 14;
+constexpr size_t kExchangeRecordBytes = size_t(kRankWords) * 8;
+
+__device__ __forceinline__ void pack_sums(const ppo::Sums& s, uint32_t (&w)[kRankWords]) {
+#pragma unroll
+  for (int q = 0; q < 5; ++q) {
+    const unsigned long long b = __double_as_longlong(s.t[q]);
+    w[2 * q] = uint32_t(b);
+    w[2 * q + 1] = uint32_t(b >> 32);
+  }
+  w[10] = __float_as_uint(s.mx);
+  w[11] = 0u;
+  w[12] = uint32_t(s.c);
+  w[13] = uint32_t(s.c >> 32);
+}
+
+__device__ __forceinline__ ppo::Sums unpack_sums(const uint32_t (&w)[kRankWords]) {
+  ppo::Sums s;
+#pragma unroll
+  for (int q = 0; q < 5; ++q) s.t[q] = __hiloint2double(int(w[2 * q + 1]), int(w[2 * q]));
+  s.mx = __uint_as_float(w[10]);
+  s.c = (static_cast<unsigned long long>(w[13]) << 32) | w[12];
+  return s;
+}
+
+// Multi-GPU step with the PPO exchange fused in (one launch per rank per step).  Each rank reduces
+// its own chunk partials exactly as the one-GPU step does; the CTA that does so stores the rank's
+// totals, in LL form, into slot `rank` of every rank's buffer (16-byte stores of two {word, epoch}
+// pairs over NVLink; no fence, no flag), reads every rank's totals from its own buffer (thread r
+// reads rank r's, waiting until its epoch has arrived) and adds them in rank order.  Every rank
+// writes the same outputs; with one rank they are bit-identical to the one-GPU step.
+template <bool kVec, bool kEnt>
+__global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_exchange_kernel(const Args a, const PeerView pv) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint64_t bars[kRows][2];
+  __shared__ ppo::Sums s_rank[kMaxPeers];
+  step_prologue(a);
+  const int64_t b = blockIdx.x, G = gridDim.x;
+  const int64_t rtg_before = (b * a.rtg_ctas) / G;
+  const bool is_rtg = ((b + 1) * a.rtg_ctas) / G > rtg_before;
+  if (is_rtg) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    rtg::warp_rows(a.reward, a.done, a.gamma, a.B, a.T, a.rtg_out, rtg_before * kRows + warp, a.rtg_ctas * kRows,
+                   smem + warp * rtg::kWarpSmem, bars[warp], 1, lane);
+    return;
+  }
+  const int64_t pidx = b - rtg_before;
+  ppo::chunk_partials<kVec, kEnt>(a.cur, a.old, a.adv, a.ent, a.n, a.clip, a.partials, pidx, a.ppo_ctas);
+  if (threadIdx.x == 0) pdl_wait();
+  if (!elect_last_add(a.ticket, 1u, unsigned(a.ppo_ctas))) return;
+  pdl_trigger();
+  const ppo::Sums mine = ppo::reduce_partials(a.partials, ppo::num_chunks(a.n));
+  if (threadIdx.x == 0) {
+    uint32_t w[kRankWords];
+    pack_sums(mine, w);
+    for (int r = 0; r < pv.world; ++r) {
+      ulonglong2* rec = peer_record(pv, r, pv.rank, 0);
+#pragma unroll
+      for (int q = 0; q < kRankWords / 2; ++q)
+        ll_store2(rec + q, ll_word(w[2 * q], pv.epoch), ll_word(w[2 * q + 1], pv.epoch));
+    }
+  }
+  if (threadIdx.x < pv.world) {
+    LLReader<kRankWords> rd{peer_record(pv, pv.rank, 0, 0), pv.epoch};
+    uint32_t w[kRankWords];
+    rd.read(threadIdx.x, w);
+    s_rank[threadIdx.x] = unpack_sums(w);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ppo::Sums t = s_rank[0];
+    for (int r = 1; r < pv.world; ++r) {
+#pragma unroll
+      for (int q = 0; q < 5; ++q) t.t[q] += s_rank[r].t[q];
+      t.mx = fmaxf(t.mx, s_rank[r].mx);
+      t.c += s_rank[r].c;
+    }
+    ppo::write_outputs(t, int64_t(pv.world) * a.n, a.inv_n, kEnt, a.ppo_out);
   }
 }
 
@@ -77,8 +174,7 @@ template <bool kVec, bool kEnt, bool kFinish>
 inline int launch(const Args& a, cudaStream_t stream) {
   auto kern = step_kernel<kVec, kEnt, kFinish>;
   if (!ensure_dyn_smem(kern, kSmem)) return kCudaError;
-  kern<<<unsigned(a.rtg_ctas + a.ppo_ctas), kThreads, kSmem, stream>>>(a);
-  return launch_status();
+  return launch_pdl(kern, unsigned(a.rtg_ctas + a.ppo_ctas), kThreads, kSmem, stream, a);
 }
 
 // Split of `slots` CTAs into reward-to-go CTAs and PPO CTAs: the count r of reward-to-go CTAs
@@ -116,14 +212,17 @@ inline void split_roles(int64_t rows, int64_t row_bytes, int64_t chunks, int64_t
 // Both ops in one launch.  PPO workspace: ppo::workspace_bytes(n) (first 4 bytes zero before the
 // first call; left zero).  With finish == false the PPO chunk partials are written to
 // `partials_out` (one ppo::Partial per chunk) and ppo_out is untouched (the multi-GPU shard form).
+// early_reads: the caller declares that the kernel launched just before on the stream writes none
+// of the inputs, so they may be read before it completes.
 inline int run(const float* reward, const unsigned char* done, float gamma, int32_t B, int32_t T, float* rtg_out,
                const float* cur, const float* old, const float* adv, const float* ent, int64_t n, float eps,
                float* ppo_out, void* workspace, size_t ws_bytes, bool finish, void* partials_out,
-               cudaStream_t stream) {
+               bool early_reads, cudaStream_t stream) {
   if (B < 0 || T < 0 || n < 0) return kInvalidArgument;
   if (int64_t(B) * T > 0 && (reward == nullptr || done == nullptr || rtg_out == nullptr)) return kInvalidArgument;
   if (n > 0 && (cur == nullptr || old == nullptr || adv == nullptr)) return kInvalidArgument;
   Args a;
+  a.early_reads = early_reads;
   a.reward = reward;
   a.done = done;
   a.gamma = gamma;
@@ -159,6 +258,52 @@ inline int run(const float* reward, const unsigned char* done, float gamma, int3
   }
   if (ent != nullptr) return vec ? launch<true, true, false>(a, stream) : launch<false, true, false>(a, stream);
   return vec ? launch<true, false, false>(a, stream) : launch<false, false, false>(a, stream);
+}
+
+// The fused multi-GPU step: every rank calls this with its own batch (the same B, T and n on
+// every rank) and the same `epoch` (1 on the first step, peer_next_epoch() of the previous one
+// after); ppo_out receives the PPO outputs of all ranks' samples on every rank.  The exchange must
+// have been created with one slot of kExchangeRecordBytes bytes, and opened.  workspace as for run().
+inline int run_exchange(const float* reward, const unsigned char* done, float gamma, int32_t B, int32_t T,
+                        float* rtg_out, const float* cur, const float* old, const float* adv, const float* ent,
+                        int64_t n, float eps, float* ppo_out, void* workspace, size_t ws_bytes,
+                        const PeerExchange* x, unsigned epoch, bool early_reads, cudaStream_t stream) {
+  if (B < 0 || T < 0 || n < 0 || x == nullptr || ppo_out == nullptr || epoch == 0) return kInvalidArgument;
+  if (int64_t(B) * T > 0 && (reward == nullptr || done == nullptr || rtg_out == nullptr)) return kInvalidArgument;
+  if (n > 0 && (cur == nullptr || old == nullptr || adv == nullptr)) return kInvalidArgument;
+  if (x->slots != 1 || x->rec_bytes != kExchangeRecordBytes || x->world > kMaxPeers) return kInvalidArgument;
+  for (int r = 0; r < x->world; ++r)
+    if (x->base[r] == nullptr) return kInvalidArgument;  // not opened
+  if (workspace == nullptr || ws_bytes < ppo::workspace_bytes(n)) return kWorkspaceTooSmall;
+  Args a;
+  a.early_reads = early_reads;
+  a.reward = reward;
+  a.done = done;
+  a.gamma = gamma;
+  a.B = T > 0 ? int64_t(B) : 0;
+  a.T = T;
+  a.rtg_out = rtg_out;
+  a.cur = cur;
+  a.old = old;
+  a.adv = adv;
+  a.ent = ent;
+  a.n = n;
+  a.clip = ppo::make_clip(eps);
+  a.ticket = static_cast<unsigned*>(workspace);
+  a.partials = reinterpret_cast<ppo::Partial*>(static_cast<char*>(workspace) + 256);
+  a.ppo_out = ppo_out;
+  a.inv_n = ppo::inv_count(int64_t(x->world) * n);
+  const int64_t slots = int64_t(sm_count()) * B200_RL_MIN_CTAS;
+  split_roles(a.B, 9 * int64_t(T), ppo::num_chunks(n), (ent != nullptr ? 16 : 12) * ppo::kChunk, slots, true,
+              &a.rtg_ctas, &a.ppo_ctas);
+  const PeerView pv = peer_view(*x, epoch);
+  const bool vec = aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
+  auto go = [&](auto kern) {
+    if (!ensure_dyn_smem(kern, kSmem)) return int(kCudaError);
+    return launch_pdl(kern, unsigned(a.rtg_ctas + a.ppo_ctas), kThreads, kSmem, stream, a, pv);
+  };
+  if (ent != nullptr) return vec ? go(step_exchange_kernel<true, true>) : go(step_exchange_kernel<false, true>);
+  return vec ? go(step_exchange_kernel<true, false>) : go(step_exchange_kernel<false, false>);
 }
 
 }  // namespace rl

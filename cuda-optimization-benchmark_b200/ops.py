@@ -157,9 +157,16 @@ def reward_to_go(reward, done, gamma, out=None):
 
 
 # ---------------------------------------------------------------------------- fused RL loss step
-def rl_step(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_out=None, ppo_out=None):
+STEP_INPUTS_READY = 1  # B200_STEP_INPUTS_READY
+
+
+def rl_step(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_out=None, ppo_out=None,
+            inputs_ready=False):
     """reward_to_go and ppo_clip on independent inputs in one launch; the same bits as the two
-    separate calls.  Returns (returns [B, T], PPO outputs [6] or [7])."""
+    separate calls.  Returns (returns [B, T], PPO outputs [6] or [7]).
+
+    inputs_ready=True declares that the kernel launched just before on the stream writes none of
+    the inputs, so the step reads them while that kernel finishes (programmatic dependent launch)."""
     _need(reward, "reward", torch.float32)
     dev = reward.device
     _need(done, "done", torch.bool, dev)
@@ -178,9 +185,10 @@ def rl_step(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_
     ppo_out = torch.empty(k, dtype=torch.float32, device=dev) if ppo_out is None else ppo_out
     lib = _lib()
     ws = workspace("ppo", lib.b200_ppo_workspace_bytes(n), dev)
-    _native.check(lib.b200_rl_step_async(_ptr(reward), _ptr(done), float(gamma), B, T, _ptr(rtg_out), _ptr(cur),
-                                         _ptr(old), _ptr(adv), _opt_ptr(entropy, ppo_out), n, float(clip_epsilon),
-                                         _ptr(ppo_out), _ptr(ws), ws.numel(), _stream(dev)), "rl_step")
+    _native.check(lib.b200_rl_step_ex_async(_ptr(reward), _ptr(done), float(gamma), B, T, _ptr(rtg_out), _ptr(cur),
+                                            _ptr(old), _ptr(adv), _opt_ptr(entropy, ppo_out), n, float(clip_epsilon),
+                                            _ptr(ppo_out), _ptr(ws), ws.numel(),
+                                            STEP_INPUTS_READY if inputs_ready else 0, _stream(dev)), "rl_step")
     return rtg_out, ppo_out
 
 
@@ -213,6 +221,74 @@ def rl_step_shard(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None
                                                float(clip_epsilon), _ptr(partials_out), _stream(dev)),
                   "rl_step_shard")
     return rtg_out, partials_out
+
+
+# ------------------------------------------------------- multi-GPU RL step over NVLink peer memory
+class PeerExchange:
+    """The per-rank exchange buffer of the fused multi-GPU RL step (one process per GPU).
+
+    `swap(handle) -> list of handles` must return every rank's 64-byte handle in rank order; with
+    torch.distributed initialised, the default does that with all_gather_object."""
+
+    def __init__(self, world, rank, n, swap=None):
+        lib = _lib()
+        self._ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * lib.b200_peer_handle_bytes())()
+        _native.check(lib.b200_peer_exchange_create(int(world), int(rank), 1, lib.b200_rl_step_exchange_record_bytes(),
+                                                    ctypes.byref(self._ptr), handle), "peer_exchange_create")
+        if swap is None:
+            import torch.distributed as dist
+
+            def swap(h):
+                out = [None] * world
+                dist.all_gather_object(out, h)
+                return out
+        handles = swap(bytes(handle))
+        if len(handles) != world:
+            raise ValueError("swap() must return one handle per rank")
+        blob = b"".join(handles)
+        _native.check(lib.b200_peer_exchange_open(self._ptr, blob), "peer_exchange_open")
+        self.world, self.rank, self.n, self.epoch = world, rank, int(n), 0
+
+    @property
+    def handle(self):
+        return self._ptr
+
+    def close(self):
+        if self._ptr:
+            _native.check(_lib().b200_peer_exchange_destroy(self._ptr), "peer_exchange_destroy")
+            self._ptr = ctypes.c_void_p()
+
+
+def rl_step_exchange(exchange, reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_out=None,
+                     ppo_out=None, inputs_ready=False):
+    """One rank's fused multi-GPU RL step: this rank's returns, and the PPO outputs over every
+    rank's samples (the same bits on every rank).  Every rank must call it the same number of
+    times.  inputs_ready as for rl_step."""
+    _need(reward, "reward", torch.float32)
+    dev = reward.device
+    _need(done, "done", torch.bool, dev)
+    for t, nm in ((cur, "current_log_prob"), (old, "old_log_prob"), (adv, "advantage")):
+        _need(t, nm, torch.float32, dev)
+    if entropy is not None:
+        _need(entropy, "entropy", torch.float32, dev)
+    n = cur.numel()
+    if n != exchange.n:
+        raise ValueError("the exchange was created for a different sample count")
+    B, T = reward.shape
+    rtg_out = torch.empty_like(reward) if rtg_out is None else rtg_out
+    k = 7 if entropy is not None else 6
+    ppo_out = torch.empty(k, dtype=torch.float32, device=dev) if ppo_out is None else ppo_out
+    lib = _lib()
+    ws = workspace("ppo", lib.b200_ppo_workspace_bytes(n), dev)
+    exchange.epoch = lib.b200_peer_next_epoch(exchange.epoch)
+    _native.check(lib.b200_rl_step_exchange_async(_ptr(reward), _ptr(done), float(gamma), B, T, _ptr(rtg_out),
+                                                  _ptr(cur), _ptr(old), _ptr(adv), _opt_ptr(entropy, ppo_out), n,
+                                                  float(clip_epsilon), _ptr(ppo_out), _ptr(ws), ws.numel(),
+                                                  exchange.handle, exchange.epoch,
+                                                  STEP_INPUTS_READY if inputs_ready else 0, _stream(dev)),
+                  "rl_step_exchange")
+    return rtg_out, ppo_out
 
 
 # ----------------------------------------------------------------------------------------- LIF

@@ -138,12 +138,54 @@ int b200_rl_step_async(const float* reward, const uint8_t* done, float gamma, in
                        const float* current_log_prob, const float* old_log_prob, const float* advantage,
                        const float* entropy, int64_t n, float clip_epsilon, float* ppo_out, void* workspace,
                        size_t workspace_bytes, void* stream);
+/* The step kernels are launched with programmatic dependent launch: a step may begin while the
+ * kernel before it on the stream is finishing.  By default it waits for that kernel before reading
+ * anything, so only the launch latency overlaps.  With B200_STEP_INPUTS_READY in `flags` the caller
+ * declares that the kernel launched just before on the stream writes none of this step's inputs
+ * (they were written by copies, or by kernels launched earlier): the inputs are then read while
+ * that kernel finishes, and the step waits only before its own writes.  Steps over resident
+ * batches issued back to back qualify; a step right after the kernel producing its log-probs does
+ * not.  Other flag bits are rejected. */
+#define B200_STEP_INPUTS_READY 1u
+int b200_rl_step_ex_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                          float* rtg_out, const float* current_log_prob, const float* old_log_prob,
+                          const float* advantage, const float* entropy, int64_t n, float clip_epsilon, float* ppo_out,
+                          void* workspace, size_t workspace_bytes, unsigned flags, void* stream);
 /* Multi-GPU shard form: the PPO half writes its per-chunk partials (as b200_ppo_shard_partials)
  * for a cross-GPU gather and b200_ppo_finish. */
 int b200_rl_step_shard_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
                              float* rtg_out, const float* current_log_prob, const float* old_log_prob,
                              const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
                              void* partials, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Multi-GPU RL step with the PPO exchange fused into the kernel (one process per GPU of one node,
+ * NVLink / NVSwitch peer memory through CUDA IPC; no collective library on the step's path).
+ * Each rank creates an exchange (its 64-byte IPC handle comes back in `handle`), the ranks swap
+ * handles over their own channel, and each opens the others' (`handles`: world x 64 bytes in rank
+ * order).  b200_rl_step_exchange_async then runs one rank's step: its own reward-to-go batch and
+ * PPO samples (the same B, T, n on every rank; the exchange created with slots = 1 and
+ * record_bytes = b200_rl_step_exchange_record_bytes()); `epoch` is the same on every rank, 1 on the
+ * first step and b200_peer_next_epoch(previous) after; `flags` as b200_rl_step_ex_async.  Each rank
+ * reduces its own PPO chunk partials exactly as b200_rl_step_async does, stores its totals into
+ * every rank's buffer as 8-byte {word, epoch} values (no fence or flag needed), and adds all ranks'
+ * totals in rank order: every rank's ppo_out receives the same bits, the outputs over all ranks'
+ * samples (with one rank, bit-identical to b200_rl_step_async).  A rank whose totals do not arrive
+ * within 2 s makes the others set bit 0 of the device fault word (b200_last_status after a
+ * synchronize) instead of hanging.
+ * ------------------------------------------------------------------------------------------- */
+size_t b200_peer_handle_bytes(void);
+size_t b200_rl_step_exchange_record_bytes(void);
+unsigned b200_peer_next_epoch(unsigned epoch);
+int b200_peer_exchange_create(int world, int rank, int64_t slots, size_t record_bytes, void** exchange,
+                              void* handle);
+int b200_peer_exchange_open(void* exchange, const void* handles);
+int b200_peer_exchange_destroy(void* exchange);
+int b200_rl_step_exchange_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
+                                float* rtg_out, const float* current_log_prob, const float* old_log_prob,
+                                const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
+                                float* ppo_out, void* workspace, size_t workspace_bytes, void* exchange,
+                                unsigned epoch, unsigned flags, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Leaky integrate-and-fire layer (task leaky).

@@ -3,7 +3,9 @@ same bits as the two separate entry points, at the BASELINE.json configs[1] size
 empty and misaligned shapes, with and without entropy; its shard form gives the same per-chunk
 partials as b200_ppo_shard_partials.  Through that identity the fused step inherits the separate
 ops' oracle parity (tests/test_stream_ops_gpu.py, tests/test_baseline_gpu.py), which is checked
-again here at the full size.
+again here at the full size.  Steps issued back to back with B200_STEP_INPUTS_READY (inputs read
+while the previous step finishes) give the same bits, and so does the multi-GPU exchange step
+run with one rank.
 """
 import ctypes
 
@@ -131,3 +133,71 @@ def test_fused_status_codes(ops):
     assert lib.b200_rl_step_async(p, p, 0.9, 1, 4, p, p, p, p, None, 16, 0.2, out.data_ptr(), p, 8, None) == 4
     # shard form without a partials buffer
     assert lib.b200_rl_step_shard_async(p, p, 0.9, 1, 4, p, p, p, p, None, 16, 0.2, None, None) == 1
+
+
+def test_inputs_ready_back_to_back(ops):
+    """Back-to-back steps over different resident batches, inputs declared ready: each step's
+    outputs equal a step launched alone (the overlap with the previous step changes nothing)."""
+    sets = [make(257, 900, 600_001, seed=40 + i) for i in range(3)]
+    want = []
+    for reward, done, cur, old, adv, ent in sets:
+        r, p = ops.rl_step(reward, done, 0.97, cur, old, adv, 0.2, ent)
+        torch.cuda.synchronize()
+        want.append((r.clone(), p.clone()))
+    outs = [(torch.full_like(sets[i][0], float("nan")), torch.full((7,), float("nan"), device="cuda"))
+            for i in range(3)]
+    for rep in range(4):
+        for i, (reward, done, cur, old, adv, ent) in enumerate(sets):
+            ops.rl_step(reward, done, 0.97, cur, old, adv, 0.2, ent, rtg_out=outs[i][0], ppo_out=outs[i][1],
+                        inputs_ready=True)
+    torch.cuda.synchronize()
+    for (r, p), (wr, wp) in zip(outs, want):
+        assert torch.equal(bits(r), bits(wr))
+        assert torch.equal(bits(p), bits(wp))
+
+
+def test_inputs_ready_after_producer(ops):
+    """Without the declaration a step right after the kernel that writes its inputs reads them
+    only after that kernel completes: the outputs follow the freshly written values."""
+    reward, done, cur, old, adv, ent = make(64, 512, 300_000, seed=9)
+    ref_r, ref_p = ops.rl_step(reward, done, 0.99, cur, old, adv, 0.2, ent)
+    torch.cuda.synchronize()
+    ref_r, ref_p = ref_r.clone(), ref_p.clone()
+    saved_reward, saved_cur = reward.clone(), cur.clone()
+    for _ in range(5):
+        reward.zero_()  # producer kernels on the same stream, right before the step
+        cur.zero_()
+        reward.copy_(saved_reward)
+        cur.copy_(saved_cur)
+        r, p = ops.rl_step(reward, done, 0.99, cur, old, adv, 0.2, ent)
+        torch.cuda.synchronize()
+        assert torch.equal(bits(r), bits(ref_r))
+        assert torch.equal(bits(p), bits(ref_p))
+
+
+@pytest.mark.parametrize("entropy", [True, False], ids=["ent", "noent"])
+def test_exchange_one_rank_matches_step(ops, entropy):
+    """The multi-GPU exchange step with a world of one: the same bits as rl_step, over several
+    epochs (alternating buffer halves), with and without the inputs-ready declaration."""
+    ex = ops.PeerExchange(1, 0, 1_000_003, swap=lambda h: [h])
+    try:
+        for step in range(4):
+            reward, done, cur, old, adv, ent = make(100, 777, 1_000_003, seed=70 + step, entropy=entropy)
+            want_r, want_p = ops.rl_step(reward, done, 0.98, cur, old, adv, 0.2, ent)
+            got_r, got_p = ops.rl_step_exchange(ex, reward, done, 0.98, cur, old, adv, 0.2, ent,
+                                                inputs_ready=bool(step & 1))
+            torch.cuda.synchronize()
+            assert torch.equal(bits(got_r), bits(want_r))
+            assert torch.equal(bits(got_p), bits(want_p))
+        assert pkg().load().b200_device_fault() == 0
+    finally:
+        ex.close()
+
+
+def test_step_flags_rejected(ops):
+    lib = pkg().load()
+    x = torch.zeros(64, device="cuda")
+    out = torch.zeros(8, device="cuda")
+    p = x.data_ptr()
+    assert lib.b200_rl_step_ex_async(p, p, 0.9, 1, 4, p, p, p, p, None, 16, 0.2, out.data_ptr(), p, 4096, 2,
+                                     None) == 1
