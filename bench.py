@@ -64,8 +64,19 @@ def dist_setup(n_gpus):
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # NCCL writes a version banner to file descriptor 1 when its communicator is created; this
+        # run's stdout carries exactly one JSON line, so fd 1 points at stderr until then.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            os.dup2(saved, 1)
+            os.close(saved)
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local

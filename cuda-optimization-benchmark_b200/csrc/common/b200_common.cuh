@@ -49,13 +49,20 @@ inline int launch_status() {
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// First statement of a kernel that reads its inputs only after the previous kernel has completed:
+// wait for it, then let the next launch queue up behind this one (its CTAs take SM slots as this
+// kernel's free up and wait there), which hides the launch latency between back-to-back calls.
+__device__ __forceinline__ void pdl_begin() {
+  pdl_wait();
+  pdl_trigger();
+}
 
 template <typename... KArgs, typename... Args>
-inline int launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                       const Args&... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(block);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -2,17 +2,15 @@
 // NVLink / NVSwitch peer memory (CUDA IPC mappings; plain 16-byte stores and loads, no switch
 // reduction, no collective library).
 //
-// Every rank owns one device buffer of records [2 halves][world][slots], half = epoch & 1.  A
-// record travels in "LL" form: each 4-byte word of the payload is stored together with the epoch
-// as one 8-byte value, which a reader sees whole or not at all, so a word whose epoch field equals
-// the reader's epoch is that epoch's word.  No fence and no separate ready flag are needed, and a
-// record is pushed to every rank the moment it is computed.  Rank `rank` stores its records for
-// epoch e into half (e & 1), slot range of `rank`, of every rank's buffer (its own included); each
-// rank reads all ranks' records from its own buffer, waiting (bounded) on words not yet arrived.
-// The two halves keep a peer's records of epoch e + 1 away from the half still being read for
-// epoch e, and a peer cannot reach e + 2 before it has read this rank's e + 1 records, which this
-// rank stores only after it has finished reading e.  Epochs start at 1 (the buffer starts zeroed)
-// and go up by one a step, skipping 0 on wrap-around without repeating a half.
+// Every rank owns one device buffer of records [2 halves][world][slots], half = epoch & 1.  Records
+// travel in LL form (ll.cuh): every 4-byte word with the epoch in one 8-byte value, so a record is
+// pushed to a peer the moment it is computed, with no fence and no ready flag.  Rank `rank` stores
+// its records for epoch e into half (e & 1), slot range of `rank`, of the other ranks' buffers;
+// each rank reads the others' records from its own buffer, waiting (bounded) on words not yet
+// arrived.  The two halves keep a peer's records of epoch e + 1 away from the half still being
+// read for epoch e, and a peer cannot reach e + 2 before it has read this rank's e + 1 records,
+// which this rank stores only after it has finished reading e.  Epochs start at 1 (the buffer
+// starts zeroed) and go up by one a step, skipping 0 on wrap-around without repeating a half.
 //
 // The ranks exchange their 64-byte CUDA IPC handles through the caller's own channel (the Python
 // side uses torch.distributed) and open one another's buffers with peer_open().
@@ -24,6 +22,7 @@
 
 #include "b200_common.cuh"
 #include "bulk.cuh"
+#include "ll.cuh"
 
 namespace b200 {
 
@@ -118,69 +117,6 @@ __device__ __forceinline__ ulonglong2* peer_record(const PeerView& v, int r, int
   return reinterpret_cast<ulonglong2*>(v.base[r] + size_t(v.epoch & 1u) * v.half_bytes +
                                   (size_t(owner) * v.slots + i) * v.rec_bytes);
 }
-
-// LL words: a 4-byte payload word in the low half and the epoch in the high half of one 8-byte
-// value.  Each 64-bit element of a vector access is a single-copy-atomic access of its own, so a
-// reader sees a word and its epoch together; two words move per 16-byte access (volatile: neither
-// kept in L1 nor merged with other accesses).
-__device__ __forceinline__ unsigned long long ll_word(uint32_t word, uint32_t epoch) {
-  return (static_cast<unsigned long long>(epoch) << 32) | word;
-}
-__device__ __forceinline__ void ll_store2(ulonglong2* p, unsigned long long a, unsigned long long b) {
-  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
-}
-__device__ __forceinline__ ulonglong2 ll_load2(const ulonglong2* p) {
-  ulonglong2 v;
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ bool ll_fresh(unsigned long long v, uint32_t epoch) { return uint32_t(v >> 32) == epoch; }
-
-// Reader of LL records of kWords payload words (kWords even; 16-byte aligned records) that arrive
-// from other GPUs.  One per thread: a thread waits at most kWaitLimitNs in all (from its first
-// wait); past that it records kFaultWaitTimeout and takes whatever the words hold, so the kernel
-// always ends and the host sees the fault.
-template <int kWords>
-struct LLReader {
-  static_assert(kWords % 2 == 0, "records are whole 16-byte pairs of LL words");
-  static constexpr int kPairs = kWords / 2;
-  const ulonglong2* recs;  // record 0
-  unsigned epoch;
-  unsigned long long t0 = 0;
-  bool dead = false;
-
-  __device__ __forceinline__ void read(int64_t i, uint32_t (&w)[kWords]) {
-    const ulonglong2* p = recs + i * kPairs;
-    ulonglong2 v[kPairs];
-    bool ok = true;
-#pragma unroll
-    for (int q = 0; q < kPairs; ++q) {
-      v[q] = ll_load2(p + q);
-      ok &= ll_fresh(v[q].x, epoch) & ll_fresh(v[q].y, epoch);
-    }
-    if (!ok && !dead) {
-      if (t0 == 0) t0 = global_ns();
-      do {  // re-read the pairs still stale (static indices: v stays in registers)
-        if (global_ns() - t0 > kWaitLimitNs) {
-          atomicOr(&g_b200_fault, kFaultWaitTimeout);
-          dead = true;
-          break;
-        }
-        ok = true;
-#pragma unroll
-        for (int q = 0; q < kPairs; ++q) {
-          if (!(ll_fresh(v[q].x, epoch) & ll_fresh(v[q].y, epoch))) v[q] = ll_load2(p + q);
-          ok &= ll_fresh(v[q].x, epoch) & ll_fresh(v[q].y, epoch);
-        }
-      } while (!ok);
-    }
-#pragma unroll
-    for (int q = 0; q < kPairs; ++q) {
-      w[2 * q] = uint32_t(v[q].x);
-      w[2 * q + 1] = uint32_t(v[q].y);
-    }
-  }
-};
 
 // The epoch after e: e + 1, with 0 (the zeroed buffer's value) skipped by going on to 2, which
 // keeps the halves alternating (0xffffffff is odd, 2 is even).

@@ -1,13 +1,13 @@
 // Per-device scratch arena for the drop-in (`void reference(...)`-shaped) entry points.
 //
 // The reference ABI gives a kernel no workspace argument (tasks/FORMAT.md:35), so ops that need
-// scratch (grid-reduction partials, a completion counter) take it from this arena.  The arena is
+// scratch (grid-reduction partials and their control words) take it from this arena.  The arena is
 // allocated with cudaMalloc on the first call on a device, grows when a larger call needs it, and
 // is never freed before process exit; after the first call at a given size a call performs no
 // allocation.  Fresh memory is zero-filled on the caller's stream before first use.
 //
 // Each op has its own slot (ArenaClient), because ops keep state in their scratch between calls
-// (the reductions' completion counter must stay zero between calls).  Calls of one op that share
+// (the reductions' control words carry over from one call to the next).  Calls of one op that share
 // its slot must not overlap on the GPU: issue them on one stream, or order them with events.
 // The stream forms in the C ABI that take a caller workspace have no such restriction beyond the
 // usual one for the workspace they are given.

@@ -100,6 +100,7 @@ template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
                 float scale, const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int vec_ok) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   using C = Cfg<BN>;
   constexpr int S = C::kStages;
 #if !B200_TCGEN05
@@ -226,6 +227,7 @@ __device__ __forceinline__ float e4m3_value(unsigned b) {
 __global__ void __launch_bounds__(256) simt_kernel(int M, int N, int K, const uint8_t* __restrict__ x,
                                                    const uint8_t* __restrict__ w, float scale,
                                                    const uint16_t* __restrict__ bias, uint16_t* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   __shared__ float lut[256];
   __shared__ float xs[32][65], ws[32][65];
   lut[threadIdx.x] = e4m3_value(threadIdx.x);
@@ -325,7 +327,7 @@ inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, fl
   const int n_tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   const int vec_ok = (N % 8 == 0) && aligned16(out);
-  kern<<<grid, kThreads, Cfg<BN>::kSmem, stream>>>(a, b, M, N, K, scale, bias, out, vec_ok);
+  launch_pdl(kern, grid, kThreads, Cfg<BN>::kSmem, stream, a, b, M, N, K, scale, bias, out, vec_ok);
   return launch_status();
 }
 
@@ -350,7 +352,7 @@ inline int run(int32_t M, int32_t K, int32_t N, const uint8_t* x, float sx, cons
   if (bn == 128) return launch_tc<128>(M, N, K, x, w, scale, bias, out, stream);
   if (bn == 64) return launch_tc<64>(M, N, K, x, w, scale, bias, out, stream);
   dim3 grid((N + 63) / 64, (M + 63) / 64);
-  simt_kernel<<<grid, 256, 0, stream>>>(M, N, K, x, w, scale, bias, out);
+  launch_pdl(simt_kernel, grid, 256, 0, stream, M, N, K, x, w, scale, bias, out);
   return launch_status();
 }
 
@@ -361,7 +363,7 @@ inline int run_simt(int32_t M, int32_t K, int32_t N, const uint8_t* x, float sx,
   if (M == 0 || N == 0) return kOk;
   const float scale = float(1.0 / (double(sx) * double(sw)));
   dim3 grid((N + 63) / 64, (M + 63) / 64);
-  simt_kernel<<<grid, 256, 0, stream>>>(M, N, K, x, w, scale, bias, out);
+  launch_pdl(simt_kernel, grid, 256, 0, stream, M, N, K, x, w, scale, bias, out);
   return launch_status();
 }
 

@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(256) prep_w_kernel(const float* __restrict__ w
                                                      const float* __restrict__ sc, int I, int O, int C, int64_t kp,
                                                      __half* __restrict__ w_hi, __half* __restrict__ w_lo,
                                                      float* __restrict__ cs) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   __shared__ float s_red[33];
   const int o = blockIdx.x;
   const float* wbr = wb + int64_t(o) * I;
@@ -249,6 +250,7 @@ template <int NK, int KO>
 __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x, const float* __restrict__ grid,
                                                      int I, int C, int K, int64_t kp, __half* __restrict__ a_hi,
                                                      __half* __restrict__ a_lo, float* __restrict__ rs) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   __shared__ float s_red[33];
   const int bi = blockIdx.x;
   const int nk = NK > 0 ? NK : C + K + 1;
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                 const __grid_constant__ CUtensorMap tm_whi, const __grid_constant__ CUtensorMap tm_wlo, int M, int N,
                 int64_t kp, const float* __restrict__ rs, const float* __restrict__ cs, float* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
 #if !B200_TCGEN05
   if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
   return;
@@ -470,10 +473,10 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   float* rs = reinterpret_cast<float*>(w + L.rs);
   float* cs = reinterpret_cast<float*>(w + L.cs);
   const int64_t kp = padded_k(I, C);
-  prep_w_kernel<<<O, 256, 0, stream>>>(wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
-  if (G == 5 && K == 3) prep_a_kernel<12, 3><<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
-  else if (G == 8 && K == 3) prep_a_kernel<15, 3><<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
-  else prep_a_kernel<0, 0><<<B, 256, 0, stream>>>(x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  launch_pdl(prep_w_kernel, O, 256, 0, stream, wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
+  if (G == 5 && K == 3) launch_pdl(prep_a_kernel<12, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  else if (G == 8 && K == 3) launch_pdl(prep_a_kernel<15, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  else launch_pdl(prep_a_kernel<0, 0>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
   CUtensorMap m_ahi, m_alo, m_whi, m_wlo;
   if (!tc::make_map_sw128(&m_ahi, a_hi, uint64_t(B), uint64_t(kp), 2, kBM) ||
       !tc::make_map_sw128(&m_alo, a_lo, uint64_t(B), uint64_t(kp), 2, kBM) ||
@@ -483,7 +486,7 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   if (!ensure_dyn_smem(gemm_kernel, kSmem)) return kCudaError;
   const int n_tiles = ((B + kBM - 1) / kBM) * ((O + kBN - 1) / kBN);
   const int grid_ctas = n_tiles < sm_count() ? n_tiles : sm_count();
-  gemm_kernel<<<grid_ctas, kThreads, kSmem, stream>>>(m_ahi, m_alo, m_whi, m_wlo, B, O, kp, rs, cs, out);
+  launch_pdl(gemm_kernel, grid_ctas, kThreads, kSmem, stream, m_ahi, m_alo, m_whi, m_wlo, B, O, kp, rs, cs, out);
   return launch_status();
 }
 

@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restri
                                                           const float* __restrict__ th, int T, int64_t NB, int H,
                                                           int S, int depth, float* __restrict__ spikes,
                                                           float* __restrict__ final_mem) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   extern __shared__ __align__(128) float sm[];
   __shared__ uint64_t full[kMaxDepth];
   float* xr = sm;                  // depth slices of S floats
@@ -116,6 +117,7 @@ __global__ void __launch_bounds__(kThreads) lif_scalar_kernel(const float* __res
                                                               const float* __restrict__ th, int T, int64_t NB, int H,
                                                               float* __restrict__ spikes,
                                                               float* __restrict__ final_mem) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   const int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x;
   if (i >= NB) return;
   float m = mem0[i];
@@ -161,13 +163,13 @@ inline int run(const float* x, const float* mem0, const float* beta, const float
     if (depth < 2) depth = 2;
     const size_t smem = size_t(depth + kOut) * size_t(S) * 4;
     if (!ensure_dyn_smem(lif_slab_kernel, int(smem))) return kCudaError;
-    lif_slab_kernel<<<unsigned(grid), unsigned(S / 4), smem, stream>>>(x, mem0, beta, th, T, NB, H, int(S), depth,
-                                                                       spikes, final_mem);
+    return launch_pdl(lif_slab_kernel, unsigned(grid), unsigned(S / 4), smem, stream, x, mem0, beta, th, T, NB, H,
+                      int(S), depth, spikes, final_mem);
   } else {
     const int64_t grid = (NB + kThreads - 1) / kThreads;
-    lif_scalar_kernel<<<unsigned(grid), kThreads, 0, stream>>>(x, mem0, beta, th, T, NB, H, spikes, final_mem);
+    return launch_pdl(lif_scalar_kernel, unsigned(grid), kThreads, 0, stream, x, mem0, beta, th, T, NB, H, spikes,
+                      final_mem);
   }
-  return launch_status();
 }
 
 }  // namespace lif

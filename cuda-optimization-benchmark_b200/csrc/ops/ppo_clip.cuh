@@ -21,10 +21,14 @@
 // thread streams 4 float4 of every input (one of each at a time, 64 registers, 4 CTAs per SM)
 // with 128-bit non-allocating loads, accumulates in fp32,
 // each warp folds its lanes into one fp32 record, and the 8 records are combined in fp64 into a
-// 48-byte chunk partial; the last CTA to finish combines the partials in chunk order.  The result
-// is bit-identical for any grid, any pointer alignment, and any chunk-aligned split of the range
-// across GPUs (the multi-GPU path gathers the same partials and runs the same finish), and the
-// fused reward-to-go + PPO step kernel reuses the same per-chunk routine.  The clip decision
+// 48-byte chunk partial.  In the one-launch form of the PPO entry points each chunk partial is
+// stored in LL form (every word with the launch's epoch) and the first CTA to reach its last chunk
+// becomes the reducer: it folds the partials in chunk order as they arrive, so when the last chunk
+// lands only about one L2 round trip remains.  (The fused RL step, where it measured slower, keeps
+// plain partials and lets the last CTA to finish combine them, in the same order.)  The result is bit-identical for any grid, any pointer alignment, and any
+// chunk-aligned split of the range across GPUs (the multi-GPU path gathers the same partials and
+// runs the same combination), and the fused reward-to-go + PPO step kernel reuses the same
+// per-chunk routine.  The clip decision
 // matches the fp64 oracle exactly: it is taken in fp32 and re-taken in fp64 for elements within
 // a few ulps of a clip boundary (Clip::margin).  Elements with lw > 30 (outside the reference's stated input range,
 // where r^2 could overflow fp32 sums) take an fp64 path.
@@ -34,6 +38,7 @@
 
 #include "../common/b200_common.cuh"
 #include "../common/bulk.cuh"
+#include "../common/ll.cuh"
 #include "../common/workspace.cuh"
 
 namespace b200 {
@@ -80,7 +85,31 @@ inline Clip make_clip(float eps) {
 }
 
 __host__ __device__ inline int64_t num_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
-inline size_t workspace_bytes(int64_t n) { return 256 + align256(size_t(num_chunks(n)) * sizeof(Partial)); }
+
+// Workspace of the one-launch forms: a 256-byte control block, then one plain 48-byte partial per
+// chunk, then one 96-byte LL chunk record per chunk.  The control block must be zero before the
+// first launch on it.
+//   - ticket: completion counter of the last-CTA election (the fused RL step); left zero.
+//   - claim, gen: the reducer claim and last epoch of the LL form (the PPO entry points); each
+//     launch leaves `claim` zero and `gen` at its epoch, and the next launch's records carry
+//     gen + 1, so no record of an earlier launch reads as fresh until the 32-bit counter wraps,
+//     2^32 launches later.
+// The two forms keep their records apart: a stale plain partial never meets an LL reader.
+struct Control {
+  unsigned ticket;
+  unsigned claim;  // 1 once a CTA has become this launch's reducer
+  unsigned gen;    // epoch of the last completed launch
+};
+constexpr int kPartWords = int(sizeof(Partial) / 4);          // 12
+constexpr size_t kLLPartBytes = size_t(kPartWords) * 8;        // 96
+inline size_t plain_region_bytes(int64_t n) { return align256(size_t(num_chunks(n)) * sizeof(Partial)); }
+inline Partial* ws_partials(void* ws) { return reinterpret_cast<Partial*>(static_cast<char*>(ws) + 256); }
+inline ulonglong2* ws_records(void* ws, int64_t n) {
+  return reinterpret_cast<ulonglong2*>(static_cast<char*>(ws) + 256 + plain_region_bytes(n));
+}
+inline size_t workspace_bytes(int64_t n) {
+  return 256 + plain_region_bytes(n) + align256(size_t(num_chunks(n)) * kLLPartBytes);
+}
 
 struct Acc {
   float gain = 0.f, lw = 0.f, r = 0.f, r2 = 0.f, ent = 0.f, rmax = 0.f;
@@ -338,49 +367,37 @@ struct Sums {
   unsigned long long c;
 };
 
-// Combination of partials[0..n_parts) in a fixed order by the kThreads threads of one CTA (thread
-// t adds partials t, t + kThreads, ... in order, then a warp butterfly, then warp 0..7 in order);
-// the totals are valid in thread 0.  Every ratio is > 0, so 0 is the identity of the max.
-__device__ __forceinline__ Sums reduce_partials(const Partial* parts, int64_t n_parts) {
-  __shared__ double s_d[5][kThreads / 32];
-  __shared__ float s_max[kThreads / 32];
-  __shared__ unsigned long long s_cnt[kThreads / 32];
+// Thread t accumulates records t, t + kThreads, ... in order (kU per round, loads issued before the
+// adds); combine_threads then adds each warp's lanes by a butterfly and the 8 warps in order.  The
+// totals are valid in thread 0.  Every ratio is > 0, so 0 is the identity of the max.
+struct ThreadSums {
   double v[5] = {0, 0, 0, 0, 0};
   float m = 0.f;
   unsigned long long cnt = 0;
-  // Four partials per thread per round, loads issued before the adds (one L2 round trip a round;
-  // ld.cg: other CTAs wrote them).
-  for (int64_t i0 = threadIdx.x; i0 < n_parts; i0 += 4 * kThreads) {
-    double d[4][6];
+  __device__ __forceinline__ void add(const double (&d)[6]) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int64_t i = i0 + int64_t(u) * kThreads;
-      const double* pd = reinterpret_cast<const double*>(parts + (i < n_parts ? i : 0));
-#pragma unroll
-      for (int q = 0; q < 6; ++q) d[u][q] = i < n_parts ? ld_cg_f64(pd + q) : 0.0;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (i0 + int64_t(u) * kThreads < n_parts) {
-#pragma unroll
-        for (int q = 0; q < 5; ++q) v[q] += d[u][q];
-        const unsigned long long w = __double_as_longlong(d[u][5]);
-        m = fmaxf(m, __uint_as_float(unsigned(w & 0xffffffffull)));
-        cnt += unsigned(w >> 32);
-      }
-    }
+    for (int q = 0; q < 5; ++q) v[q] += d[q];
+    const unsigned long long w = __double_as_longlong(d[5]);
+    m = fmaxf(m, __uint_as_float(unsigned(w & 0xffffffffull)));
+    cnt += unsigned(w >> 32);
   }
+};
+
+__device__ __forceinline__ Sums combine_threads(ThreadSums a) {
+  __shared__ double s_d[5][kThreads / 32];
+  __shared__ float s_max[kThreads / 32];
+  __shared__ unsigned long long s_cnt[kThreads / 32];
 #pragma unroll
-  for (int q = 0; q < 5; ++q) v[q] = warp_sum(v[q]);
-  m = warp_max(m);
+  for (int q = 0; q < 5; ++q) a.v[q] = warp_sum(a.v[q]);
+  a.m = warp_max(a.m);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  for (int o = 16; o > 0; o >>= 1) a.cnt += __shfl_xor_sync(0xffffffffu, a.cnt, o);
   const int w = threadIdx.x >> 5;
   if ((threadIdx.x & 31) == 0) {
 #pragma unroll
-    for (int q = 0; q < 5; ++q) s_d[q][w] = v[q];
-    s_max[w] = m;
-    s_cnt[w] = cnt;
+    for (int q = 0; q < 5; ++q) s_d[q][w] = a.v[q];
+    s_max[w] = a.m;
+    s_cnt[w] = a.cnt;
   }
   named_sync(kRedBar, kThreads);
   Sums t{{0, 0, 0, 0, 0}, 0.f, 0ull};
@@ -393,6 +410,61 @@ __device__ __forceinline__ Sums reduce_partials(const Partial* parts, int64_t n_
     }
   }
   return t;
+}
+
+__device__ __forceinline__ void partial_words(const Partial& p, uint32_t (&w)[kPartWords]) { memcpy(w, &p, sizeof(p)); }
+__device__ __forceinline__ void words_to_doubles(const uint32_t (&w)[kPartWords], double (&d)[6]) {
+#pragma unroll
+  for (int q = 0; q < 6; ++q) d[q] = __hiloint2double(int(w[2 * q + 1]), int(w[2 * q]));
+}
+
+// Combination of partials[0..n_parts) (all written before this launch or by CTAs that have
+// finished) by the kThreads threads of one CTA.
+__device__ __forceinline__ Sums reduce_partials(const Partial* parts, int64_t n_parts) {
+  ThreadSums a;
+  for (int64_t i0 = threadIdx.x; i0 < n_parts; i0 += 4 * kThreads) {
+    double d[4][6];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t i = i0 + int64_t(u) * kThreads;
+      const double* pd = reinterpret_cast<const double*>(parts + (i < n_parts ? i : 0));
+#pragma unroll
+      for (int q = 0; q < 6; ++q) d[u][q] = i < n_parts ? ld_cg_f64(pd + q) : 0.0;  // L2: other CTAs wrote them
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i0 + int64_t(u) * kThreads < n_parts) a.add(d[u]);
+  }
+  return combine_threads(a);
+}
+
+// The same combination over LL chunk records of this launch's epoch that are still arriving: each
+// thread waits (bounded) for the records it adds, in its fixed order.
+// kU records in flight per thread (24 registers of loads each).
+template <int kU>
+__device__ __forceinline__ Sums reduce_arriving(const ulonglong2* recs, int64_t n_parts, unsigned epoch) {
+  ThreadSums a;
+  LLReader<kPartWords, LLScope::kGpu> rd{recs, epoch};  // records of this grid's CTAs
+  for (int64_t i0 = threadIdx.x; i0 < n_parts; i0 += kU * kThreads) {
+    int64_t idx[kU];
+    bool use[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      idx[u] = i0 + int64_t(u) * kThreads;
+      use[u] = idx[u] < n_parts;
+    }
+    uint32_t w[kU][kPartWords];
+    rd.read<kU>(idx, use, w);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (use[u]) {
+        double d[6];
+        words_to_doubles(w[u], d);
+        a.add(d);
+      }
+    }
+  }
+  return combine_threads(a);
 }
 
 // The 6 (or 7) outputs from the totals over n_total samples (one thread).  inv_n = 1 / n_total
@@ -448,59 +520,138 @@ __device__ __forceinline__ void chunk_partials(const float* __restrict__ cur, co
   chunk_partials_to<kVec, kEnt>(cur, old, adv, ent, n, clip, PlainStore{partials}, cta, n_ctas);
 }
 
-// One launch: CTA c handles chunks c, c + gridDim.x, ...; with kFinish the last CTA to finish
-// combines every partial.  kVec: 128-bit loads for full chunks (16-byte aligned inputs).
-template <bool kVec, bool kEnt, bool kFinish>
-__global__ void __launch_bounds__(kThreads, 4) chunk_kernel(const float* __restrict__ cur, const float* __restrict__ old,
-                                                         const float* __restrict__ adv, const float* __restrict__ ent,
-                                                         int64_t n, Clip clip, Partial* __restrict__ partials,
-                                                         unsigned* __restrict__ ticket, double inv_n,
-                                                         float* __restrict__ out) {
-  chunk_partials<kVec, kEnt>(cur, old, adv, ent, n, clip, partials, blockIdx.x, gridDim.x);
-  if (kFinish) {
-    if (elect_last_cta(ticket)) finish(partials, (n + kChunk - 1) / kChunk, n, inv_n, kEnt, out);
+// The one-launch form's epoch: once the previous kernel on the stream has completed (so the last
+// launch's `gen` is visible and its claim reset), gen + 1, skipping 0.  By thread 0.
+__device__ __forceinline__ unsigned open_epoch(Control* ctl) {
+  pdl_wait();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(&ctl->gen) + 1u;
+  return e == 0u ? 1u : e;
+}
+
+// By the reducer's thread 0 when the launch's outputs are written: the control block is ready for
+// the next launch (which reads it only after this one has completed).
+__device__ __forceinline__ void close_epoch(Control* ctl, unsigned epoch) {
+  *reinterpret_cast<volatile unsigned*>(&ctl->claim) = 0u;
+  *reinterpret_cast<volatile unsigned*>(&ctl->gen) = epoch;
+}
+
+// One-launch form of chunk_partials: the partials of chunks cta, cta + n_ctas, ... go to `recs` in
+// LL form with the launch's epoch.  Thread 0 claims the reduction before it stores its CTA's last
+// chunk (a CTA without a chunk, only the single CTA of an empty batch, claims at once), so the
+// claim is taken exactly once, and before the reducer can have seen every record.  Returns true
+// in the claiming CTA; *epoch receives the launch's epoch (all threads).
+template <bool kVec, bool kEnt>
+__device__ __forceinline__ bool chunk_records(const float* __restrict__ cur, const float* __restrict__ old,
+                                              const float* __restrict__ adv, const float* __restrict__ ent, int64_t n,
+                                              const Clip& clip, ulonglong2* __restrict__ recs, Control* ctl,
+                                              int64_t cta, int64_t n_ctas, unsigned* epoch) {
+  __shared__ unsigned s_epoch, s_claim;
+  const int64_t n_chunks = num_chunks(n);
+  unsigned e = 0;
+  bool claimed = false;
+  for (int64_t c = cta; c < n_chunks; c += n_ctas) {
+    Acc acc;
+    thread_chunk_global<kVec, kEnt>(acc, cur, old, adv, ent, c * kChunk, n, clip);
+    const Partial p = cta_reduce(acc);
+    if (threadIdx.x == 0) {
+      if (e == 0) e = open_epoch(ctl);
+      if (c + n_ctas >= n_chunks) claimed = atomicCAS(&ctl->claim, 0u, 1u) == 0u;
+      uint32_t w[kPartWords];
+      partial_words(p, w);
+      ll_store_record<kPartWords, LLScope::kGpu>(recs + c * (kPartWords / 2), w, e);
+    }
   }
+  if (threadIdx.x == 0) {
+    if (e == 0) {
+      e = open_epoch(ctl);
+      claimed = atomicCAS(&ctl->claim, 0u, 1u) == 0u;
+    }
+    s_epoch = e;
+    s_claim = claimed ? 1u : 0u;
+  }
+  __syncthreads();
+  *epoch = s_epoch;
+  return s_claim != 0u;
+}
+
+// One launch of the whole op (CTA c handles chunks c, c + gridDim.x, ...; the grid is one resident
+// wave, so the reducer's waits always end).  kVec: 128-bit loads for full chunks (16-byte aligned
+// inputs).
+template <bool kVec, bool kEnt>
+__global__ void __launch_bounds__(kThreads, 4) loss_kernel(const float* __restrict__ cur, const float* __restrict__ old,
+                                                        const float* __restrict__ adv, const float* __restrict__ ent,
+                                                        int64_t n, Clip clip, ulonglong2* __restrict__ recs,
+                                                        Control* __restrict__ ctl, double inv_n,
+                                                        float* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  unsigned epoch;
+  if (!chunk_records<kVec, kEnt>(cur, old, adv, ent, n, clip, recs, ctl, blockIdx.x, gridDim.x, &epoch)) return;
+  const Sums s = reduce_arriving<1>(recs, num_chunks(n), epoch);  // 64 registers at 4 CTAs per SM
+  if (threadIdx.x == 0) {
+    write_outputs(s, n, inv_n, kEnt, out);
+    close_epoch(ctl, epoch);
+  }
+}
+
+// Chunk partials only (the multi-GPU shard form), plain 48-byte records.
+template <bool kVec, bool kEnt>
+__global__ void __launch_bounds__(kThreads, 4) partials_kernel(const float* __restrict__ cur,
+                                                            const float* __restrict__ old,
+                                                            const float* __restrict__ adv,
+                                                            const float* __restrict__ ent, int64_t n, Clip clip,
+                                                            Partial* __restrict__ partials) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  chunk_partials<kVec, kEnt>(cur, old, adv, ent, n, clip, partials, blockIdx.x, gridDim.x);
 }
 
 __global__ void __launch_bounds__(kThreads) finish_kernel(const Partial* __restrict__ partials, int64_t n_parts,
                                                           int64_t n_total, double inv_n, int ext,
                                                           float* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   finish(partials, n_parts, n_total, inv_n, ext != 0, out);
 }
 
 inline double inv_count(int64_t n) { return 1.0 / double(n); }
 
-template <bool kVec, bool kEnt, bool kFinish>
-inline void launch_direct(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
-                          const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
-  auto kern = chunk_kernel<kVec, kEnt, kFinish>;
+template <bool kVec, bool kEnt>
+inline void launch_loss(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
+                        const Clip& clip, ulonglong2* recs, Control* ctl, float* out, cudaStream_t stream) {
+  auto kern = loss_kernel<kVec, kEnt>;
   const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
-  kern<<<grid, kThreads, 0, stream>>>(cur, old, adv, ent, n, clip, partials, ticket, inv_count(n), out);
+  launch_pdl(kern, grid, kThreads, 0, stream, cur, old, adv, ent, n, clip, recs, ctl, inv_count(n), out);
 }
 
-template <bool kFinish>
-inline void launch_chunks(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
-                          const Clip& clip, Partial* partials, unsigned* ticket, float* out, cudaStream_t stream) {
-  const bool vec = aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
-  if (ent != nullptr) {
-    if (vec) launch_direct<true, true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-    else launch_direct<false, true, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-  } else {
-    if (vec) launch_direct<true, false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-    else launch_direct<false, false, kFinish>(cur, old, adv, ent, n, clip, partials, ticket, out, stream);
-  }
+template <bool kVec, bool kEnt>
+inline void launch_partials(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
+                            const Clip& clip, Partial* partials, cudaStream_t stream) {
+  auto kern = partials_kernel<kVec, kEnt>;
+  const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
+  launch_pdl(kern, grid, kThreads, 0, stream, cur, old, adv, ent, n, clip, partials);
 }
 
-// Full op with a caller workspace (workspace_bytes(n), first 4 bytes zero before the first call).
-// `ent` may be null (6 outputs) or an entropy stream (7 outputs).
+inline bool vec_ok(const float* cur, const float* old, const float* adv, const float* ent) {
+  return aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
+}
+
+// Full op with a caller workspace (workspace_bytes(n); its control block zero before the first
+// call, as every call leaves it ready for the next), in one launch with the progressive reducer.  `ent` may be null (6 outputs) or an entropy
+// stream (7 outputs).
 inline int run(const float* cur, const float* old, const float* adv, const float* ent, int64_t n, float eps,
                float* out, void* workspace, size_t ws_bytes, cudaStream_t stream) {
   if (n < 0 || out == nullptr || (n > 0 && (cur == nullptr || old == nullptr || adv == nullptr)))
     return kInvalidArgument;
   if (workspace == nullptr || ws_bytes < workspace_bytes(n)) return kWorkspaceTooSmall;
-  unsigned* ticket = static_cast<unsigned*>(workspace);
-  Partial* partials = reinterpret_cast<Partial*>(static_cast<char*>(workspace) + 256);
-  launch_chunks<true>(cur, old, adv, ent, n, make_clip(eps), partials, ticket, out, stream);
+  Control* ctl = static_cast<Control*>(workspace);
+  ulonglong2* recs = ws_records(workspace, n);
+  const Clip clip = make_clip(eps);
+  const bool vec = vec_ok(cur, old, adv, ent);
+  if (ent != nullptr) {
+    if (vec) launch_loss<true, true>(cur, old, adv, ent, n, clip, recs, ctl, out, stream);
+    else launch_loss<false, true>(cur, old, adv, ent, n, clip, recs, ctl, out, stream);
+  } else {
+    if (vec) launch_loss<true, false>(cur, old, adv, ent, n, clip, recs, ctl, out, stream);
+    else launch_loss<false, false>(cur, old, adv, ent, n, clip, recs, ctl, out, stream);
+  }
   return launch_status();
 }
 
@@ -509,15 +660,23 @@ inline int shard_partials(const float* cur, const float* old, const float* adv, 
   if (n < 0 || (n > 0 && (cur == nullptr || old == nullptr || adv == nullptr || partials == nullptr)))
     return kInvalidArgument;
   if (n == 0) return kOk;
-  launch_chunks<false>(cur, old, adv, ent, n, make_clip(eps), partials, nullptr, nullptr, stream);
+  const Clip clip = make_clip(eps);
+  const bool vec = vec_ok(cur, old, adv, ent);
+  if (ent != nullptr) {
+    if (vec) launch_partials<true, true>(cur, old, adv, ent, n, clip, partials, stream);
+    else launch_partials<false, true>(cur, old, adv, ent, n, clip, partials, stream);
+  } else {
+    if (vec) launch_partials<true, false>(cur, old, adv, ent, n, clip, partials, stream);
+    else launch_partials<false, false>(cur, old, adv, ent, n, clip, partials, stream);
+  }
   return launch_status();
 }
 
 inline int shard_finish(const Partial* partials, int64_t n_parts, int64_t n_total, bool ext, float* out,
                         cudaStream_t stream) {
   if (n_parts < 0 || n_total < 0 || out == nullptr || (n_parts > 0 && partials == nullptr)) return kInvalidArgument;
-  finish_kernel<<<1, kThreads, 0, stream>>>(partials, n_parts, n_total, inv_count(n_total), ext ? 1 : 0, out);
-  return launch_status();
+  return launch_pdl(finish_kernel, 1, kThreads, 0, stream, partials, n_parts, n_total, inv_count(n_total), ext ? 1 : 0,
+                    out);
 }
 
 // B*T*H of the reference ABI, or -1 when a dimension is negative.

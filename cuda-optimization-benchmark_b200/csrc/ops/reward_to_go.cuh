@@ -320,6 +320,7 @@ __device__ __forceinline__ void one_row(const float* __restrict__ reward, const 
 __global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restrict__ reward,
                                                        const unsigned char* __restrict__ done, float gamma,
                                                        int B, int T, int nbuf, float* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint64_t bars[kWarps][2];  // one barrier per staging buffer
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -340,8 +341,7 @@ inline int run(const float* reward, const unsigned char* done, float gamma, int3
   const int nbuf = single ? 1 : 2;
   const int64_t cap = single ? one_wave : int64_t(sm_count()) * 2;
   const int grid = int(ctas_needed < cap ? ctas_needed : cap);
-  rtg_kernel<<<grid, kThreads, nbuf * kSmemPerBuffer, stream>>>(reward, done, gamma, B, T, nbuf, out);
-  return launch_status();
+  return launch_pdl(rtg_kernel, grid, kThreads, nbuf * kSmemPerBuffer, stream, reward, done, gamma, B, T, nbuf, out);
 }
 
 }  // namespace rtg

@@ -8,11 +8,14 @@
 // scans overlap the PPO streams.
 //   - reward-to-go CTAs: 8 warps, one row per warp at a time, exactly rtg::warp_rows (the same
 //     passes and the same bits as the reward_to_go entry points);
-//   - PPO CTAs: chunks of 4096 samples through ppo::chunk_partials (the same partials, hence the
-//     same bits, as the ppo_clip entry points); the PPO CTA that finishes last combines the
-//     partials, or, in the shard form, the partials are left for a cross-GPU gather and ppo finish.
+//   - PPO CTAs: chunks of 4096 samples through ppo::chunk_partials (the same partials, combined in
+//     the same order, hence the same bits, as the ppo_clip entry points); the PPO CTA that finishes
+//     last combines the partials, or, in the shard form, the partials are left for a cross-GPU
+//     gather and ppo finish.
 // One resident wave of B200_RL_MIN_CTAS CTAs per SM is split between the roles so that the
-// slowest CTA of either kind has the least work (see split_roles).
+// slowest CTA of either kind has the least work (see split_roles).  Steps are launched with
+// programmatic dependent launch, so back-to-back steps overlap the tail of one with the start of
+// the next (step_prologue).
 #pragma once
 
 #include "../common/b200_common.cuh"
@@ -45,8 +48,8 @@ struct Args {
   const float* ent;
   int64_t n;
   ppo::Clip clip;
-  ppo::Partial* partials;
-  unsigned* ticket;
+  ppo::Partial* partials;  // chunk partials (workspace, or the caller's buffer in the shard form)
+  unsigned* ticket;        // completion counter of the last-CTA election (workspace)
   float* ppo_out;
   double inv_n;      // 1 / n for the PPO finish
   int64_t rtg_ctas;  // CTAs with the reward-to-go role (kRows rows each per round)
@@ -55,11 +58,14 @@ struct Args {
 };
 
 // Under PDL the launch may begin before the previous kernel on the stream has finished.  Unless
-// the caller has declared that no kernel of the stream writes the inputs (early_reads), every
-// thread first waits for it, so only the launch latency overlaps; otherwise the loads go ahead and
-// each thread waits just before its first global write.
+// the caller has declared that the kernel launched just before writes none of the inputs
+// (early_reads), every thread first waits for it, so only the launch latency overlaps; otherwise
+// the loads go ahead and each thread waits just before its first global write.  Either way the
+// next launch is released at once: its CTAs take the SM slots this step's CTAs free as they finish
+// (every CTA of this step is resident by then, so none of them can be starved of a slot).
 __device__ __forceinline__ void step_prologue(const Args& a) {
   if (!a.early_reads) pdl_wait();
+  pdl_trigger();
 }
 
 template <bool kVec, bool kEnt, bool kFinish>
@@ -80,10 +86,8 @@ __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_kernel(const 
   ppo::chunk_partials<kVec, kEnt>(a.cur, a.old, a.adv, a.ent, a.n, a.clip, a.partials, pidx, a.ppo_ctas);
   if (kFinish) {
     if (threadIdx.x == 0) pdl_wait();  // the ticket (also when this CTA had no chunk)
-    if (elect_last_add(a.ticket, 1u, unsigned(a.ppo_ctas))) {
-      pdl_trigger();  // the next launch may start while this CTA combines the partials
+    if (elect_last_add(a.ticket, 1u, unsigned(a.ppo_ctas)))
       ppo::finish(a.partials, ppo::num_chunks(a.n), a.n, a.inv_n, kEnt, a.ppo_out);
-    }
   }
 }
 
@@ -115,11 +119,12 @@ __device__ __forceinline__ ppo::Sums unpack_sums(const uint32_t (&w)[kRankWords]
 }
 
 // Multi-GPU step with the PPO exchange fused in (one launch per rank per step).  Each rank reduces
-// its own chunk partials exactly as the one-GPU step does; the CTA that does so stores the rank's
-// totals, in LL form, into slot `rank` of every rank's buffer (16-byte stores of two {word, epoch}
-// pairs over NVLink; no fence, no flag), reads every rank's totals from its own buffer (thread r
-// reads rank r's, waiting until its epoch has arrived) and adds them in rank order.  Every rank
-// writes the same outputs; with one rank they are bit-identical to the one-GPU step.
+// its own chunk partials exactly as the one-GPU step does; the CTA that does so (the last PPO CTA
+// to finish) stores the rank's totals, in LL form, into slot `rank` of every other rank's buffer
+// (16-byte stores of two {word, epoch} pairs over NVLink; no fence, no flag), reads the other
+// ranks' totals from its own buffer (one thread per rank, each waiting until its record's epoch
+// has arrived) and adds all ranks' totals in rank order.  Every rank writes the same outputs; with
+// one rank they are bit-identical to the one-GPU step.
 template <bool kVec, bool kEnt>
 __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_exchange_kernel(const Args a, const PeerView pv) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -137,25 +142,28 @@ __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_exchange_kern
   }
   const int64_t pidx = b - rtg_before;
   ppo::chunk_partials<kVec, kEnt>(a.cur, a.old, a.adv, a.ent, a.n, a.clip, a.partials, pidx, a.ppo_ctas);
-  if (threadIdx.x == 0) pdl_wait();
+  if (threadIdx.x == 0) pdl_wait();  // the ticket (also when this CTA had no chunk)
   if (!elect_last_add(a.ticket, 1u, unsigned(a.ppo_ctas))) return;
-  pdl_trigger();
   const ppo::Sums mine = ppo::reduce_partials(a.partials, ppo::num_chunks(a.n));
   if (threadIdx.x == 0) {
     uint32_t w[kRankWords];
     pack_sums(mine, w);
     for (int r = 0; r < pv.world; ++r) {
+      if (r == pv.rank) continue;
       ulonglong2* rec = peer_record(pv, r, pv.rank, 0);
 #pragma unroll
       for (int q = 0; q < kRankWords / 2; ++q)
-        ll_store2(rec + q, ll_word(w[2 * q], pv.epoch), ll_word(w[2 * q + 1], pv.epoch));
+        ll_store2<LLScope::kSys>(rec + q, ll_word(w[2 * q], pv.epoch), ll_word(w[2 * q + 1], pv.epoch));
     }
   }
-  if (threadIdx.x < pv.world) {
-    LLReader<kRankWords> rd{peer_record(pv, pv.rank, 0, 0), pv.epoch};
+  if (threadIdx.x == 0) {
+    s_rank[pv.rank] = mine;  // this rank's own totals need no round trip through memory
+  } else if (threadIdx.x < pv.world) {
+    const int r = threadIdx.x - 1 < pv.rank ? threadIdx.x - 1 : threadIdx.x;  // threads 1.. take the other ranks
+    LLReader<kRankWords, LLScope::kSys> rd{peer_record(pv, pv.rank, 0, 0), pv.epoch};
     uint32_t w[kRankWords];
-    rd.read(threadIdx.x, w);
-    s_rank[threadIdx.x] = unpack_sums(w);
+    rd.read(r, w);
+    s_rank[r] = unpack_sums(w);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -238,8 +246,8 @@ inline int run(const float* reward, const unsigned char* done, float gamma, int3
   if (finish) {
     if (ppo_out == nullptr) return kInvalidArgument;
     if (workspace == nullptr || ws_bytes < ppo::workspace_bytes(n)) return kWorkspaceTooSmall;
-    a.ticket = static_cast<unsigned*>(workspace);
-    a.partials = reinterpret_cast<ppo::Partial*>(static_cast<char*>(workspace) + 256);
+    a.ticket = &static_cast<ppo::Control*>(workspace)->ticket;
+    a.partials = ppo::ws_partials(workspace);
   } else {
     if (n > 0 && partials_out == nullptr) return kInvalidArgument;
     a.ticket = nullptr;
@@ -289,8 +297,8 @@ inline int run_exchange(const float* reward, const unsigned char* done, float ga
   a.ent = ent;
   a.n = n;
   a.clip = ppo::make_clip(eps);
-  a.ticket = static_cast<unsigned*>(workspace);
-  a.partials = reinterpret_cast<ppo::Partial*>(static_cast<char*>(workspace) + 256);
+  a.ticket = &static_cast<ppo::Control*>(workspace)->ticket;
+  a.partials = ppo::ws_partials(workspace);
   a.ppo_out = ppo_out;
   a.inv_n = ppo::inv_count(int64_t(x->world) * n);
   const int64_t slots = int64_t(sm_count()) * B200_RL_MIN_CTAS;

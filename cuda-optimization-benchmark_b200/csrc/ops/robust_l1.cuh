@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict
                                                          int64_t n, double* __restrict__ partials,
                                                          unsigned* __restrict__ ticket, double inv_n,
                                                          float* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   const int64_t n_chunks = (n + kChunk - 1) / kChunk;
   for (int64_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const float t = thread_chunk_sum<kVec>(a, b, c * kChunk, n);
@@ -120,6 +121,7 @@ __global__ void __launch_bounds__(kThreads) chunk_kernel(const float* __restrict
 
 __global__ void __launch_bounds__(kThreads) finish_kernel(const double* __restrict__ partials, int64_t n_parts,
                                                           double inv_n, float* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   finish(partials, n_parts, inv_n, out);
 }
 
@@ -128,7 +130,7 @@ inline void launch_chunks(const float* a, const float* b, int64_t n, double* par
                           cudaStream_t stream) {
   auto kern = chunk_kernel<kVec, kFinish>;
   const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
-  kern<<<grid, kThreads, 0, stream>>>(a, b, n, partials, ticket, inv_count(n), out);
+  launch_pdl(kern, grid, kThreads, 0, stream, a, b, n, partials, ticket, inv_count(n), out);
 }
 
 // Full op on one device with a caller workspace of workspace_bytes(n) bytes whose first 4 bytes
@@ -156,8 +158,7 @@ inline int shard_partials(const float* a, const float* b, int64_t n, double* par
 
 inline int shard_finish(const double* partials, int64_t n_parts, int64_t n_total, float* out, cudaStream_t stream) {
   if (n_parts < 0 || n_total < 0 || out == nullptr || (n_parts > 0 && partials == nullptr)) return kInvalidArgument;
-  finish_kernel<<<1, kThreads, 0, stream>>>(partials, n_parts, inv_count(n_total), out);
-  return launch_status();
+  return launch_pdl(finish_kernel, 1, kThreads, 0, stream, partials, n_parts, inv_count(n_total), out);
 }
 
 // Element count of the reference ABI's (batch_size, 4, height, width) tensors, or -1 when a

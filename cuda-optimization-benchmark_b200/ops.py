@@ -54,8 +54,8 @@ def _need(t, name, dtype, device=None):
 def workspace(op, nbytes, device):
     """Zero-initialised scratch for `op` on `device` and the current stream, grown on demand.
 
-    The reduction kernels leave their completion counter at zero, so one buffer serves every
-    later call issued on the same stream."""
+    The reduction kernels leave their control words ready for the next call, so one buffer serves
+    every later call issued on the same stream (never two streams at once)."""
     key = (op, device.index, torch.cuda.current_stream(device).cuda_stream)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
