@@ -11,14 +11,15 @@
 //
 // B200 design: the membrane state lives in registers for the whole time loop.  Each CTA owns a
 // contiguous slab of S neurons of the flattened (B*H) neuron axis (S ~ B*H / #SMs, one CTA per
-// SM), one thread per 4 neurons, and moves whole time-step slices of its slab with cp.async.bulk:
-// one thread keeps kDepth future x[t] slices (S*4 bytes each) in flight into a shared-memory
-// ring, the threads read their 4 neurons with one 128-bit shared load, write their 4 spikes into
-// a shared staging ring, and after one CTA barrier per step the same thread writes the slice of
-// spikes back with one bulk store.  DRAM sees S*4-byte contiguous transfers instead of
-// per-warp 512-byte pieces scattered over many time slices.  8 bytes of HBM traffic per
-// neuron-step (read x, write spike).  Shapes whose neuron count is not a multiple of 4, or
-// unaligned pointers, take the one-neuron-per-thread form of the same loop.
+// SM).  One producer thread keeps up to kMaxDepth future x[t] slab slices (S*4 contiguous bytes
+// each) in flight into a shared-memory ring with cp.async.bulk, one "full" mbarrier per slot; the
+// consumer warps (one thread per 4 neurons) wait on the slot, read their 4 inputs with one 128-bit
+// shared load, store their 4 spikes straight to global memory with one 128-bit streaming store
+// (each warp writes 512 contiguous bytes), and release the slot through its "empty" mbarrier, one
+// arrive per warp.  No CTA-wide barrier is taken per step: warps drift apart by up to the ring
+// depth, and the producer refills a slot as soon as every warp has read it.  8 bytes of HBM
+// traffic per neuron-step (read x, write spike).  Shapes whose neuron count is not a multiple of
+// 4, or unaligned pointers, take the one-neuron-per-thread form of the same loop.
 #pragma once
 
 #include "../common/b200_common.cuh"
@@ -28,7 +29,7 @@ namespace b200 {
 namespace lif {
 
 constexpr int kThreads = 128;
-constexpr int kDepth = 8;   // time steps of x in flight per thread
+constexpr int kDepth = 8;   // time steps of x in flight per thread (scalar form)
 
 __device__ __forceinline__ float clamp01(float b) { return fminf(fmaxf(b, 0.0f), 1.0f); }
 
@@ -38,76 +39,82 @@ __device__ __forceinline__ float step(float& mem, float x, float beta, float th)
   return mem >= th ? 1.0f : 0.0f;
 }
 
-constexpr int kMaxDepth = 16;  // x slices in flight per CTA
-constexpr int kOut = 4;        // spike slices being written back per CTA
-constexpr int kSmemBudget = 160 * 1024;
+constexpr int kMaxDepth = 24;               // x slices in flight per CTA
+constexpr int kSmemBudget = 192 * 1024;      // bytes of the x ring
+constexpr int kMaxSlab = (1024 - 32) * 4;    // neurons per CTA: consumer threads + one producer warp
 
-// Slab form (NB % 4 == 0, 16-byte aligned pointers): CTA c owns neurons [c*S, c*S + cnt).
+// Slab form (NB % 4 == 0, 16-byte aligned pointers): CTA c owns neurons [c*S, c*S + cnt); warp 0
+// produces, warps 1.. consume (thread 32 + i owns neurons 4i .. 4i + 3 of the slab).
 __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restrict__ x, const float* __restrict__ mem0,
                                                           const float* __restrict__ beta,
                                                           const float* __restrict__ th, int T, int64_t NB, int H,
                                                           int S, int depth, float* __restrict__ spikes,
                                                           float* __restrict__ final_mem) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
-  extern __shared__ __align__(128) float sm[];
-  __shared__ uint64_t full[kMaxDepth];
-  float* xr = sm;                  // depth slices of S floats
-  float* so = sm + int64_t(depth) * S;  // kOut slices of S floats
+  extern __shared__ __align__(128) float xr[];  // depth slices of S floats
+  __shared__ uint64_t full[kMaxDepth], empty[kMaxDepth];
   const int64_t n0 = int64_t(blockIdx.x) * S;
   const int cnt = int(NB - n0 < S ? NB - n0 : S);
   const uint32_t bytes = uint32_t(cnt) * 4u;
-  const int tid = threadIdx.x;
-  const bool mine = 4 * tid < cnt;
-  if (tid == 0) {
-    for (int d = 0; d < depth; ++d) mbar_init(&full[d], 1);
+  const int consumer_warps = int(blockDim.x / 32) - 1;
+  if (threadIdx.x == 0) {
+    for (int d = 0; d < depth; ++d) {
+      mbar_init(&full[d], 1);
+      mbar_init(&empty[d], uint32_t(consumer_warps));
+    }
     fence_barrier_init();
   }
   __syncthreads();
-  if (tid == 0) {
-    for (int t = 0; t < depth && t < T; ++t) {
-      mbar_arrive_expect_tx(&full[t], bytes);
-      bulk_g2s(xr + int64_t(t) * S, x + int64_t(t) * NB + n0, bytes, &full[t]);
+  if (threadIdx.x < 32) {
+    // Producer: slot d holds x[t] for t = d, d + depth, ...; it is refilled once every consumer
+    // warp has released the previous use.
+    if (threadIdx.x == 0) {
+      int issued = 0;
+      for (int t = 0; t < T; ++t) {
+        const int d = t % depth, k = t / depth;
+        if (k > 0 && !mbar_wait_sleep(&empty[d], uint32_t(k - 1) & 1u)) break;
+        mbar_arrive_expect_tx(&full[d], bytes);
+        bulk_g2s(xr + int64_t(d) * S, x + int64_t(t) * NB + n0, bytes, &full[d]);
+        issued = t + 1;
+      }
+      // No copy may still be writing this CTA's shared memory when it exits (the consumers wait
+      // for every copy on the normal path; this covers a wait that gave up): the last use of each
+      // slot has completed once its phase has.
+      for (int t = issued > depth ? issued - depth : 0; t < issued; ++t)
+        if (!mbar_wait_sleep(&full[t % depth], uint32_t(t / depth) & 1u)) break;
     }
+    return;
   }
+  const int i = threadIdx.x - 32, lane = threadIdx.x & 31;
+  const bool mine = 4 * i < cnt;
   float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
   float bq[4] = {0.f, 0.f, 0.f, 0.f}, tq[4] = {0.f, 0.f, 0.f, 0.f};
   if (mine) {
-    m = *reinterpret_cast<const float4*>(mem0 + n0 + 4 * tid);
+    m = *reinterpret_cast<const float4*>(mem0 + n0 + 4 * i);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int h = int((n0 + 4 * tid + j) % H);
+      const int h = int((n0 + 4 * i + j) % H);
       bq[j] = clamp01(beta[h]);
       tq[j] = th[h];
     }
   }
+  float* out = spikes + n0 + 4 * i;
   for (int t = 0; t < T; ++t) {
     const int d = t % depth;
-    mbar_wait(&full[d], uint32_t(t / depth) & 1u);
+    if (!mbar_wait(&full[d], uint32_t(t / depth) & 1u)) break;
     if (mine) {
-      const float4 xv = *reinterpret_cast<const float4*>(xr + int64_t(d) * S + 4 * tid);
+      const float4 xv = *reinterpret_cast<const float4*>(xr + int64_t(d) * S + 4 * i);
       float4 sp;
       sp.x = step(m.x, xv.x, bq[0], tq[0]);
       sp.y = step(m.y, xv.y, bq[1], tq[1]);
       sp.z = step(m.z, xv.z, bq[2], tq[2]);
       sp.w = step(m.w, xv.w, bq[3], tq[3]);
-      *reinterpret_cast<float4*>(so + int64_t(t % kOut) * S + 4 * tid) = sp;
+      st_stream_f4(out + int64_t(t) * NB, sp);
     }
-    // Before anyone writes staging slot (t+1) % kOut in the next step, the bulk store that last
-    // read it (step t+1-kOut) must be done: at most kOut-2 older stores may still be reading.
-    if (tid == 0) bulk_wait_read<kOut - 2>();
-    __syncthreads();
-    if (tid == 0) {
-      fence_proxy_async_smem();
-      bulk_s2g(spikes + int64_t(t) * NB + n0, so + int64_t(t % kOut) * S, bytes);
-      bulk_commit();
-      if (t + depth < T) {
-        mbar_arrive_expect_tx(&full[d], bytes);
-        bulk_g2s(xr + int64_t(d) * S, x + int64_t(t + depth) * NB + n0, bytes, &full[d]);
-      }
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[d]);
   }
-  if (mine) *reinterpret_cast<float4*>(final_mem + n0 + 4 * tid) = m;
-  if (tid == 0) bulk_wait_all();
+  if (mine) *reinterpret_cast<float4*>(final_mem + n0 + 4 * i) = m;
 }
 
 // Scalar form: one neuron per thread, same per-neuron arithmetic.
@@ -152,18 +159,18 @@ inline int run(const float* x, const float* mem0, const float* beta, const float
   const bool slab = T > 0 && (NB % 4 == 0) && aligned16(mem0) && aligned16(final_mem) && aligned16(x) &&
                     aligned16(spikes);
   if (slab) {
-    // Slab of S neurons per CTA: about one CTA per SM, S a multiple of 128 (whole warps).
+    // Slab of S neurons per CTA: about one CTA per SM, S a multiple of 128 (whole consumer warps).
     const int sms = sm_count();
     int64_t S = (NB + sms - 1) / sms;
     S = (S + 127) / 128 * 128;
-    if (S > 4096) S = 4096;
+    if (S > kMaxSlab) S = kMaxSlab;
     const int64_t grid = (NB + S - 1) / S;
-    int depth = int(kSmemBudget / (S * 4)) - kOut;
+    int depth = int(kSmemBudget / (S * 4));
     if (depth > kMaxDepth) depth = kMaxDepth;
     if (depth < 2) depth = 2;
-    const size_t smem = size_t(depth + kOut) * size_t(S) * 4;
+    const size_t smem = size_t(depth) * size_t(S) * 4;
     if (!ensure_dyn_smem(lif_slab_kernel, int(smem))) return kCudaError;
-    return launch_pdl(lif_slab_kernel, unsigned(grid), unsigned(S / 4), smem, stream, x, mem0, beta, th, T, NB, H,
+    return launch_pdl(lif_slab_kernel, unsigned(grid), unsigned(S / 4 + 32), smem, stream, x, mem0, beta, th, T, NB, H,
                       int(S), depth, spikes, final_mem);
   } else {
     const int64_t grid = (NB + kThreads - 1) / kThreads;

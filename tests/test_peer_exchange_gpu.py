@@ -8,6 +8,7 @@ each rank's PPO totals exchanged over NVLink peer memory inside the kernel.
   tree) and meet the fp64 oracle.
 - Each rank's returns are bit-identical to reward_to_go on its own batch.
 - With a per-rank sample count that is not a multiple of the chunk, the same holds.
+- On a box with more than two GPUs, the same over all of them (up to 8 ranks).
 Skipped on a box with fewer than two GPUs.
 """
 import os
@@ -76,13 +77,13 @@ def _worker(rank, world, port, B, T, n, ent, steps, q):
         dist.destroy_process_group()
 
 
-def _run(B, T, n, ent, steps=3):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _run(B, T, n, ent, steps=3, world=2):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, B, T, n, ent, steps, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, B, T, n, ent, steps, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict()
@@ -131,3 +132,23 @@ def test_exchange_ragged_ranks_agree():
         p1, _, _ = res[1][step]
         assert torch.equal(p0.view(torch.int32), p1.view(torch.int32))
         _check_against_oracle(p0, [_inputs(r, B, T, n, True, step) for r in range(2)], True)
+
+
+@pytest.mark.timeout(400)
+def test_exchange_all_gpus():
+    """Every GPU of the box as one rank each (3 to 8 ranks): all ranks agree bit for bit, meet the
+    fp64 oracle over all ranks' samples and match one GPU within a few ulps."""
+    world = min(torch.cuda.device_count(), 8)
+    if world < 3:
+        pytest.skip("needs more than two GPUs")
+    B, T, n = 16, 700, 5 * 4096 + 123
+    res = _run(B, T, n, True, steps=3, world=world)
+    for step in range(3):
+        p0, rtg_ok0, single = res[0][step]
+        assert rtg_ok0
+        for r in range(1, world):
+            pr, rtg_ok, _ = res[r][step]
+            assert rtg_ok
+            assert torch.equal(p0.view(torch.int32), pr.view(torch.int32)), (step, r, p0, pr)
+        assert torch.allclose(p0, single, rtol=4e-7, atol=1e-9), (step, p0, single)
+        _check_against_oracle(p0, [_inputs(r, B, T, n, True, step) for r in range(world)], True)
