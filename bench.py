@@ -55,6 +55,14 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def bf16_tflops():
+    """Measured dense bf16 TFLOP/s (burst, cuBLAS) of this pool's B200s, else the fallback figure."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
+
+
 # ------------------------------------------------------------------------------ distributed set-up
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -493,23 +501,34 @@ def run_b200(args, world, rank, local):
 
 
 def other_ops(ops, dev, world, rank):
-    """Device-timed µs of the other streaming ops at their BASELINE sizes (one input set each,
-    already larger than L2)."""
+    """Device-timed µs of the other BASELINE ops at their BASELINE sizes (one input set each,
+    already larger than L2 for the streaming ops), with their roofline fractions."""
     from oracle import inputs
     peak, _ = peaks()
     res = {}
 
     def timeit(fn, reps=20):
-        for _ in range(3):
-            fn()
+        """Device ms per call: `reps` back-to-back calls captured in a CUDA graph and replayed, so
+        the Python cost of a call (more than a small kernel's runtime) stays out of the number."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # warm-up on the capture stream: its scratch exists before capture
+            for _ in range(3):
+                fn()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(reps):
+                fn()
+        g.replay()  # warm
         torch.cuda.synchronize(dev)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(reps):
-            fn()
+        g.replay()
         b.record()
         torch.cuda.synchronize(dev)
+        del g
         return a.elapsed_time(b) / reps
 
     s = inputs.baseline_inputs("robust_l1", seed=rank)
@@ -526,6 +545,38 @@ def other_ops(ops, dev, world, rank):
     ms = timeit(lambda: ops.leaky(xs, m0, be, th, spikes=sp, final_mem=fm))
     res["leaky"] = {"us": ms * 1e3, "bytes": LIF_BYTES, "gbs": LIF_BYTES / ms / 1e6,
                     "frac_of_hbm": LIF_BYTES / ms / 1e6 / peak}
+    del xs, m0, be, th, sp, fm
+
+    # Tensor-core ops against the measured dense bf16 peak (burst); FP8 against twice that figure
+    # (the E4M3 rate of this part is twice its bf16 rate).  KAN issues three fp16 GEMM passes per
+    # useful flop (the hi/lo operand split), so both its useful and its issued rates are reported.
+    bf16_peak = bf16_tflops()
+    s = inputs.baseline_inputs("kan", seed=rank)
+    t = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in s.items()}
+    kout = torch.empty((s["B"], s["O"]), device=dev)
+    ms = timeit(lambda: ops.efficient_kan(t["x"], t["grid"], t["base_weight"], t["spline_weight"], t["spline_scaler"],
+                                          t["grid_size"], t["spline_order"], out=kout), reps=10)
+    flops = 2 * s["B"] * s["O"] * s["I"] * (s["grid_size"] + s["spline_order"] + 1)
+    res["efficient_kan"] = {"us": ms * 1e3, "useful_tflops": flops / ms / 1e9,
+                            "issued_tflops": 3 * flops / ms / 1e9,
+                            "frac_of_bf16_peak_issued": 3 * flops / ms / 1e9 / bf16_peak}
+    del t, kout
+    # FP8 at the four BASELINE shapes; inputs drawn on the device (the values do not change the
+    # timing; parity is tested on the oracle's own inputs).
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    for M, N, K in inputs.BASELINE_SHAPES["fp8_linear"]:
+        x8, w8 = (torch.randn(r, K, device=dev, generator=g).clamp_(-448, 448).to(torch.float8_e4m3fn)
+                  for r in (M, N))
+        bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        yout = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        ms = timeit(lambda: ops.fp8_linear(x8, 1.0, w8, 1.0, bias, out=yout), reps=10 if M * N * K > 1 << 36 else 50)
+        flops = 2 * M * N * K
+        nbytes = M * K + N * K + 2 * N + 2 * M * N
+        res[f"fp8_linear M{M} N{N} K{K}"] = {
+            "us": ms * 1e3, "tflops": flops / ms / 1e9, "frac_of_fp8_peak": flops / ms / 1e9 / (2 * bf16_peak),
+            "gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / peak,
+            "bound": "hbm" if flops / nbytes < 2 * bf16_peak * 1e3 / peak else "fp8 tensor"}
+        del x8, w8, bias, yout
     torch.cuda.synchronize(dev)
     return res
 

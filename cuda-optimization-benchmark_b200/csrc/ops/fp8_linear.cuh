@@ -19,8 +19,9 @@
 //   - warps 2-5: epilogue; tcgen05.ld the accumulator (one TMEM lane quarter per warp, one
 //     output row per thread), fused acc * (1/(sx*sw)) + bias, round to bf16, 128-bit stores;
 //     it drains one accumulator while the MMAs fill the other.
-// Small problems take BN = 128 or 64 so more SMs get tiles.  Other shapes (K not a multiple of 16,
-// unaligned operands) take a shared-memory tiled CUDA-core kernel with the same arithmetic.
+// Small problems take BN = 128 or 64 so more SMs get tiles; M <= 64 swaps the operands and splits
+// K over a cluster (gemv_kernel).  Other shapes (K not a multiple of 16, unaligned operands) take a
+// shared-memory tiled CUDA-core kernel with the same arithmetic.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -211,6 +212,179 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
 }
 
+// ------------------------------------------------------------------ small M: swap-AB, split-K
+// For M <= 64 the W stream dominates and a 128-row tile of x would be mostly padding.  The MMA
+// roles swap: a CTA computes D^T[128 rows of W, BNX >= M columns] = W_tile . x^T with
+// tcgen05.mma M = 128, N = BNX, and a cluster of SK CTAs splits K between them.  Each CTA
+// accumulates its K range in TMEM, its epilogue warps park the fp32 partial tile in shared memory,
+// and after a cluster barrier the cluster's first CTA adds the SK partials in rank order (reading
+// the others through distributed shared memory), applies scale and bias and writes out[m][n].  A
+// second cluster barrier keeps every CTA's shared memory alive until that read is done.  W is read
+// once from HBM; the small x tile is read by every CTA (L2).  No multicast.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_cluster_smem(uint32_t smem_byte_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_byte_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+template <int BNX>
+struct SmallCfg {
+  static constexpr int kATile = kBM * kBK;   // 128 rows of W x 128 bytes of K
+  static constexpr int kBTile = BNX * kBK;   // BNX rows of x x 128 bytes of K
+  static constexpr int kStage = kATile + kBTile;
+  static constexpr int kStages = (192 * 1024) / kStage;
+  static constexpr int kTmemCols = BNX < 32 ? 32 : BNX;
+  static constexpr int kSmem = kStages * kStage + 1024;
+  static_assert(kStage % 1024 == 0, "stages keep the 1024-byte swizzle-atom alignment");
+  static_assert(kBM * BNX * 4 <= kStages * kStage, "the partial tile fits in the stage ring");
+};
+
+// grid = (SK, ceil(N / 128)), cluster (SK, 1, 1).  tmW: map over w [N, K], 128-row box; tmX: map
+// over x [M, K], BNX-row box.
+template <int BNX>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N, int K,
+                float scale, const uint16_t* __restrict__ bias, uint16_t* __restrict__ out) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  using C = SmallCfg<BNX>;
+  constexpr int S = C::kStages;
+#if !B200_TCGEN05
+  if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
+  return;
+#else
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full[S], empty[S], tfull;
+  __shared__ uint32_t tmem_base_s;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* part = reinterpret_cast<float*>(smem);  // [128][BNX] fp32 partial tile, after the MMAs
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank(), SK = gridDim.x;
+  const int nb = blockIdx.y;
+  const int nkb = (K + kBK - 1) / kBK;
+  const int kb0 = int((int64_t(nkb) * rank) / SK), kb1 = int((int64_t(nkb) * (rank + 1)) / SK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&tmW);
+    tc::prefetch_tensormap(&tmX);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&tmem_base_s, C::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer over this CTA's K range
+      for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
+        const uint32_t s = uint32_t(i) % S, ph = (uint32_t(i) / S) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u)) break;
+        mbar_arrive_expect_tx(&full[s], C::kStage);
+        uint8_t* a = smem + s * C::kStage;
+        tc::tma_load_2d(a, &tmW, kb * kBK, nb * kBM, &full[s]);
+        tc::tma_load_2d(a + C::kATile, &tmX, kb * kBK, 0, &full[s]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      const uint32_t id = tc::idesc(kBM, BNX, 0);
+      for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
+        const uint32_t s = uint32_t(i) % S, ph = (uint32_t(i) / S) & 1u;
+        if (!mbar_wait(&full[s], ph)) break;
+        tc::fence_after_sync();
+        const uint32_t a_addr = smem_addr(smem + s * C::kStage);
+        const uint64_t ad = tc::sdesc_kmajor_sw128(a_addr);
+        const uint64_t bd = tc::sdesc_kmajor_sw128(a_addr + C::kATile);
+#pragma unroll
+        for (int k = 0; k < kBK / kUmmaK; ++k)
+          tc::mma_f8(tmem, ad + uint64_t((k * kUmmaK) >> 4), bd + uint64_t((k * kUmmaK) >> 4), id,
+                     (i | k) != 0 ? 1u : 0u);
+        tc::mma_commit(&empty[s]);
+      }
+      tc::mma_commit(&tfull);  // also when this CTA's K range is empty (then nothing is added)
+    }
+    __syncwarp();
+  } else {  // epilogue warps 2..5: warp w holds TMEM lanes (W rows) [32*(w%4), 32*(w%4)+32)
+    const int q = warp & 3, r = q * 32 + lane;
+    const bool have_k = kb1 > kb0;
+    if (have_k) {
+      mbar_wait(&tfull, 0u);
+      tc::fence_after_sync();
+    }
+    float* mine = part + r * BNX;
+#pragma unroll
+    for (int c0 = 0; c0 < BNX; c0 += 32) {
+      uint32_t v[32];
+      if (have_k) {
+        tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+        tc::tmem_ld_wait();
+      }
+#pragma unroll
+      for (int j = 0; j < 32 && c0 + j < BNX; ++j) mine[c0 + j] = have_k ? __uint_as_float(v[j]) : 0.f;
+    }
+  }
+  cluster_sync_all();  // every CTA's partial tile is in its shared memory
+  if (rank == 0 && warp >= 2) {
+    const int q = warp & 3, r = q * 32 + lane;
+    const int n = nb * kBM + r;
+    float acc[BNX];
+#pragma unroll
+    for (int j = 0; j < BNX; ++j) acc[j] = 0.f;
+    const uint32_t base = smem_addr(part + r * BNX);
+    for (uint32_t k = 0; k < SK; ++k) {  // rank order: the same sum on every call
+      const uint32_t src = map_cluster_smem(base, k);
+#pragma unroll
+      for (int j = 0; j < BNX; j += 4) {
+        const float4 t = ld_cluster_f4(src + uint32_t(j) * 4u);
+        acc[j] += t.x;
+        acc[j + 1] += t.y;
+        acc[j + 2] += t.z;
+        acc[j + 3] += t.w;
+      }
+    }
+    if (n < N) {
+      const float b = bf16_bits_to_float(__ldg(bias + n));
+#pragma unroll
+      for (int j = 0; j < BNX; ++j)
+        if (j < M) out[int64_t(j) * N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(fmaf(acc[j], scale, b)));
+    }
+  }
+  tc::fence_before_sync();
+  cluster_sync_all();  // the first CTA has read every partial tile
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::kTmemCols);
+  }
+#endif
+}
+
 // ------------------------------------------------------------------------ CUDA-core fallback
 // 64 x 64 output tiles, 256 threads, each thread a 4 x 4 block; K in steps of 32 through shared
 // memory, E4M3 bytes decoded with a 256-entry table built from the format definition (sign,
@@ -275,9 +449,9 @@ __global__ void __launch_bounds__(256) simt_kernel(int M, int N, int K, const ui
 
 // ------------------------------------------------------------------------------------- host
 struct MapKey {
-  const void* x;
-  const void* w;
-  int M, N, K, BN;
+  const void* a;
+  const void* b;
+  int rows_a, rows_b, K, box_a, box_b;
 };
 
 struct MapEntry {
@@ -287,18 +461,21 @@ struct MapEntry {
   bool used = false;
 };
 
-// A few recently used (x, w, shape) tensor-map pairs: a repeated call at the same pointers skips
-// the host-side encoding.
-inline bool get_maps(const void* x, const void* w, int M, int N, int K, int BN, CUtensorMap* a, CUtensorMap* b) {
+// A few recently used tensor-map pairs (operand A [rows_a, K] with box_a-row boxes, operand B
+// [rows_b, K] with box_b-row boxes): a repeated call at the same pointers skips the host-side
+// encoding.
+inline bool get_maps(const void* pa, const void* pb, int rows_a, int rows_b, int K, int box_a, int box_b,
+                     CUtensorMap* a, CUtensorMap* b) {
   static MapEntry cache[8];
   static int next = 0;
   static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
+  const MapKey k{pa, pb, rows_a, rows_b, K, box_a, box_b};
   std::lock_guard<std::mutex> lock(mu);
   for (auto& e : cache) {
-    if (e.used && e.dev == dev && e.key.x == x && e.key.w == w && e.key.M == M && e.key.N == N && e.key.K == K &&
-        e.key.BN == BN) {
+    if (e.used && e.dev == dev && e.key.a == k.a && e.key.b == k.b && e.key.rows_a == k.rows_a &&
+        e.key.rows_b == k.rows_b && e.key.K == k.K && e.key.box_a == k.box_a && e.key.box_b == k.box_b) {
       *a = e.a;
       *b = e.b;
       return true;
@@ -307,9 +484,9 @@ inline bool get_maps(const void* x, const void* w, int M, int N, int K, int BN, 
   MapEntry& e = cache[next];
   next = (next + 1) % 8;
   e.used = false;
-  if (!tc::make_map_sw128(&e.a, x, uint64_t(M), uint64_t(K), 1, kBM)) return false;
-  if (!tc::make_map_sw128(&e.b, w, uint64_t(N), uint64_t(K), 1, uint32_t(BN))) return false;
-  e.key = MapKey{x, w, M, N, K, BN};
+  if (!tc::make_map_sw128(&e.a, pa, uint64_t(rows_a), uint64_t(K), 1, uint32_t(box_a))) return false;
+  if (!tc::make_map_sw128(&e.b, pb, uint64_t(rows_b), uint64_t(K), 1, uint32_t(box_b))) return false;
+  e.key = k;
   e.dev = dev;
   e.used = true;
   *a = e.a;
@@ -321,13 +498,49 @@ template <int BN>
 inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const uint16_t* bias,
                      uint16_t* out, cudaStream_t stream) {
   CUtensorMap a, b;
-  if (!get_maps(x, w, M, N, K, BN, &a, &b)) return kUnsupported;
+  if (!get_maps(x, w, M, N, K, kBM, BN, &a, &b)) return kUnsupported;
   auto kern = gemm_kernel<BN>;
   if (!ensure_dyn_smem(kern, Cfg<BN>::kSmem)) return kCudaError;
   const int n_tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   const int vec_ok = (N % 8 == 0) && aligned16(out);
   launch_pdl(kern, grid, kThreads, Cfg<BN>::kSmem, stream, a, b, M, N, K, scale, bias, out, vec_ok);
+  return launch_status();
+}
+
+// Split-K factor of the small-M kernel: enough clusters x CTAs to cover the SMs, at most 8 (the
+// portable cluster size) and at most one CTA per 128-byte K block.
+inline int small_split(int N, int K) {
+  const int n_tiles = (N + kBM - 1) / kBM, nkb = (K + kBK - 1) / kBK;
+  int sk = sm_count() / n_tiles;
+  if (sk > 8) sk = 8;
+  if (sk > nkb) sk = nkb;
+  return sk < 1 ? 1 : sk;
+}
+
+template <int BNX>
+inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const uint16_t* bias,
+                        uint16_t* out, cudaStream_t stream) {
+  CUtensorMap mw, mx;
+  if (!get_maps(w, x, N, M, K, kBM, BNX, &mw, &mx)) return kUnsupported;
+  auto kern = gemv_kernel<BNX>;
+  if (!ensure_dyn_smem(kern, SmallCfg<BNX>::kSmem)) return kCudaError;
+  const int sk = small_split(N, K);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(sk), unsigned((N + kBM - 1) / kBM));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = SmallCfg<BNX>::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(sk);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, kern, mw, mx, M, N, K, scale, bias, out) != cudaSuccess) return kCudaError;
   return launch_status();
 }
 
@@ -348,6 +561,11 @@ inline int run(int32_t M, int32_t K, int32_t N, const uint8_t* x, float sx, cons
   if (out == nullptr || bias == nullptr || (K > 0 && (x == nullptr || w == nullptr))) return kInvalidArgument;
   const float scale = float(1.0 / (double(sx) * double(sw)));
   const int bn = K > 0 ? plan_bn(M, N, K, x, w) : 0;
+  if (bn != 0 && M <= 64) {  // W-stream bound: swap-AB with split-K over a cluster
+    if (M <= 16) return launch_small<16>(M, N, K, x, w, scale, bias, out, stream);
+    if (M <= 32) return launch_small<32>(M, N, K, x, w, scale, bias, out, stream);
+    return launch_small<64>(M, N, K, x, w, scale, bias, out, stream);
+  }
   if (bn == 256) return launch_tc<256>(M, N, K, x, w, scale, bias, out, stream);
   if (bn == 128) return launch_tc<128>(M, N, K, x, w, scale, bias, out, stream);
   if (bn == 64) return launch_tc<64>(M, N, K, x, w, scale, bias, out, stream);

@@ -3,7 +3,8 @@
 - Every case of tests/task.json and public_cases.json under the grader's 3-call protocol on the
   drop-in entry point, against the fp64 oracle (tolerance 1e-2/1e-2, task.json) and against the
   reference oracle's outputs recorded in tests/golden/.
-- The tensor-core path against the CUDA-core path on the same inputs, for each tile width.
+- The tensor-core path against the CUDA-core path on the same inputs, for each tile width and for
+  the small-M path (M <= 64: swapped operands, K split over a cluster of CTAs).
 - The BASELINE.json shapes: the two smaller ones against the full fp64 oracle, the two large ones
   against the oracle on a seeded subset of rows.
 """
@@ -72,7 +73,11 @@ def _run(lib, fn, s, dev="cuda"):
 
 
 @pytest.mark.parametrize("shape", [(1, 64, 64), (16, 4096, 512), (128, 256, 256), (300, 384, 1008),
-                                   (1024, 2048, 4096), (257, 4096, 528)])
+                                   (1024, 2048, 4096), (257, 4096, 528),
+                                   # M <= 64: swap-AB with K split over a cluster (split 1 to 8,
+                                   # 16 / 32 / 64 columns, partial last W tile and K block)
+                                   (5, 130, 4096), (17, 4096, 1040), (33, 1000, 2048), (64, 4096, 4096),
+                                   (16, 28672, 1024), (2, 256, 16)])
 def test_tensor_path_matches_cuda_core_path(lib, shape):
     M, N, K = shape
     s = inputs.baseline_inputs("fp8_linear", seed=7, shape=(M, N, K))
