@@ -212,6 +212,140 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
 }
 
+// ------------------------------------------------------------- large shapes: 256 x 256 tiles
+// A CTA's operand bandwidth from L2 (about 100 GB/s per SM here) caps a 128 x 256 tile at ~175
+// flop per staged byte, below the E4M3 rate.  For large problems each CTA computes a 256 x 256
+// tile as two M = 128 MMAs that share one 256-row B tile (262 flop per staged byte): A and B are
+// each one 256-row TMA box per stage, the two fp32 accumulators fill all 512 TMEM columns (one
+// tile at a time; the MMAs of the next tile wait for the epilogue), and eight epilogue warps
+// drain them, two per TMEM lane quarter (warps 2-5 the upper 128 rows, warps 6-9 the lower).
+constexpr int kBM2 = 256;          // rows of x per tile (two UMMAs of 128)
+constexpr int kBN2 = 256;          // columns (rows of w) per tile
+constexpr int kThreads2 = 320;     // warp 0 loads, warp 1 issues MMAs, warps 2-9 epilogue
+struct Cfg2 {
+  static constexpr int kATile = kBM2 * kBK;
+  static constexpr int kBTile = kBN2 * kBK;
+  static constexpr int kStage = kATile + kBTile;  // 64 KB
+  static constexpr int kStages = (200 * 1024) / kStage;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kSmem = kStages * kStage + 1024;
+};
+
+__global__ void __launch_bounds__(kThreads2, 1)
+    gemm256_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, float scale, const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int vec_ok) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  using C = Cfg2;
+  constexpr int S = C::kStages;
+#if !B200_TCGEN05
+  if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
+  return;
+#else
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full[S], empty[S], tfull, tempty;
+  __shared__ uint32_t tmem_base_s;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_m = (M + kBM2 - 1) / kBM2, n_n = (N + kBN2 - 1) / kBN2, n_tiles = n_m * n_n;
+  const int nkb = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull, 1);
+    mbar_init(&tempty, 8);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&tmA);
+    tc::prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&tmem_base_s, C::kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer (a wait that gives up ends this role: no tile after it)
+      uint32_t kb_all = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, n_m, n_n, mb, nb);
+        for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
+          const uint32_t s = kb_all % S, ph = (kb_all / S) & 1u;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1u))) break;
+          mbar_arrive_expect_tx(&full[s], C::kStage);
+          uint8_t* a = smem + s * C::kStage;
+          tc::tma_load_2d(a, &tmA, kb * kBK, mb * kBM2, &full[s]);
+          tc::tma_load_2d(a + C::kATile, &tmB, kb * kBK, nb * kBN2, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer: D0 (rows 0-127) at column 0, D1 (rows 128-255) at column 256
+      const uint32_t id = tc::idesc(128, kBN2, 0);
+      uint32_t kb_all = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++it) {
+        ok = mbar_wait(&tempty, (it & 1u) ^ 1u);  // the epilogue has drained the previous tile
+        tc::fence_after_sync();
+        for (int kb = 0; kb < nkb && ok; ++kb, ++kb_all) {
+          const uint32_t s = kb_all % S, ph = (kb_all / S) & 1u;
+          if (!(ok = mbar_wait(&full[s], ph))) break;
+          tc::fence_after_sync();
+          const uint32_t a_addr = smem_addr(smem + s * C::kStage);
+          const uint64_t a0 = tc::sdesc_kmajor_sw128(a_addr);
+          const uint64_t a1 = tc::sdesc_kmajor_sw128(a_addr + 128 * kBK);
+          const uint64_t bd = tc::sdesc_kmajor_sw128(a_addr + C::kATile);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint64_t ko = uint64_t((k * kUmmaK) >> 4);
+            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            tc::mma_f8(tmem, a0 + ko, bd + ko, id, acc);
+            tc::mma_f8(tmem + 256u, a1 + ko, bd + ko, id, acc);
+          }
+          tc::mma_commit(&empty[s]);
+        }
+        tc::mma_commit(&tfull);
+      }
+    }
+  } else {  // epilogue warps 2..9: warp w reads TMEM lanes of quarter w % 4; w < 6: D0, else D1
+    const int q = warp & 3, half = warp < 6 ? 0 : 1;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      int mb, nb;
+      tile_coords(tile, n_m, n_n, mb, nb);
+      if (!mbar_wait(&tfull, it & 1u)) break;
+      tc::fence_after_sync();
+      const int row = mb * kBM2 + half * 128 + q * 32 + lane;
+#pragma unroll 1
+      for (int cc = 0; cc < kBN2 / 32; ++cc) {
+        uint32_t r[32];
+        tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(half * 256 + cc * 32), r);
+        tc::tmem_ld_wait();
+        store_row32(r, row, nb * kBN2 + cc * 32, M, N, scale, bias, out, vec_ok != 0);
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::kTmemCols);
+  }
+#endif
+}
+
 // ------------------------------------------------------------------ small M: swap-AB, split-K
 // For M <= 64 the W stream dominates and a 128-row tile of x would be mostly padding.  The MMA
 // roles swap: a CTA computes D^T[128 rows of W, BNX >= M columns] = W_tile . x^T with
@@ -508,6 +642,18 @@ inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, fl
   return launch_status();
 }
 
+inline int launch_tc256(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const uint16_t* bias,
+                        uint16_t* out, cudaStream_t stream) {
+  CUtensorMap a, b;
+  if (!get_maps(x, w, M, N, K, kBM2, kBN2, &a, &b)) return kUnsupported;
+  if (!ensure_dyn_smem(gemm256_kernel, Cfg2::kSmem)) return kCudaError;
+  const int n_tiles = ((M + kBM2 - 1) / kBM2) * ((N + kBN2 - 1) / kBN2);
+  const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
+  const int vec_ok = (N % 8 == 0) && aligned16(out);
+  launch_pdl(gemm256_kernel, grid, kThreads2, Cfg2::kSmem, stream, a, b, M, N, K, scale, bias, out, vec_ok);
+  return launch_status();
+}
+
 // Split-K factor of the small-M kernel: enough clusters x CTAs to cover the SMs, at most 8 (the
 // portable cluster size) and at most one CTA per 128-byte K block.
 inline int small_split(int N, int K) {
@@ -545,11 +691,13 @@ inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w,
 }
 
 // Which tensor-core tile width a shape uses (0 = CUDA-core fallback).
+// 512 = the 256 x 256 tiles of gemm256_kernel, for problems with at least four waves of them.
 inline int plan_bn(int M, int N, int K, const void* x, const void* w) {
   if (K % 16 != 0 || !aligned16(x) || !aligned16(w)) return 0;
   const int n_m = (M + kBM - 1) / kBM;
   const int sms = sm_count();
-  if (n_m * ((N + 255) / 256) >= sms) return 256;
+  if (((M + kBM2 - 1) / kBM2) * ((N + kBN2 - 1) / kBN2) >= 4 * sms) return 512;
+  if (n_m * ((N + 255) / 256) >= (sms * 4) / 5) return 256;
   if (n_m * ((N + 127) / 128) >= sms / 2) return 128;
   return 64;
 }
@@ -566,6 +714,7 @@ inline int run(int32_t M, int32_t K, int32_t N, const uint8_t* x, float sx, cons
     if (M <= 32) return launch_small<32>(M, N, K, x, w, scale, bias, out, stream);
     return launch_small<64>(M, N, K, x, w, scale, bias, out, stream);
   }
+  if (bn == 512) return launch_tc256(M, N, K, x, w, scale, bias, out, stream);
   if (bn == 256) return launch_tc<256>(M, N, K, x, w, scale, bias, out, stream);
   if (bn == 128) return launch_tc<128>(M, N, K, x, w, scale, bias, out, stream);
   if (bn == 64) return launch_tc<64>(M, N, K, x, w, scale, bias, out, stream);

@@ -3,8 +3,9 @@
 - Every case of tests/task.json and public_cases.json under the grader's 3-call protocol on the
   drop-in entry point, against the fp64 oracle (tolerance 1e-2/1e-2, task.json) and against the
   reference oracle's outputs recorded in tests/golden/.
-- The tensor-core path against the CUDA-core path on the same inputs, for each tile width and for
-  the small-M path (M <= 64: swapped operands, K split over a cluster of CTAs).
+- The tensor-core path against the CUDA-core path on the same inputs, for each tile width (the
+  256 x 256 tiles of the large-problem kernel included) and for the small-M path (M <= 64:
+  swapped operands, K split over a cluster of CTAs).
 - The BASELINE.json shapes: the two smaller ones against the full fp64 oracle, the two large ones
   against the oracle on a seeded subset of rows.
 """
@@ -77,12 +78,14 @@ def _run(lib, fn, s, dev="cuda"):
                                    # M <= 64: swap-AB with K split over a cluster (split 1 to 8,
                                    # 16 / 32 / 64 columns, partial last W tile and K block)
                                    (5, 130, 4096), (17, 4096, 1040), (33, 1000, 2048), (64, 4096, 4096),
-                                   (16, 28672, 1024), (2, 256, 16)])
+                                   (16, 28672, 1024), (2, 256, 16),
+                                   # 256 x 256 tiles (at least four waves of them), exact and ragged
+                                   (4096, 10240, 256), (4100, 10250, 272)])
 def test_tensor_path_matches_cuda_core_path(lib, shape):
     M, N, K = shape
     s = inputs.baseline_inputs("fp8_linear", seed=7, shape=(M, N, K))
     plan = lib.b200_fp8_linear_plan(M, K, N, ctypes.c_void_p(256), ctypes.c_void_p(256))
-    assert plan in (64, 128, 256)
+    assert plan in (64, 128, 256, 512)
     tcore = _run(lib, lib.b200_fp8_linear_async, s)
     ccore = _run(lib, lib.b200_fp8_linear_cuda_core_async, s)
     a = exact.bf16_bits_to_f64(bf16_bits(tcore))
