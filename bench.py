@@ -582,6 +582,17 @@ def other_ops(ops, dev, world, rank):
             "gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / peak,
             "bound": "hbm" if flops / nbytes < 2 * bf16_peak * 1e3 / peak else "fp8 tensor"}
         del x8, w8, bias, yout
+    # E4M3 quantisation of the largest BASELINE activation (bf16 16384 x 8192): a per-tensor amax
+    # needs every value before the first byte can be written, so the op reads x twice (the second
+    # pass partly from L2) and writes one byte per value; those 5 bytes per value are its traffic.
+    xq = torch.randn(16384, 8192, device=dev, generator=g).to(torch.bfloat16)
+    qq = torch.empty(xq.shape, dtype=torch.float8_e4m3fn, device=dev)
+    sq = torch.empty(1, device=dev)
+    ms = timeit(lambda: ops.fp8_quantize(xq, q=qq, scale=sq), reps=20)
+    nbytes = 5 * xq.numel()
+    res["fp8_quantize bf16 16384x8192"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                           "frac_of_hbm": nbytes / ms / 1e6 / peak}
+    del xq, qq, sq
     torch.cuda.synchronize(dev)
     return res
 

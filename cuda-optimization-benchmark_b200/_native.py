@@ -71,6 +71,10 @@ SIGNATURES = {
     "b200_fp8_linear_async": (c_int, [c_i32, c_i32, c_i32, c_p, c_f, c_p, c_f, c_p, c_p, c_p]),
     "b200_fp8_linear_cuda_core_async": (c_int, [c_i32, c_i32, c_i32, c_p, c_f, c_p, c_f, c_p, c_p, c_p]),
     "b200_fp8_linear_plan": (c_int, [c_i32, c_i32, c_i32, c_p, c_p]),
+    "b200_fp8_quantize_workspace_bytes": (c_sz, []),
+    "b200_fp8_quantize_async": (c_int, [c_p, c_i32, c_i64, c_p, c_p, c_p, c_sz, c_p]),
+    "b200_fp8_linear_bf16_workspace_bytes": (c_sz, [c_i32, c_i32]),
+    "b200_fp8_linear_bf16_async": (c_int, [c_i32, c_i32, c_i32, c_p, c_p, c_f, c_p, c_p, c_p, c_p, c_sz, c_p]),
 }
 
 

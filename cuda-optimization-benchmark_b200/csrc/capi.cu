@@ -13,6 +13,7 @@
 #include "dropin/pow_abs_sqrt_mean.cuh"
 #include "dropin/ppo_clip.cuh"
 #include "dropin/reward_to_go.cuh"
+#include "ops/fp8_pipeline.cuh"
 #include "ops/rl_step.cuh"
 
 namespace {
@@ -200,6 +201,25 @@ int b200_fp8_linear_plan(const int32_t M, const int32_t K, const int32_t N, cons
                          const uint8_t* w_fp8) {
   if (M <= 0 || K <= 0 || N <= 0) return 0;
   return b200::fp8::plan_bn(M, N, K, x_fp8, w_fp8);
+}
+
+// ------------------------------------------------------------------- E4M3 quantisation (fp8)
+size_t b200_fp8_quantize_workspace_bytes(void) { return b200::fp8q::workspace_bytes(); }
+
+int b200_fp8_quantize_async(const void* x, int32_t x_is_bf16, int64_t n, uint8_t* q, float* scale, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  return b200::fp8q::run(x, x_is_bf16 != 0, n, q, scale, 1.0f, workspace, workspace_bytes, as_stream(stream));
+}
+
+size_t b200_fp8_linear_bf16_workspace_bytes(int32_t M, int32_t K) {
+  return M < 0 || K < 0 ? 0 : b200::fp8q::linear_workspace_bytes(M, K);
+}
+
+int b200_fp8_linear_bf16_async(const int32_t M, const int32_t K, const int32_t N, const uint16_t* x_bf16,
+                               const uint8_t* w_fp8, float scale_w, const uint16_t* bias, uint16_t* output,
+                               float* scale_x, void* workspace, size_t workspace_bytes, void* stream) {
+  return b200::fp8q::linear_bf16(M, K, N, x_bf16, w_fp8, scale_w, bias, output, scale_x, workspace, workspace_bytes,
+                                 as_stream(stream));
 }
 
 // ----------------------------------------------------------------------------------------- KAN

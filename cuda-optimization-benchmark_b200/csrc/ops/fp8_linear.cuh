@@ -100,8 +100,10 @@ __device__ __forceinline__ void store_row32(const uint32_t (&r)[32], int row, in
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
-                float scale, const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int vec_ok) {
+                float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
+                uint16_t* __restrict__ out, int vec_ok) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  if (scale_ptr != nullptr) scale = *scale_ptr;  // written on the device by the quantisation kernels
   using C = Cfg<BN>;
   constexpr int S = C::kStages;
 #if !B200_TCGEN05
@@ -233,8 +235,10 @@ struct Cfg2 {
 
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm256_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, float scale, const uint16_t* __restrict__ bias, uint16_t* __restrict__ out, int vec_ok) {
+                   int K, float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
+                   uint16_t* __restrict__ out, int vec_ok) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  if (scale_ptr != nullptr) scale = *scale_ptr;
   using C = Cfg2;
   constexpr int S = C::kStages;
 #if !B200_TCGEN05
@@ -394,8 +398,10 @@ struct SmallCfg {
 template <int BNX>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N, int K,
-                float scale, const uint16_t* __restrict__ bias, uint16_t* __restrict__ out) {
+                float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
+                uint16_t* __restrict__ out) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  if (scale_ptr != nullptr) scale = *scale_ptr;
   using C = SmallCfg<BNX>;
   constexpr int S = C::kStages;
 #if !B200_TCGEN05
@@ -534,8 +540,10 @@ __device__ __forceinline__ float e4m3_value(unsigned b) {
 
 __global__ void __launch_bounds__(256) simt_kernel(int M, int N, int K, const uint8_t* __restrict__ x,
                                                    const uint8_t* __restrict__ w, float scale,
+                                                   const float* __restrict__ scale_ptr,
                                                    const uint16_t* __restrict__ bias, uint16_t* __restrict__ out) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  if (scale_ptr != nullptr) scale = *scale_ptr;
   __shared__ float lut[256];
   __shared__ float xs[32][65], ws[32][65];
   lut[threadIdx.x] = e4m3_value(threadIdx.x);
@@ -629,8 +637,8 @@ inline bool get_maps(const void* pa, const void* pb, int rows_a, int rows_b, int
 }
 
 template <int BN>
-inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const uint16_t* bias,
-                     uint16_t* out, cudaStream_t stream) {
+inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const float* scale_ptr,
+                     const uint16_t* bias, uint16_t* out, cudaStream_t stream) {
   CUtensorMap a, b;
   if (!get_maps(x, w, M, N, K, kBM, BN, &a, &b)) return kUnsupported;
   auto kern = gemm_kernel<BN>;
@@ -638,19 +646,20 @@ inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, fl
   const int n_tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   const int vec_ok = (N % 8 == 0) && aligned16(out);
-  launch_pdl(kern, grid, kThreads, Cfg<BN>::kSmem, stream, a, b, M, N, K, scale, bias, out, vec_ok);
+  launch_pdl(kern, grid, kThreads, Cfg<BN>::kSmem, stream, a, b, M, N, K, scale, scale_ptr, bias, out, vec_ok);
   return launch_status();
 }
 
-inline int launch_tc256(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const uint16_t* bias,
-                        uint16_t* out, cudaStream_t stream) {
+inline int launch_tc256(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const float* scale_ptr,
+                        const uint16_t* bias, uint16_t* out, cudaStream_t stream) {
   CUtensorMap a, b;
   if (!get_maps(x, w, M, N, K, kBM2, kBN2, &a, &b)) return kUnsupported;
   if (!ensure_dyn_smem(gemm256_kernel, Cfg2::kSmem)) return kCudaError;
   const int n_tiles = ((M + kBM2 - 1) / kBM2) * ((N + kBN2 - 1) / kBN2);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   const int vec_ok = (N % 8 == 0) && aligned16(out);
-  launch_pdl(gemm256_kernel, grid, kThreads2, Cfg2::kSmem, stream, a, b, M, N, K, scale, bias, out, vec_ok);
+  launch_pdl(gemm256_kernel, grid, kThreads2, Cfg2::kSmem, stream, a, b, M, N, K, scale, scale_ptr, bias, out,
+             vec_ok);
   return launch_status();
 }
 
@@ -665,8 +674,8 @@ inline int small_split(int N, int K) {
 }
 
 template <int BNX>
-inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const uint16_t* bias,
-                        uint16_t* out, cudaStream_t stream) {
+inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w, float scale, const float* scale_ptr,
+                        const uint16_t* bias, uint16_t* out, cudaStream_t stream) {
   CUtensorMap mw, mx;
   if (!get_maps(w, x, N, M, K, kBM, BNX, &mw, &mx)) return kUnsupported;
   auto kern = gemv_kernel<BNX>;
@@ -686,7 +695,7 @@ inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w,
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (cudaLaunchKernelEx(&cfg, kern, mw, mx, M, N, K, scale, bias, out) != cudaSuccess) return kCudaError;
+  if (cudaLaunchKernelEx(&cfg, kern, mw, mx, M, N, K, scale, scale_ptr, bias, out) != cudaSuccess) return kCudaError;
   return launch_status();
 }
 
@@ -702,24 +711,26 @@ inline int plan_bn(int M, int N, int K, const void* x, const void* w) {
   return 64;
 }
 
+// scale_ptr (may be null): a device float holding 1 / (sx * sw), read by the kernel in place of the
+// host-computed factor (the fused bf16 entry, whose activation scale is computed on the device).
 inline int run(int32_t M, int32_t K, int32_t N, const uint8_t* x, float sx, const uint8_t* w, float sw,
-               const uint16_t* bias, uint16_t* out, cudaStream_t stream) {
+               const uint16_t* bias, uint16_t* out, cudaStream_t stream, const float* scale_ptr = nullptr) {
   if (M < 0 || K < 0 || N < 0) return kInvalidArgument;
   if (M == 0 || N == 0) return kOk;
   if (out == nullptr || bias == nullptr || (K > 0 && (x == nullptr || w == nullptr))) return kInvalidArgument;
   const float scale = float(1.0 / (double(sx) * double(sw)));
   const int bn = K > 0 ? plan_bn(M, N, K, x, w) : 0;
   if (bn != 0 && M <= 64) {  // W-stream bound: swap-AB with split-K over a cluster
-    if (M <= 16) return launch_small<16>(M, N, K, x, w, scale, bias, out, stream);
-    if (M <= 32) return launch_small<32>(M, N, K, x, w, scale, bias, out, stream);
-    return launch_small<64>(M, N, K, x, w, scale, bias, out, stream);
+    if (M <= 16) return launch_small<16>(M, N, K, x, w, scale, scale_ptr, bias, out, stream);
+    if (M <= 32) return launch_small<32>(M, N, K, x, w, scale, scale_ptr, bias, out, stream);
+    return launch_small<64>(M, N, K, x, w, scale, scale_ptr, bias, out, stream);
   }
-  if (bn == 512) return launch_tc256(M, N, K, x, w, scale, bias, out, stream);
-  if (bn == 256) return launch_tc<256>(M, N, K, x, w, scale, bias, out, stream);
-  if (bn == 128) return launch_tc<128>(M, N, K, x, w, scale, bias, out, stream);
-  if (bn == 64) return launch_tc<64>(M, N, K, x, w, scale, bias, out, stream);
+  if (bn == 512) return launch_tc256(M, N, K, x, w, scale, scale_ptr, bias, out, stream);
+  if (bn == 256) return launch_tc<256>(M, N, K, x, w, scale, scale_ptr, bias, out, stream);
+  if (bn == 128) return launch_tc<128>(M, N, K, x, w, scale, scale_ptr, bias, out, stream);
+  if (bn == 64) return launch_tc<64>(M, N, K, x, w, scale, scale_ptr, bias, out, stream);
   dim3 grid((N + 63) / 64, (M + 63) / 64);
-  launch_pdl(simt_kernel, grid, 256, 0, stream, M, N, K, x, w, scale, bias, out);
+  launch_pdl(simt_kernel, grid, 256, 0, stream, M, N, K, x, w, scale, scale_ptr, bias, out);
   return launch_status();
 }
 
@@ -730,7 +741,7 @@ inline int run_simt(int32_t M, int32_t K, int32_t N, const uint8_t* x, float sx,
   if (M == 0 || N == 0) return kOk;
   const float scale = float(1.0 / (double(sx) * double(sw)));
   dim3 grid((N + 63) / 64, (M + 63) / 64);
-  launch_pdl(simt_kernel, grid, 256, 0, stream, M, N, K, x, w, scale, bias, out);
+  launch_pdl(simt_kernel, grid, 256, 0, stream, M, N, K, x, w, scale, static_cast<const float*>(nullptr), bias, out);
   return launch_status();
 }
 

@@ -329,6 +329,42 @@ def efficient_kan(x, grid, base_weight, spline_weight, spline_scaler, grid_size,
 
 
 # ---------------------------------------------------------------------------------- FP8 linear
+def fp8_quantize(x, q=None, scale=None):
+    """Per-tensor E4M3 quantisation of an fp32 or bf16 tensor (tasks/fp8_linear/reference.py:15-18):
+    returns (q as float8_e4m3fn with x's shape, scale as a 1-element fp32 device tensor)."""
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("fp8_quantize: x must be float32 or bfloat16")
+    _need(x, "x", x.dtype)
+    dev = x.device
+    q = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=dev) if q is None else q
+    scale = torch.empty(1, dtype=torch.float32, device=dev) if scale is None else scale
+    lib = _lib()
+    ws = workspace("fp8q", lib.b200_fp8_quantize_workspace_bytes(), dev)
+    _native.check(lib.b200_fp8_quantize_async(_ptr(x), 1 if x.dtype == torch.bfloat16 else 0, x.numel(), _ptr(q),
+                                              _ptr(scale), _ptr(ws), ws.numel(), _stream(dev)), "fp8_quantize")
+    return q, scale
+
+
+def fp8_linear_bf16(x, w_fp8, scale_w, bias, out=None, scale_x=None):
+    """The linear layer from a bf16 activation x [M, K]: quantise x on the device, then the E4M3
+    GEMM; the same bits as fp8_quantize followed by fp8_linear with the computed scale."""
+    _need(x, "x", torch.bfloat16)
+    dev = x.device
+    _need(w_fp8, "w_fp8", torch.float8_e4m3fn, dev)
+    _need(bias, "bias", torch.bfloat16, dev)
+    M, K = x.shape
+    N = w_fp8.shape[0]
+    if w_fp8.shape[1] != K or bias.numel() != N:
+        raise ValueError("fp8_linear_bf16: inconsistent shapes")
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev) if out is None else out
+    lib = _lib()
+    ws = workspace("fp8lin", lib.b200_fp8_linear_bf16_workspace_bytes(M, K), dev)
+    _native.check(lib.b200_fp8_linear_bf16_async(M, K, N, _ptr(x), _ptr(w_fp8), float(scale_w), _ptr(bias),
+                                                 _ptr(out), _opt_ptr(scale_x, None), _ptr(ws), ws.numel(),
+                                                 _stream(dev)), "fp8_linear_bf16")
+    return out
+
+
 def fp8_linear(x_fp8, scale_x, w_fp8, scale_w, bias, out=None):
     """bf16 (x_fp8 / scale_x) (w_fp8 / scale_w)^T + bias with E4M3 operands [M, K] and [N, K]."""
     _need(x_fp8, "x_fp8", torch.float8_e4m3fn)

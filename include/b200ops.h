@@ -239,6 +239,26 @@ int b200_fp8_linear_cuda_core_async(const int32_t M, const int32_t K, const int3
 int b200_fp8_linear_plan(const int32_t M, const int32_t K, const int32_t N, const uint8_t* x_fp8,
                          const uint8_t* w_fp8);
 
+/* ---------------------------------------------------------------------------------------------
+ * Per-tensor E4M3 quantisation, the step before fp8_linear (tasks/fp8_linear/reference.py:15-18,
+ * `_quantize`): scale = fp32(448 / max(max|x|, 1e-9)) (division in fp64), q = e4m3(clamp(x * scale,
+ * -448, 448)), round to nearest even, NaN kept (0x7F with the input's sign).  x holds n fp32
+ * values, or bf16 values when x_is_bf16 != 0; q receives n bytes (may be NULL: amax and scale
+ * only); scale (device, may be NULL) receives the scale.  workspace:
+ * b200_fp8_quantize_workspace_bytes() bytes, zero-filled once before first use.
+ * ------------------------------------------------------------------------------------------- */
+size_t b200_fp8_quantize_workspace_bytes(void);
+int b200_fp8_quantize_async(const void* x, int32_t x_is_bf16, int64_t n, uint8_t* q, float* scale, void* workspace,
+                            size_t workspace_bytes, void* stream);
+/* The linear layer from a bf16 activation: quantise x [M, K] on the device and run the E4M3 GEMM
+ * with it; output bit-identical to b200_fp8_quantize_async followed by b200_fp8_linear_async with
+ * the computed scale.  scale_x (device, may be NULL) receives the activation scale.  workspace:
+ * b200_fp8_linear_bf16_workspace_bytes(M, K) bytes, zero-filled once before first use. */
+size_t b200_fp8_linear_bf16_workspace_bytes(int32_t M, int32_t K);
+int b200_fp8_linear_bf16_async(const int32_t M, const int32_t K, const int32_t N, const uint16_t* x_bf16,
+                               const uint8_t* w_fp8, float scale_w, const uint16_t* bias, uint16_t* output,
+                               float* scale_x, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,43 @@ def _quantize_e4m3(x):
     return q, scale
 
 
+# Seeded inputs of the E4M3 quantisation step (tests/golden/fp8_quantize.json): name, shape, the
+# value recipe and whether the values are bf16-representable (the BASELINE sources are bf16).
+QUANT_CASES = [
+    ("randn_64x100", (64, 100), "randn", False, 1),
+    ("single", (1, 1), "randn", False, 2),
+    ("zeros_16x16", (16, 16), "zeros", False, 3),
+    ("tiny_17x33", (17, 33), "tiny", False, 4),
+    ("bf16_128x257", (128, 257), "randn", True, 5),
+    ("wide_31x129", (31, 129), "wide", False, 6),
+    ("negative_8x64", (8, 64), "negative", False, 7),
+    ("uniform_333x77", (333, 77), "uniform", False, 8),
+    ("randn_1024x1024", (1024, 1024), "randn", False, 9),
+    ("bf16_512x4096", (512, 4096), "randn", True, 10),
+]
+
+
+def quant_input(name):
+    """fp32 input of quantisation case `name` (values bf16-representable for the bf16 cases)."""
+    for nm, shape, kind, bf16, seed in QUANT_CASES:
+        if nm == name:
+            g = torch.Generator(device="cpu").manual_seed(seed)
+            if kind == "zeros":
+                x = torch.zeros(shape)
+            elif kind == "tiny":
+                x = torch.randn(shape, generator=g) * 1e-6
+            elif kind == "wide":
+                x = torch.randn(shape, generator=g) * torch.exp2(torch.randint(-20, 20, shape, generator=g).float())
+            elif kind == "negative":
+                x = -torch.randn(shape, generator=g).abs()
+            elif kind == "uniform":
+                x = torch.rand(shape, generator=g) * 6.0 - 3.0
+            else:
+                x = torch.randn(shape, generator=g)
+            return x.to(torch.bfloat16).float() if bf16 else x
+    raise KeyError(name)
+
+
 def task_inputs(task, case, seed):
     """Inputs of one reference test case on the CPU, as `make_inputs(case, seed, "cpu")`."""
     g = _gen(seed)
