@@ -547,7 +547,26 @@ def other_ops(ops, dev, world, rank):
     ms = timeit(lambda: ops.leaky(xs, m0, be, th, spikes=sp, final_mem=fm))
     res["leaky"] = {"us": ms * 1e3, "bytes": LIF_BYTES, "gbs": LIF_BYTES / ms / 1e6,
                     "frac_of_hbm": LIF_BYTES / ms / 1e6 / peak}
-    del xs, m0, be, th, sp, fm
+    bits = torch.empty(((xs.shape[0] + 31) // 32,) + tuple(xs.shape[1:]), dtype=torch.int32, device=dev)
+    ms = timeit(lambda: ops.leaky_packed(xs, m0, be, th, spike_bits=bits, final_mem=fm))
+    nbytes = LIF_BYTES - 4 * xs.numel() + bits.numel() * 4  # spikes as bits instead of fp32
+    res["leaky bit-packed spikes"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                      "frac_of_hbm": nbytes / ms / 1e6 / peak}
+    del xs, m0, be, th, sp, fm, bits
+
+    # GAE over the configs[1] batch: reward, value, next_value (f32), done, terminated (u8) in,
+    # advantage and value target (f32) out: 22 bytes per element of algorithmic traffic.
+    s = inputs.baseline_inputs("rl_pipeline", seed=rank)
+    r = s["reward"].to(dev)
+    dn = s["done"].to(dev)
+    vv = torch.randn(r.shape, device=dev) * 0.5
+    nv = torch.roll(vv, -1, dims=1)
+    adv, tgt = torch.empty_like(r), torch.empty_like(r)
+    ms = timeit(lambda: ops.gae(r, vv, nv, dn, dn, 0.99, 0.95, advantage=adv, value_target=tgt))
+    nbytes = 22 * r.numel()
+    res["gae B4096 T1000"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                              "frac_of_hbm": nbytes / ms / 1e6 / peak}
+    del r, dn, vv, nv, adv, tgt
 
     # Tensor-core ops against the measured dense bf16 peak, burst and sustained (the long GEMMs run
     # at the power-capped clock); FP8 against twice those figures (the E4M3 rate of this part is
@@ -690,10 +709,13 @@ def run_profile(ops_list, reps):
                 ops.reward_to_go(s["reward"], s["done"], s["gamma"], out=out)
             if "ppo" in ops_list:
                 ops.ppo_clip(s["current_log_prob"], s["old_log_prob"], s["advantage"], 0.2, s["entropy"], out=po)
-    if "lif" in ops_list:
+    if "lif" in ops_list or "lif_packed" in ops_list:
         s = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs.baseline_inputs("lif", 0).items()}
         for _ in range(reps):
-            ops.leaky(s["input_current"], s["mem0"], s["beta"], s["threshold"])
+            if "lif" in ops_list:
+                ops.leaky(s["input_current"], s["mem0"], s["beta"], s["threshold"])
+            if "lif_packed" in ops_list:
+                ops.leaky_packed(s["input_current"], s["mem0"], s["beta"], s["threshold"])
     if "robust_l1" in ops_list:
         s = inputs.baseline_inputs("robust_l1", 0)
         a, b = s["inp"].to(dev), s["target"].to(dev)
@@ -730,7 +752,8 @@ def main():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile", default=None,
-                    help="comma list of ops (rl_step, rtg, ppo, lif, robust_l1, kan, fp8_m16, fp8_m1024, fp8_8192, "
+                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, robust_l1, kan, fp8_m16, fp8_m1024, "
+                         "fp8_8192, "
                          "fp8_16384, fp8_ref_timed): run each --steps times for ncu, no timing")
     args = ap.parse_args()
     if args.profile:

@@ -58,9 +58,12 @@ SIGNATURES = {
     "b200_peer_exchange_destroy": (c_int, [c_p]),
     "b200_rl_step_exchange_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p,
                                             c_sz, c_p, ctypes.c_uint, ctypes.c_uint, c_p]),
+    # GAE
+    "b200_gae_async": (c_int, [c_p, c_p, c_p, c_p, c_p, c_f, c_f, c_i32, c_i32, c_p, c_p, c_p]),
     # LIF
     "b200_leaky": (None, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p]),
     "b200_leaky_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
+    "b200_leaky_packed_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
     # KAN
     "b200_efficient_kan": (None, [c_p, c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p]),
     "b200_efficient_kan_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),

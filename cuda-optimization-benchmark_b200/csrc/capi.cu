@@ -14,6 +14,7 @@
 #include "dropin/ppo_clip.cuh"
 #include "dropin/reward_to_go.cuh"
 #include "ops/fp8_pipeline.cuh"
+#include "ops/gae.cuh"
 #include "ops/rl_step.cuh"
 
 namespace {
@@ -168,6 +169,14 @@ int b200_rl_step_exchange_async(const float* reward, const uint8_t* done, float 
                                 (flags & B200_STEP_INPUTS_READY) != 0, as_stream(stream));
 }
 
+// ----------------------------------------------------------------------------------------- GAE
+int b200_gae_async(const float* reward, const float* value, const float* next_value, const uint8_t* done,
+                   const uint8_t* terminated, float gamma, float lmbda, int32_t B, int32_t T, float* advantage,
+                   float* value_target, void* stream) {
+  return b200::gae::run(reward, value, next_value, done, terminated, gamma, lmbda, B, T, advantage, value_target,
+                        as_stream(stream));
+}
+
 // ---------------------------------------------------------------------------------------- LIF
 void b200_leaky(const float* input_current, const float* mem0, const float* beta, const float* threshold,
                 int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem) {
@@ -177,6 +186,12 @@ void b200_leaky(const float* input_current, const float* mem0, const float* beta
 int b200_leaky_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
                      int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, void* stream) {
   return b200::lif::run(input_current, mem0, beta, threshold, T, B, H, spikes, final_mem, as_stream(stream));
+}
+
+int b200_leaky_packed_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                            int32_t T, int32_t B, int32_t H, uint32_t* spike_bits, float* final_mem, void* stream) {
+  return b200::lif::run_packed(input_current, mem0, beta, threshold, T, B, H, spike_bits, final_mem,
+                               as_stream(stream));
 }
 
 // --------------------------------------------------------------------------------- FP8 linear

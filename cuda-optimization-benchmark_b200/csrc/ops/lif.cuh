@@ -18,7 +18,7 @@
 // (each warp writes 512 contiguous bytes), and release the slot through its "empty" mbarrier, one
 // arrive per warp.  No CTA-wide barrier is taken per step: warps drift apart by up to the ring
 // depth, and the producer refills a slot as soon as every warp has read it.  8 bytes of HBM
-// traffic per neuron-step (read x, write spike).  Shapes whose neuron count is not a multiple of
+// traffic per neuron-step (read x, write spike); 4 + 1/8 with bit-packed spikes (run_packed).  Shapes whose neuron count is not a multiple of
 // 4, or unaligned pointers, take the one-neuron-per-thread form of the same loop.
 #pragma once
 
@@ -33,10 +33,13 @@ constexpr int kDepth = 8;   // time steps of x in flight per thread (scalar form
 
 __device__ __forceinline__ float clamp01(float b) { return fminf(fmaxf(b, 0.0f), 1.0f); }
 
-__device__ __forceinline__ float step(float& mem, float x, float beta, float th) {
+__device__ __forceinline__ bool step_bit(float& mem, float x, float beta, float th) {
   const float reset = mem >= th ? 1.0f : 0.0f;
   mem = __fsub_rn(__fadd_rn(__fmul_rn(beta, mem), x), __fmul_rn(reset, th));
-  return mem >= th ? 1.0f : 0.0f;
+  return mem >= th;
+}
+__device__ __forceinline__ float step(float& mem, float x, float beta, float th) {
+  return step_bit(mem, x, beta, th) ? 1.0f : 0.0f;
 }
 
 constexpr int kMaxDepth = 24;               // x slices in flight per CTA
@@ -44,11 +47,13 @@ constexpr int kSmemBudget = 192 * 1024;      // bytes of the x ring
 constexpr int kMaxSlab = (1024 - 32) * 4;    // neurons per CTA: consumer threads + one producer warp
 
 // Slab form (NB % 4 == 0, 16-byte aligned pointers): CTA c owns neurons [c*S, c*S + cnt); warp 0
-// produces, warps 1.. consume (thread 32 + i owns neurons 4i .. 4i + 3 of the slab).
+// produces, warps 1.. consume (thread 32 + i owns neurons 4i .. 4i + 3 of the slab).  kPacked:
+// spikes are bits, bit t % 32 of word [t / 32][neuron] (uint32), written 32 steps at a time.
+template <bool kPacked>
 __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restrict__ x, const float* __restrict__ mem0,
                                                           const float* __restrict__ beta,
                                                           const float* __restrict__ th, int T, int64_t NB, int H,
-                                                          int S, int depth, float* __restrict__ spikes,
+                                                          int S, int depth, void* __restrict__ spikes,
                                                           float* __restrict__ final_mem) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   extern __shared__ __align__(128) float xr[];  // depth slices of S floats
@@ -98,18 +103,32 @@ __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restri
       tq[j] = th[h];
     }
   }
-  float* out = spikes + n0 + 4 * i;
+  float* out = static_cast<float*>(spikes) + n0 + 4 * i;
+  uint32_t* bits = static_cast<uint32_t*>(spikes) + n0 + 4 * i;
+  uint4 pk = make_uint4(0u, 0u, 0u, 0u);
   for (int t = 0; t < T; ++t) {
     const int d = t % depth;
     if (!mbar_wait(&full[d], uint32_t(t / depth) & 1u)) break;
     if (mine) {
       const float4 xv = *reinterpret_cast<const float4*>(xr + int64_t(d) * S + 4 * i);
-      float4 sp;
-      sp.x = step(m.x, xv.x, bq[0], tq[0]);
-      sp.y = step(m.y, xv.y, bq[1], tq[1]);
-      sp.z = step(m.z, xv.z, bq[2], tq[2]);
-      sp.w = step(m.w, xv.w, bq[3], tq[3]);
-      st_stream_f4(out + int64_t(t) * NB, sp);
+      if (kPacked) {
+        const uint32_t bit = 1u << (t & 31);
+        pk.x |= step_bit(m.x, xv.x, bq[0], tq[0]) ? bit : 0u;
+        pk.y |= step_bit(m.y, xv.y, bq[1], tq[1]) ? bit : 0u;
+        pk.z |= step_bit(m.z, xv.z, bq[2], tq[2]) ? bit : 0u;
+        pk.w |= step_bit(m.w, xv.w, bq[3], tq[3]) ? bit : 0u;
+        if ((t & 31) == 31 || t == T - 1) {
+          *reinterpret_cast<uint4*>(bits + int64_t(t >> 5) * NB) = pk;
+          pk = make_uint4(0u, 0u, 0u, 0u);
+        }
+      } else {
+        float4 sp;
+        sp.x = step(m.x, xv.x, bq[0], tq[0]);
+        sp.y = step(m.y, xv.y, bq[1], tq[1]);
+        sp.z = step(m.z, xv.z, bq[2], tq[2]);
+        sp.w = step(m.w, xv.w, bq[3], tq[3]);
+        st_stream_f4(out + int64_t(t) * NB, sp);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[d]);
@@ -117,12 +136,13 @@ __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restri
   if (mine) *reinterpret_cast<float4*>(final_mem + n0 + 4 * i) = m;
 }
 
-// Scalar form: one neuron per thread, same per-neuron arithmetic.
+// Scalar form: one neuron per thread, same per-neuron arithmetic (kPacked as the slab form).
+template <bool kPacked>
 __global__ void __launch_bounds__(kThreads) lif_scalar_kernel(const float* __restrict__ x,
                                                               const float* __restrict__ mem0,
                                                               const float* __restrict__ beta,
                                                               const float* __restrict__ th, int T, int64_t NB, int H,
-                                                              float* __restrict__ spikes,
+                                                              void* __restrict__ spikes,
                                                               float* __restrict__ final_mem) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   const int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x;
@@ -135,6 +155,7 @@ __global__ void __launch_bounds__(kThreads) lif_scalar_kernel(const float* __res
 #pragma unroll
   for (int d = 0; d < kDepth; ++d)
     if (d < T) ring[d] = ld_stream_f1(x + i + int64_t(d) * NB);
+  uint32_t pk = 0;
   for (int t0 = 0; t0 < T; t0 += kDepth) {
 #pragma unroll
     for (int d = 0; d < kDepth; ++d) {
@@ -142,15 +163,24 @@ __global__ void __launch_bounds__(kThreads) lif_scalar_kernel(const float* __res
       if (t < T) {
         const float xv = ring[d];
         if (t + kDepth < T) ring[d] = ld_stream_f1(x + i + int64_t(t + kDepth) * NB);
-        st_stream_f1(spikes + i + int64_t(t) * NB, step(m, xv, b, tt));
+        if (kPacked) {
+          pk |= step_bit(m, xv, b, tt) ? (1u << (t & 31)) : 0u;
+          if ((t & 31) == 31 || t == T - 1) {
+            static_cast<uint32_t*>(spikes)[int64_t(t >> 5) * NB + i] = pk;
+            pk = 0;
+          }
+        } else {
+          st_stream_f1(static_cast<float*>(spikes) + i + int64_t(t) * NB, step(m, xv, b, tt));
+        }
       }
     }
   }
   final_mem[i] = m;
 }
 
-inline int run(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B, int32_t H,
-               float* spikes, float* final_mem, cudaStream_t stream) {
+template <bool kPacked>
+inline int run_impl(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B,
+                    int32_t H, void* spikes, float* final_mem, cudaStream_t stream) {
   if (T < 0 || B < 0 || H < 0) return kInvalidArgument;
   const int64_t NB = int64_t(B) * int64_t(H);
   if (NB == 0) return kOk;
@@ -169,14 +199,27 @@ inline int run(const float* x, const float* mem0, const float* beta, const float
     if (depth > kMaxDepth) depth = kMaxDepth;
     if (depth < 2) depth = 2;
     const size_t smem = size_t(depth) * size_t(S) * 4;
-    if (!ensure_dyn_smem(lif_slab_kernel, int(smem))) return kCudaError;
-    return launch_pdl(lif_slab_kernel, unsigned(grid), unsigned(S / 4 + 32), smem, stream, x, mem0, beta, th, T, NB, H,
-                      int(S), depth, spikes, final_mem);
-  } else {
-    const int64_t grid = (NB + kThreads - 1) / kThreads;
-    return launch_pdl(lif_scalar_kernel, unsigned(grid), kThreads, 0, stream, x, mem0, beta, th, T, NB, H, spikes,
-                      final_mem);
+    auto kern = lif_slab_kernel<kPacked>;
+    if (!ensure_dyn_smem(kern, int(smem))) return kCudaError;
+    return launch_pdl(kern, unsigned(grid), unsigned(S / 4 + 32), smem, stream, x, mem0, beta, th, T, NB, H, int(S),
+                      depth, spikes, final_mem);
   }
+  const int64_t grid = (NB + kThreads - 1) / kThreads;
+  return launch_pdl(lif_scalar_kernel<kPacked>, unsigned(grid), kThreads, 0, stream, x, mem0, beta, th, T, NB, H,
+                    spikes, final_mem);
+}
+
+// spikes: fp32 [T, B*H], 0 or 1 (the reference layout).
+inline int run(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B, int32_t H,
+               float* spikes, float* final_mem, cudaStream_t stream) {
+  return run_impl<false>(x, mem0, beta, th, T, B, H, spikes, final_mem, stream);
+}
+
+// spike_bits: uint32 [ceil(T / 32), B*H]; bit t % 32 of word [t / 32][n] is the spike of neuron n
+// at step t (bits past T are zero).  1/32 of the fp32 layout's spike bytes.
+inline int run_packed(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B,
+                      int32_t H, uint32_t* spike_bits, float* final_mem, cudaStream_t stream) {
+  return run_impl<true>(x, mem0, beta, th, T, B, H, spike_bits, final_mem, stream);
 }
 
 }  // namespace lif

@@ -291,7 +291,43 @@ def rl_step_exchange(exchange, reward, done, gamma, cur, old, adv, clip_epsilon,
     return rtg_out, ppo_out
 
 
+# ----------------------------------------------------------------------------------------- GAE
+def gae(reward, value, next_value, done, terminated, gamma, lmbda, advantage=None, value_target=None):
+    """Generalised advantage estimation over [B, T] rows: returns (advantage, value_target)."""
+    _need(reward, "reward", torch.float32)
+    dev = reward.device
+    for t, nm in ((value, "value"), (next_value, "next_value")):
+        _need(t, nm, torch.float32, dev)
+    for t, nm in ((done, "done"), (terminated, "terminated")):
+        _need(t, nm, torch.bool, dev)
+    if reward.dim() != 2 or any(t.shape != reward.shape for t in (value, next_value, done, terminated)):
+        raise ValueError("gae: all inputs must be (B, T)")
+    B, T = reward.shape
+    advantage = torch.empty_like(reward) if advantage is None else advantage
+    value_target = torch.empty_like(reward) if value_target is None else value_target
+    _native.check(_lib().b200_gae_async(_ptr(reward), _ptr(value), _ptr(next_value), _ptr(done), _ptr(terminated),
+                                        float(gamma), float(lmbda), B, T, _ptr(advantage), _ptr(value_target),
+                                        _stream(dev)), "gae")
+    return advantage, value_target
+
+
 # ----------------------------------------------------------------------------------------- LIF
+def leaky_packed(input_current, mem0, beta, threshold, spike_bits=None, final_mem=None):
+    """The LIF layer with bit-packed spikes: returns (spike_bits int32 [ceil(T/32), B, H], bit t % 32
+    of word [t // 32] being the spike at step t; final_mem [B, H])."""
+    _need(input_current, "input_current", torch.float32)
+    dev = input_current.device
+    for t, nm in ((mem0, "mem0"), (beta, "beta"), (threshold, "threshold")):
+        _need(t, nm, torch.float32, dev)
+    T, B, H = input_current.shape
+    if spike_bits is None:
+        spike_bits = torch.empty(((T + 31) // 32, B, H), dtype=torch.int32, device=dev)
+    final_mem = torch.empty((B, H), dtype=torch.float32, device=dev) if final_mem is None else final_mem
+    _native.check(_lib().b200_leaky_packed_async(_ptr(input_current), _ptr(mem0), _ptr(beta), _ptr(threshold), T, B,
+                                                 H, _ptr(spike_bits), _ptr(final_mem), _stream(dev)), "leaky_packed")
+    return spike_bits, final_mem
+
+
 def leaky(input_current, mem0, beta, threshold, spikes=None, final_mem=None):
     _need(input_current, "input_current", torch.float32)
     dev = input_current.device

@@ -188,6 +188,20 @@ int b200_rl_step_exchange_async(const float* reward, const uint8_t* done, float 
                                 unsigned epoch, unsigned flags, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Generalised advantage estimation (no reference counterpart: the step between reward_to_go and
+ * ppo_clip in the reference's source library, TorchRL's generalized_advantage_estimate; Schulman
+ * et al. 2016).  Per row of [B, T] (time along T), with done / terminated one byte per element:
+ *   delta[t] = reward[t] + gamma * next_value[t] * (1 - terminated[t]) - value[t]
+ *   advantage[t] = delta[t] + gamma * lambda * (1 - done[t]) * advantage[t + 1]  (0 past T - 1)
+ *   value_target[t] = advantage[t] + value[t]
+ * With value = next_value = 0, terminated = done and lmbda = 1 the advantages are bit-identical to
+ * b200_reward_to_go_async.
+ * ------------------------------------------------------------------------------------------- */
+int b200_gae_async(const float* reward, const float* value, const float* next_value, const uint8_t* done,
+                   const uint8_t* terminated, float gamma, float lmbda, int32_t B, int32_t T, float* advantage,
+                   float* value_target, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Leaky integrate-and-fire layer (task leaky).
  * Replaces `void reference(const float* input_current, const float* mem0, const float* beta,
  * const float* threshold, int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem)`:
@@ -197,6 +211,11 @@ void b200_leaky(const float* input_current, const float* mem0, const float* beta
                 int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem);
 int b200_leaky_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
                      int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, void* stream);
+/* Bit-packed spikes: spike_bits is uint32 [ceil(T / 32), B*H]; bit t % 32 of word [t / 32][n] is
+ * the spike of neuron n (n = b*H + h) at step t, bits past T zero.  The same arithmetic as
+ * b200_leaky_async (so the same spikes and final_mem bits); 1/32 of its spike bytes. */
+int b200_leaky_packed_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                            int32_t T, int32_t B, int32_t H, uint32_t* spike_bits, float* final_mem, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * KAN linear layer (task efficient_kan): out[B, O] = silu(x) . base_weight^T + bases(x) .

@@ -201,3 +201,26 @@ def within(out, ref, atol, rtol):
     ratio = np.where(both_nan, 0.0, err / lim)
     worst = float(np.nanmax(ratio)) if ratio.size else 0.0
     return int((~ok).sum()), worst
+
+
+def gae(inp):
+    """Generalised advantage estimation in fp64 (no reference implementation in the reference
+    repository: the published algorithm of Schulman et al. 2016 in the form of TorchRL's
+    generalized_advantage_estimate, with separate done and terminated flags):
+    delta = r + gamma * next_value * (1 - terminated) - value; A[t] = delta[t] + gamma * lambda *
+    (1 - done[t]) * A[t + 1], A past the last step 0; value_target = A + value.  gamma and lambda
+    are taken as the fp32 values the kernel receives."""
+    r = _np(inp["reward"]).astype(np.float64)
+    v = _np(inp["value"]).astype(np.float64)
+    nv = _np(inp["next_value"]).astype(np.float64)
+    done = _np(inp["done"]).astype(bool)
+    term = _np(inp["terminated"]).astype(bool)
+    g = float(np.float32(inp["gamma"]))
+    lam = float(np.float32(inp["lmbda"]))
+    delta = r + g * nv * (~term) - v
+    adv = np.zeros_like(delta)
+    a = np.zeros(delta.shape[0])
+    for t in range(delta.shape[1] - 1, -1, -1):
+        a = delta[:, t] + g * lam * (~done[:, t]) * a
+        adv[:, t] = a
+    return {"advantage": adv, "value_target": adv + v}
