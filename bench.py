@@ -109,14 +109,17 @@ def max_over_ranks(x, world):
 
 # ------------------------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples of the SM clock and throttle reasons while it runs."""
+    """nvidia-smi samples (every 100 ms) of the SM clock and throttle reasons, collected by a
+    reader thread from start to stop."""
 
     QUERY = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device):
+        import threading
         self.proc = None
+        self.lines = []
         ident = str(device)
         try:
             u = torch.cuda.get_device_properties(device).uuid
@@ -129,20 +132,33 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
+
+    def wait_first(self, timeout=5.0):
+        """Block until the first sample has arrived (nvidia-smi takes a moment to start)."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
-        time.sleep(0.25)
+        time.sleep(0.15)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+        self.reader.join(timeout=5)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for line in self.lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 8:
                 continue
@@ -264,6 +280,7 @@ def run_b200(args, world, rank, local):
         torch.cuda.synchronize(dev)
         return a.elapsed_time(b) / k
 
+    clocks = ClockSampler(dev)  # from before the warm-up to the end of the timed steps
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
@@ -291,7 +308,18 @@ def run_b200(args, world, rank, local):
         for i in range(args.warmup):
             step(i)
         torch.cuda.synchronize(dev)
-    clocks = ClockSampler(dev)
+    # Untimed soak: about 0.3 s of the same back-to-back steps just before the timed ones, so the
+    # clock samples (every 100 ms) cover the load the timed steps run under; the step count is the
+    # same on every rank (each exchange step is a collective step).
+    clocks.wait_first()
+    t_cal = time.perf_counter()
+    for i in range(50):
+        step(i)
+    torch.cuda.synchronize(dev)
+    per_step = (time.perf_counter() - t_cal) / 50
+    n_soak = int(max_over_ranks(float(min(200000, max(500, int(0.3 / max(per_step, 1e-7))))), world))
+    for i in range(n_soak):
+        step(i)
     barrier(world)
     torch.cuda.synchronize(dev)
     t0 = torch.cuda.Event(enable_timing=True)
@@ -488,7 +516,9 @@ def run_b200(args, world, rank, local):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": per_step_launches * args.steps,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
-                   "samples": clk["samples"]},
+                   "samples": clk["samples"],
+                   "window": "nvidia-smi every 100 ms over the warm-up, a 0.3 s soak of the same steps and the "
+                             "timed steps"},
     }
     if extra:
         line["ops"] = extra
