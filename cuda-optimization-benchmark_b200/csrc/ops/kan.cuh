@@ -21,7 +21,9 @@
 // each) and summed in the epilogue, which keeps K' = 9216 well inside 1e-5.  Rows of A and of W'
 // are scaled by powers of two so every value fits fp16; the epilogue undoes them.
 //   1. prep_w_kernel: W' hi/lo planes (one CTA per output row);
-//   2. prep_a_kernel: silu + Cox-de Boor bases of x in fp32, hi/lo planes (one CTA per batch row);
+//   2. silu + Cox-de Boor bases of x in fp32, hi/lo planes: for the cubic cases row_scale_kernel and
+//      prep_a2_kernel (a thread per two inputs down a block of rows, reciprocal knot differences
+//      computed once per input), otherwise prep_a_kernel (one CTA per batch row);
 //   3. gemm_kernel: persistent warp-specialised tcgen05 GEMM (kind::f16, 128 x 128 tiles, TMEM
 //      = [D0a | D0b | D0c | D1], 128-byte-swizzled TMA loads of the four planes in a 3-stage ring,
 //      12 MMAs per stage), fused combine/rescale epilogue writing fp32 rows.
@@ -287,6 +289,98 @@ __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x
   }
 }
 
+// ----------------------------------------------------------------- A planes, column-major form
+// prep_a_kernel gives each batch row to one CTA, so every (row, input) pays the whole Cox-de Boor
+// recurrence with its divisions by knot differences, which depend on the input alone.  The
+// column-major form computes each input's reciprocal knot differences once and reuses them down a
+// block of rows, with every basis step a multiply:
+//   row_scale_kernel: per row the power-of-two factor that keeps silu and the bases inside fp16
+//     (the same rule as prep_a_kernel), and the row's zero K padding;
+//   prep_a2_kernel: a thread owns two adjacent inputs (i, i + 1) and kPrepRows rows; it writes the
+//     hi / lo planes with 4-byte half2 stores (each warp a contiguous 128 bytes per plane).
+constexpr int kPrepRows = 32;
+constexpr int kPrepThreads = 128;
+
+__global__ void __launch_bounds__(256) row_scale_kernel(const float* __restrict__ x, int I, int C, int64_t kp,
+                                                        float* __restrict__ rs, __half* __restrict__ a_hi,
+                                                        __half* __restrict__ a_lo) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  __shared__ float s_red[33];
+  const int bi = blockIdx.x;
+  const float* xr = x + int64_t(bi) * I;
+  float amax = 0.0f;
+  for (int i = threadIdx.x; i < I; i += blockDim.x) amax = fmaxf(amax, fabsf(silu(xr[i])));
+  // B-spline bases on a non-decreasing grid lie in [0, 1].
+  const float f = fp16_row_factor(fmaxf(block_max(amax, s_red), 1.0f));
+  if (threadIdx.x == 0) rs[bi] = 1.0f / f;
+  const int64_t kk = int64_t(I) * (1 + C);
+  for (int64_t q = kk + threadIdx.x; q < kp; q += blockDim.x) {
+    a_hi[int64_t(bi) * kp + q] = __float2half_rn(0.0f);
+    a_lo[int64_t(bi) * kp + q] = __float2half_rn(0.0f);
+  }
+}
+
+__device__ __forceinline__ void split_store2(float v0, float v1, __half* hi, __half* lo) {
+  const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+  *reinterpret_cast<__half2*>(hi) = __halves2half2(h0, h1);
+  *reinterpret_cast<__half2*>(lo) = __halves2half2(__float2half_rn((v0 - __half2float(h0)) * kLoScale),
+                                                   __float2half_rn((v1 - __half2float(h1)) * kLoScale));
+}
+
+// grid = (ceil(I / (2 * kPrepThreads)), ceil(B / kPrepRows)); I even.  rs from row_scale_kernel.
+template <int NK, int KO>
+__global__ void __launch_bounds__(kPrepThreads) prep_a2_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ grid, int B, int I,
+                                                               int64_t kp, const float* __restrict__ rs,
+                                                               __half* __restrict__ a_hi,
+                                                               __half* __restrict__ a_lo) {
+  pdl_begin();  // the row scales are written by row_scale_kernel just before this kernel
+  constexpr int C = NK - KO - 1;
+  const int i = 2 * (int(blockIdx.x) * kPrepThreads + int(threadIdx.x));
+  if (i >= I) return;
+  // Knots and reciprocal knot differences of both inputs: rc[u][k-1][j] = 1 / (g[j+k] - g[j]).
+  float g[2][NK], rc[2][KO][NK - 1];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+#pragma unroll
+    for (int j = 0; j < NK; ++j) g[u][j] = __ldg(grid + int64_t(i + u) * NK + j);
+#pragma unroll
+    for (int k = 1; k <= KO; ++k)
+#pragma unroll
+      for (int j = 0; j + k < NK; ++j) rc[u][k - 1][j] = 1.0f / __fsub_rn(g[u][j + k], g[u][j]);
+  }
+  const int b0 = int(blockIdx.y) * kPrepRows;
+  for (int bb = 0; bb < kPrepRows; ++bb) {
+    const int b = b0 + bb;
+    if (b >= B) break;
+    const float f = 1.0f / __ldg(rs + b);  // a power of two: exact
+    const float2 xv = *reinterpret_cast<const float2*>(x + int64_t(b) * I + i);
+    float v[2][1 + C];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float xu = u == 0 ? xv.x : xv.y;
+      float bs[NK - 1];
+#pragma unroll
+      for (int j = 0; j < NK - 1; ++j) bs[j] = (xu >= g[u][j] && xu < g[u][j + 1]) ? 1.0f : 0.0f;
+#pragma unroll
+      for (int k = 1; k <= KO; ++k)
+#pragma unroll
+        for (int j = 0; j < NK - 1 - k; ++j) {
+          const float l = __fmul_rn(__fsub_rn(xu, g[u][j]), rc[u][k - 1][j]);
+          const float r = __fmul_rn(__fsub_rn(g[u][j + k + 1], xu), rc[u][k - 1][j + 1]);
+          bs[j] = __fadd_rn(__fmul_rn(l, bs[j]), __fmul_rn(r, bs[j + 1]));
+        }
+      v[u][0] = silu(xu) * f;
+#pragma unroll
+      for (int c = 0; c < C; ++c) v[u][1 + c] = bs[c] * f;
+    }
+    __half* hr = a_hi + int64_t(b) * kp + i;
+    __half* lr = a_lo + int64_t(b) * kp + i;
+#pragma unroll
+    for (int p = 0; p <= C; ++p) split_store2(v[0][p], v[1][p], hr + int64_t(p) * I, lr + int64_t(p) * I);
+  }
+}
+
 // ------------------------------------------------------------------------------------- GEMM
 __device__ __forceinline__ void tile_coords(int tile, int n_m, int n_n, int& mb, int& nb) {
   const int group = kGroupM * n_n;
@@ -474,9 +568,21 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   float* cs = reinterpret_cast<float*>(w + L.cs);
   const int64_t kp = padded_k(I, C);
   launch_pdl(prep_w_kernel, O, 256, 0, stream, wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
-  if (G == 5 && K == 3) launch_pdl(prep_a_kernel<12, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
-  else if (G == 8 && K == 3) launch_pdl(prep_a_kernel<15, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
-  else launch_pdl(prep_a_kernel<0, 0>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  // Column-major form for the cubic cases; its float2 loads of x need I even and x 8-byte aligned.
+  if (K == 3 && (G == 5 || G == 8) && I % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) {
+    launch_pdl(row_scale_kernel, B, 256, 0, stream, x, I, C, kp, rs, a_hi, a_lo);
+    const dim3 pg(unsigned((I + 2 * kPrepThreads - 1) / (2 * kPrepThreads)), unsigned((B + kPrepRows - 1) / kPrepRows));
+    if (G == 5) launch_pdl(prep_a2_kernel<12, 3>, pg, kPrepThreads, 0, stream, x, grid, B, I, kp,
+                           static_cast<const float*>(rs), a_hi, a_lo);
+    else launch_pdl(prep_a2_kernel<15, 3>, pg, kPrepThreads, 0, stream, x, grid, B, I, kp,
+                    static_cast<const float*>(rs), a_hi, a_lo);
+  } else if (G == 5 && K == 3) {
+    launch_pdl(prep_a_kernel<12, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  } else if (G == 8 && K == 3) {
+    launch_pdl(prep_a_kernel<15, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  } else {
+    launch_pdl(prep_a_kernel<0, 0>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
+  }
   CUtensorMap m_ahi, m_alo, m_whi, m_wlo;
   if (!tc::make_map_sw128(&m_ahi, a_hi, uint64_t(B), uint64_t(kp), 2, kBM) ||
       !tc::make_map_sw128(&m_alo, a_lo, uint64_t(B), uint64_t(kp), 2, kBM) ||

@@ -6,6 +6,8 @@
 - The BASELINE.json configuration (B 8192, I 1024, O 1024, G 5, K 3) against the fp64 oracle on a
   seeded subset of rows.
 - Inputs with |silu(x)| far beyond the fp16 range (the row scaling path).
+- The row-major A-plane preparation (odd I, or x not 8-byte aligned), beside the column-major one
+  the cubic cases take otherwise.
 """
 import numpy as np
 import pytest
@@ -83,6 +85,27 @@ def test_large_inputs_use_row_scaling(lib):
     s["x"][2, 7] = -3.0e4
     s["base_weight"][5, 1] = 3.0e5  # a weight beyond fp16
     out = _run_async(lib, s)
+    ref = exact.efficient_kan(s)["out"]
+    bad, worst = exact.within(out.double().cpu().numpy(), ref, ATOL, RTOL)
+    assert bad == 0, worst
+
+
+@pytest.mark.parametrize("I,shift", [(41, 0), (100, 1)], ids=["odd_I", "x_4_byte_aligned"])
+def test_row_major_prep_path(lib, I, shift):
+    s = inputs.task_inputs("efficient_kan", {"B": 9, "I": I, "O": 70}, 11)
+    dev = torch.device("cuda")
+    t = {k: s[k].to(dev) for k in IN_NAMES}
+    if shift:
+        raw = torch.empty(s["x"].numel() + shift, dtype=torch.float32, device=dev)
+        t["x"] = raw[shift:].view(s["x"].shape)
+        t["x"].copy_(s["x"])
+    out = torch.empty(s["B"], s["O"], device=dev)
+    nbytes = lib.b200_efficient_kan_workspace_bytes(s["grid_size"], s["spline_order"], s["B"], s["I"], s["O"])
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    st = lib.b200_efficient_kan_async(*(t[k].data_ptr() for k in IN_NAMES), s["grid_size"], s["spline_order"],
+                                      s["B"], s["I"], s["O"], out.data_ptr(), ws.data_ptr(), nbytes, None)
+    torch.cuda.synchronize()
+    assert st == 0
     ref = exact.efficient_kan(s)["out"]
     bad, worst = exact.within(out.double().cpu().numpy(), ref, ATOL, RTOL)
     assert bad == 0, worst
