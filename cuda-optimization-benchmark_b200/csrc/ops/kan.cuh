@@ -301,20 +301,36 @@ __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x
 constexpr int kPrepRows = 32;
 constexpr int kPrepThreads = 128;
 
-__global__ void __launch_bounds__(256) row_scale_kernel(const float* __restrict__ x, int I, int C, int64_t kp,
-                                                        float* __restrict__ rs, __half* __restrict__ a_hi,
-                                                        __half* __restrict__ a_lo) {
+// One warp per row.  The amax takes silu with fast intrinsics: the factor is a power of two chosen
+// with a 4x margin below the fp16 maximum (kFp16Safe), so an amax a few ulps low can at most double
+// the factor and every scaled value still fits fp16.
+constexpr int kScaleRowsPerCta = 8;
+__global__ void __launch_bounds__(32 * kScaleRowsPerCta) row_scale_kernel(const float* __restrict__ x, int B, int I,
+                                                                          int C, int64_t kp, float* __restrict__ rs,
+                                                                          __half* __restrict__ a_hi,
+                                                                          __half* __restrict__ a_lo) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
-  __shared__ float s_red[33];
-  const int bi = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int bi = int(blockIdx.x) * kScaleRowsPerCta + int(threadIdx.x >> 5);
+  if (bi >= B) return;
   const float* xr = x + int64_t(bi) * I;
   float amax = 0.0f;
-  for (int i = threadIdx.x; i < I; i += blockDim.x) amax = fmaxf(amax, fabsf(silu(xr[i])));
+  auto silu_fast = [](float v) { return __fdividef(v, 1.0f + __expf(-v)); };
+  if ((I & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    for (int q = lane; q < I / 4; q += 32) {
+      const float4 v = ld_stream_f4(xr + 4 * q);
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(silu_fast(v.x)), fabsf(silu_fast(v.y))),
+                               fmaxf(fabsf(silu_fast(v.z)), fabsf(silu_fast(v.w)))));
+    }
+  } else {
+    for (int i = lane; i < I; i += 32) amax = fmaxf(amax, fabsf(silu_fast(xr[i])));
+  }
+  amax = warp_max(amax);
   // B-spline bases on a non-decreasing grid lie in [0, 1].
-  const float f = fp16_row_factor(fmaxf(block_max(amax, s_red), 1.0f));
-  if (threadIdx.x == 0) rs[bi] = 1.0f / f;
+  const float f = fp16_row_factor(fmaxf(amax, 1.0f));
+  if (lane == 0) rs[bi] = 1.0f / f;
   const int64_t kk = int64_t(I) * (1 + C);
-  for (int64_t q = kk + threadIdx.x; q < kp; q += blockDim.x) {
+  for (int64_t q = kk + lane; q < kp; q += 32) {
     a_hi[int64_t(bi) * kp + q] = __float2half_rn(0.0f);
     a_lo[int64_t(bi) * kp + q] = __float2half_rn(0.0f);
   }
@@ -570,7 +586,8 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   launch_pdl(prep_w_kernel, O, 256, 0, stream, wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
   // Column-major form for the cubic cases; its float2 loads of x need I even and x 8-byte aligned.
   if (K == 3 && (G == 5 || G == 8) && I % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) {
-    launch_pdl(row_scale_kernel, B, 256, 0, stream, x, I, C, kp, rs, a_hi, a_lo);
+    launch_pdl(row_scale_kernel, unsigned((B + kScaleRowsPerCta - 1) / kScaleRowsPerCta), 32 * kScaleRowsPerCta, 0,
+               stream, x, B, I, C, kp, rs, a_hi, a_lo);
     const dim3 pg(unsigned((I + 2 * kPrepThreads - 1) / (2 * kPrepThreads)), unsigned((B + kPrepRows - 1) / kPrepRows));
     if (G == 5) launch_pdl(prep_a2_kernel<12, 3>, pg, kPrepThreads, 0, stream, x, grid, B, I, kp,
                            static_cast<const float*>(rs), a_hi, a_lo);
