@@ -366,6 +366,33 @@ def run_b200(args, world, rank, local):
         if status[0] != 0:
             raise RuntimeError(f"rl_step returned status {status[0]}")
 
+    # The same steps with the done flags as bits (B200_STEP_DONE_BITS, packed once per input set
+    # outside the timed loop), and reward-to-go alone from bits: 1/8 instead of 1 byte per flag.
+    bits_ms = rtg_bits_ms = None
+    if world == 1:
+        words = [ops.pack_done(s["done"]) for s in sets]
+        torch.cuda.synchronize(dev)
+        bits_args = [a[:1] + (P(w.data_ptr()),) + a[2:-2] + (READY | ops.STEP_DONE_BITS, cs)
+                     for a, w in zip(step_args, words)]
+        rtgb_args = [(a[0], P(w.data_ptr())) + a[2:] for a, w in zip(rtg_args, words)]
+        f_rtgb = lib.b200_reward_to_go_bits_async
+
+        def bits_step(i):
+            status[0] |= f_step(*bits_args[i % ROTATE])
+
+        def rtg_bits(i):
+            status[0] |= f_rtgb(*rtgb_args[i % ROTATE])
+        for i in range(args.warmup):
+            bits_step(i)
+            rtg_bits(i)
+        torch.cuda.synchronize(dev)
+        bits_ms = loop_ms(bits_step, args.steps)
+        rtg_bits_ms = loop_ms(rtg_bits, args.steps)
+        if status[0] != 0:
+            raise RuntimeError(f"done-bits step returned status {status[0]}")
+        rtgb_bytes = 8 * B * T + 4 * B * ((T + 31) // 32)
+        bits_bytes = rtgb_bytes + PPO_BYTES
+
     # The two ops as separate launches on the same rotation (per-op breakdown, unfused step time).
     for i in range(args.warmup):
         f_rtg(*rtg_args[i % ROTATE])
@@ -412,35 +439,51 @@ def run_b200(args, world, rank, local):
         graph_ms = g0.elapsed_time(g1) / args.steps
         del graphs
 
-    # ---- e2e: same entry points, inputs from pinned host memory, results read back each step
+    # ---- e2e: same entry points, inputs from pinned host memory, results read back each step.
+    # PCIe is full duplex: a step's results are read back on a copy stream while the next step's
+    # inputs go up, so the outputs and their host copies alternate between two buffers (step i + 2
+    # writes buffer i % 2 only after step i's read-back of it has finished).
     host = []
     for s in sets[:2]:
         host.append({k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in s.items()})
     dbuf = {k: torch.empty_like(v) for k, v in sets[0].items() if isinstance(v, torch.Tensor)}
-    rtg_host = torch.empty(B, T).pin_memory()
-    ppo_host = torch.empty(7).pin_memory()
+    rtg_o = [rtg_out, torch.empty_like(rtg_out)]
+    ppo_o = [ppo_out, torch.empty_like(ppo_out)]
+    rtg_host = [torch.empty(B, T).pin_memory() for _ in range(2)]
+    ppo_host = [torch.empty(7).pin_memory() for _ in range(2)]
     names = ["reward", "done", "current_log_prob", "old_log_prob", "advantage", "entropy"]
     h2d = sum(dbuf[k].numel() * dbuf[k].element_size() for k in names)
-    d2h = rtg_host.numel() * 4 + ppo_host.numel() * 4
+    d2h = rtg_host[0].numel() * 4 + ppo_host[0].numel() * 4
+    copy_stream = torch.cuda.Stream(dev)
+    read_done = [None, None]
 
     def e2e_step(i):
         h = host[i % 2]
+        j = i % 2
         for k in names:
             dbuf[k].copy_(h[k], non_blocking=True)
+        if read_done[j] is not None:
+            stream.wait_event(read_done[j])  # buffer j's previous results have reached the host
         if world == 1:
             ops.rl_step(dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"], dbuf["old_log_prob"],
-                        dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out, ppo_out=ppo_out)
+                        dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_o[j], ppo_out=ppo_o[j])
         elif exchange is not None:
             ops.rl_step_exchange(exchange, dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"],
-                                 dbuf["old_log_prob"], dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out,
-                                 ppo_out=ppo_out)
+                                 dbuf["old_log_prob"], dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_o[j],
+                                 ppo_out=ppo_o[j])
         else:
             ops.rl_step_shard(dbuf["reward"], dbuf["done"], gamma, dbuf["current_log_prob"], dbuf["old_log_prob"],
-                              dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_out, partials_out=local_parts)
+                              dbuf["advantage"], eps, dbuf["entropy"], rtg_out=rtg_o[j], partials_out=local_parts)
             dist.all_gather_into_tensor(all_parts, local_parts)
-            ops.ppo_finish(all_parts, world * N_SAMPLES, True, out=ppo_out)
-        rtg_host.copy_(rtg_out, non_blocking=True)
-        ppo_host.copy_(ppo_out, non_blocking=True)
+            ops.ppo_finish(all_parts, world * N_SAMPLES, True, out=ppo_o[j])
+        computed = torch.cuda.Event()
+        computed.record(stream)
+        copy_stream.wait_event(computed)
+        with torch.cuda.stream(copy_stream):
+            rtg_host[j].copy_(rtg_o[j], non_blocking=True)
+            ppo_host[j].copy_(ppo_o[j], non_blocking=True)
+            read_done[j] = torch.cuda.Event()
+            read_done[j].record(copy_stream)
 
     e2e_steps = max(3, min(args.steps, 50))
     for i in range(3):
@@ -452,6 +495,7 @@ def run_b200(args, world, rank, local):
     a.record(stream)
     for i in range(e2e_steps):
         e2e_step(i)
+    stream.wait_stream(copy_stream)  # the last read-back is inside the timed region
     b.record(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
@@ -497,6 +541,9 @@ def run_b200(args, world, rank, local):
             "rl_step (fused, inputs not declared ready)": (
                 {"us": waitfirst_ms * 1e3, "gbs": step_bytes / (waitfirst_ms * 1e-3) / 1e9,
                  "frac_of_hbm": step_bytes / (waitfirst_ms * 1e-3) / 1e9 / peak} if waitfirst_ms else None),
+            "rl_step (fused, done as bits)": (
+                {"us": bits_ms * 1e3, "bytes": bits_bytes, "gbs": bits_bytes / (bits_ms * 1e-3) / 1e9,
+                 "frac_of_hbm": bits_bytes / (bits_ms * 1e-3) / 1e9 / peak} if bits_ms else None),
             "note": "each op timed alone, back to back on the same input rotation",
             "reward_to_go": {"us": rtg_ms * 1e3, "bytes": RTG_BYTES,
                              "gbs": RTG_BYTES / (rtg_ms * 1e-3) / 1e9,
@@ -504,6 +551,9 @@ def run_b200(args, world, rank, local):
             "ppo_clip_ext": {"us": ppo_ms * 1e3, "bytes": PPO_BYTES,
                              "gbs": PPO_BYTES / (ppo_ms * 1e-3) / 1e9,
                              "frac_of_hbm": PPO_BYTES / (ppo_ms * 1e-3) / 1e9 / peak},
+            "reward_to_go, done as bits": (
+                {"us": rtg_bits_ms * 1e3, "bytes": rtgb_bytes, "gbs": rtgb_bytes / (rtg_bits_ms * 1e-3) / 1e9,
+                 "frac_of_hbm": rtgb_bytes / (rtg_bits_ms * 1e-3) / 1e9 / peak} if rtg_bits_ms else None),
         },
         "roofline": {"bound": "hbm", "kernel": "rl::step_kernel (reward_to_go + ppo_clip_ext, one launch)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -513,7 +563,9 @@ def run_b200(args, world, rank, local):
                      "traffic": profiled_traffic("rl_step"),
                      "traffic_source": TRAFFIC_FILES["rl_step"]},
         "e2e": {"value": world * N_SAMPLES / (e2e_ms * 1e-3), "unit": "samples/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "pipeline": "each step's results are read back on a second stream while the next step's inputs "
+                            "go up (PCIe full duplex)"},
         "gpu_launches": per_step_launches * args.steps,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                    "samples": clk["samples"],
@@ -582,7 +634,32 @@ def other_ops(ops, dev, world, rank):
     nbytes = LIF_BYTES - 4 * xs.numel() + bits.numel() * 4  # spikes as bits instead of fp32
     res["leaky bit-packed spikes"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
                                       "frac_of_hbm": nbytes / ms / 1e6 / peak}
-    del xs, m0, be, th, sp, fm, bits
+    del bits
+    # Training: the forward that also stores the membrane checkpoints (one per 32 steps), then the
+    # surrogate-gradient backward: x and grad_spikes in, grad_input out (12 bytes per neuron-step)
+    # plus the checkpoints, grad_final_mem in and grad_mem0 out.
+    import ctypes
+    lib, P = ops._lib(), ctypes.c_void_p
+    T_, B_, H_ = xs.shape
+    ck = torch.empty(((T_ + 31) // 32, B_, H_), device=dev)
+    gs, gx = torch.randn_like(xs), torch.empty_like(xs)
+    gf, gm = torch.randn_like(m0), torch.empty_like(m0)
+    gb, gt = torch.empty_like(be), torch.empty_like(th)
+    wsb = torch.empty(lib.b200_leaky_backward_workspace_bytes(B_, H_), dtype=torch.uint8, device=dev)
+    cur = lambda: P(torch.cuda.current_stream(dev).cuda_stream)
+    ms = timeit(lambda: lib.b200_leaky_train_async(xs.data_ptr(), m0.data_ptr(), be.data_ptr(), th.data_ptr(), T_,
+                                                   B_, H_, sp.data_ptr(), fm.data_ptr(), ck.data_ptr(), cur()))
+    nbytes = LIF_BYTES + ck.numel() * 4
+    res["leaky training forward (+checkpoints)"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                                    "frac_of_hbm": nbytes / ms / 1e6 / peak}
+    ms = timeit(lambda: lib.b200_leaky_backward_async(xs.data_ptr(), ck.data_ptr(), be.data_ptr(), th.data_ptr(), T_,
+                                                      B_, H_, gs.data_ptr(), gf.data_ptr(), 2.0, gx.data_ptr(),
+                                                      gm.data_ptr(), gb.data_ptr(), gt.data_ptr(), wsb.data_ptr(),
+                                                      wsb.numel(), cur()))
+    nbytes = 12 * xs.numel() + ck.numel() * 4 + 8 * m0.numel()
+    res["leaky surrogate backward"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                       "frac_of_hbm": nbytes / ms / 1e6 / peak}
+    del xs, m0, be, th, sp, fm, ck, gs, gx, gf, gm, gb, gt, wsb
 
     # GAE over the configs[1] batch: reward, value, next_value (f32), done, terminated (u8) in,
     # advantage and value target (f32) out: 22 bytes per element of algorithmic traffic.
@@ -739,13 +816,18 @@ def run_profile(ops_list, reps):
                 ops.reward_to_go(s["reward"], s["done"], s["gamma"], out=out)
             if "ppo" in ops_list:
                 ops.ppo_clip(s["current_log_prob"], s["old_log_prob"], s["advantage"], 0.2, s["entropy"], out=po)
-    if "lif" in ops_list or "lif_packed" in ops_list:
+    if "lif" in ops_list or "lif_packed" in ops_list or "lif_backward" in ops_list:
         s = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs.baseline_inputs("lif", 0).items()}
+        if "lif_backward" in ops_list:
+            _, _, ck = ops.leaky_train(s["input_current"], s["mem0"], s["beta"], s["threshold"])
+            gs = torch.randn_like(s["input_current"])
         for _ in range(reps):
             if "lif" in ops_list:
                 ops.leaky(s["input_current"], s["mem0"], s["beta"], s["threshold"])
             if "lif_packed" in ops_list:
                 ops.leaky_packed(s["input_current"], s["mem0"], s["beta"], s["threshold"])
+            if "lif_backward" in ops_list:
+                ops.leaky_backward(s["input_current"], ck, s["beta"], s["threshold"], gs, None, 2.0)
     if "robust_l1" in ops_list:
         s = inputs.baseline_inputs("robust_l1", 0)
         a, b = s["inp"].to(dev), s["target"].to(dev)
@@ -782,7 +864,7 @@ def main():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile", default=None,
-                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, robust_l1, kan, fp8_m16, fp8_m1024, "
+                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, lif_backward, robust_l1, kan, fp8_m16, fp8_m1024, "
                          "fp8_8192, "
                          "fp8_16384, fp8_ref_timed): run each --steps times for ncu, no timing")
     args = ap.parse_args()

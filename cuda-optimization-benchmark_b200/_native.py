@@ -42,6 +42,8 @@ SIGNATURES = {
     # reward-to-go
     "b200_reward_to_go": (None, [c_p, c_p, c_f, c_i32, c_i32, c_p]),
     "b200_reward_to_go_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p]),
+    "b200_pack_done_async": (c_int, [c_p, c_i32, c_i32, c_p, c_p]),
+    "b200_reward_to_go_bits_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p]),
     # fused RL step (reward-to-go + PPO in one launch)
     "b200_rl_step_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p, c_sz,
                                    c_p]),
@@ -64,6 +66,12 @@ SIGNATURES = {
     "b200_leaky": (None, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p]),
     "b200_leaky_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
     "b200_leaky_packed_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_p]),
+    "b200_leaky_checkpoint_bytes": (c_i64, [c_i32, c_i32, c_i32]),
+    "b200_leaky_train_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_p, c_p]),
+    "b200_leaky_checkpoints_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p]),
+    "b200_leaky_backward_workspace_bytes": (c_i64, [c_i32, c_i32]),
+    "b200_leaky_backward_async": (c_int, [c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_p, c_p, c_f, c_p, c_p, c_p,
+                                          c_p, c_p, c_i64, c_p]),
     # KAN
     "b200_efficient_kan": (None, [c_p, c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p]),
     "b200_efficient_kan_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),

@@ -15,6 +15,7 @@
 #include "dropin/reward_to_go.cuh"
 #include "ops/fp8_pipeline.cuh"
 #include "ops/gae.cuh"
+#include "ops/lif_backward.cuh"
 #include "ops/rl_step.cuh"
 
 namespace {
@@ -111,6 +112,15 @@ int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamm
   return b200::rtg::run(reward, done, gamma, B, T, output, as_stream(stream));
 }
 
+int b200_pack_done_async(const uint8_t* done, int32_t B, int32_t T, uint32_t* done_bits, void* stream) {
+  return b200::rtg::pack_done(done, B, T, done_bits, as_stream(stream));
+}
+
+int b200_reward_to_go_bits_async(const float* reward, const uint32_t* done_bits, float gamma, int32_t B, int32_t T,
+                                 float* output, void* stream) {
+  return b200::rtg::run_bits(reward, done_bits, gamma, B, T, output, as_stream(stream));
+}
+
 // ------------------------------------------------------------------------------ fused RL step
 int b200_rl_step_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T, float* rtg_out,
                        const float* current_log_prob, const float* old_log_prob, const float* advantage,
@@ -124,10 +134,10 @@ int b200_rl_step_ex_async(const float* reward, const uint8_t* done, float gamma,
                           float* rtg_out, const float* current_log_prob, const float* old_log_prob,
                           const float* advantage, const float* entropy, int64_t n, float clip_epsilon, float* ppo_out,
                           void* workspace, size_t workspace_bytes, unsigned flags, void* stream) {
-  if (flags & ~unsigned(B200_STEP_INPUTS_READY)) return b200::kInvalidArgument;
+  if (flags & ~unsigned(B200_STEP_INPUTS_READY | B200_STEP_DONE_BITS)) return b200::kInvalidArgument;
   return b200::rl::run(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy, n,
                        clip_epsilon, ppo_out, workspace, workspace_bytes, true, nullptr,
-                       (flags & B200_STEP_INPUTS_READY) != 0, as_stream(stream));
+                       (flags & B200_STEP_INPUTS_READY) != 0, (flags & B200_STEP_DONE_BITS) != 0, as_stream(stream));
 }
 
 int b200_rl_step_shard_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
@@ -135,7 +145,7 @@ int b200_rl_step_shard_async(const float* reward, const uint8_t* done, float gam
                              const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
                              void* partials, void* stream) {
   return b200::rl::run(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy, n,
-                       clip_epsilon, nullptr, nullptr, 0, false, partials, false, as_stream(stream));
+                       clip_epsilon, nullptr, nullptr, 0, false, partials, false, false, as_stream(stream));
 }
 
 // ------------------------------------------------------------- multi-GPU peer exchange (NVLink)
@@ -162,11 +172,12 @@ int b200_rl_step_exchange_async(const float* reward, const uint8_t* done, float 
                                 const float* advantage, const float* entropy, int64_t n, float clip_epsilon,
                                 float* ppo_out, void* workspace, size_t workspace_bytes, void* exchange,
                                 unsigned epoch, unsigned flags, void* stream) {
-  if (flags & ~unsigned(B200_STEP_INPUTS_READY)) return b200::kInvalidArgument;
+  if (flags & ~unsigned(B200_STEP_INPUTS_READY | B200_STEP_DONE_BITS)) return b200::kInvalidArgument;
   return b200::rl::run_exchange(reward, done, gamma, B, T, rtg_out, current_log_prob, old_log_prob, advantage, entropy,
                                 n, clip_epsilon, ppo_out, workspace, workspace_bytes,
                                 static_cast<const b200::PeerExchange*>(exchange), epoch,
-                                (flags & B200_STEP_INPUTS_READY) != 0, as_stream(stream));
+                                (flags & B200_STEP_INPUTS_READY) != 0, (flags & B200_STEP_DONE_BITS) != 0,
+                                as_stream(stream));
 }
 
 // ----------------------------------------------------------------------------------------- GAE
@@ -192,6 +203,39 @@ int b200_leaky_packed_async(const float* input_current, const float* mem0, const
                             int32_t T, int32_t B, int32_t H, uint32_t* spike_bits, float* final_mem, void* stream) {
   return b200::lif::run_packed(input_current, mem0, beta, threshold, T, B, H, spike_bits, final_mem,
                                as_stream(stream));
+}
+
+int64_t b200_leaky_checkpoint_bytes(int32_t T, int32_t B, int32_t H) {
+  if (T < 0 || B < 0 || H < 0) return -1;
+  return b200::lif::checkpoint_count(T) * int64_t(B) * int64_t(H) * int64_t(sizeof(float));
+}
+
+int b200_leaky_train_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                           int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, float* checkpoints,
+                           void* stream) {
+  return b200::lif::run_train(input_current, mem0, beta, threshold, T, B, H, spikes, final_mem, checkpoints,
+                              as_stream(stream));
+}
+
+int b200_leaky_checkpoints_async(const float* input_current, const float* mem0, const float* beta,
+                                 const float* threshold, int32_t T, int32_t B, int32_t H, float* checkpoints,
+                                 void* stream) {
+  return b200::lif::run_checkpoints(input_current, mem0, beta, threshold, T, B, H, checkpoints, as_stream(stream));
+}
+
+int64_t b200_leaky_backward_workspace_bytes(int32_t B, int32_t H) {
+  if (B < 0 || H < 0) return -1;
+  return b200::lif::backward_workspace_bytes(B, H);
+}
+
+int b200_leaky_backward_async(const float* input_current, const float* checkpoints, const float* beta,
+                              const float* threshold, int32_t T, int32_t B, int32_t H, const float* grad_spikes,
+                              const float* grad_final_mem, float alpha, float* grad_input, float* grad_mem0,
+                              float* grad_beta, float* grad_threshold, void* workspace, int64_t workspace_bytes,
+                              void* stream) {
+  return b200::lif::backward(input_current, checkpoints, beta, threshold, T, B, H, grad_spikes, grad_final_mem, alpha,
+                             grad_input, grad_mem0, grad_beta, grad_threshold, workspace, workspace_bytes,
+                             as_stream(stream));
 }
 
 // --------------------------------------------------------------------------------- FP8 linear

@@ -20,6 +20,10 @@
 // depth, and the producer refills a slot as soon as every warp has read it.  8 bytes of HBM
 // traffic per neuron-step (read x, write spike); 4 + 1/8 with bit-packed spikes (run_packed).  Shapes whose neuron count is not a multiple of
 // 4, or unaligned pointers, take the one-neuron-per-thread form of the same loop.
+//
+// For training (lif_backward.cuh) the same loop also stores the membrane state every kSeg steps,
+// checkpoint k being the state before step k * kSeg (checkpoint 0 = mem0): 1/8 byte per
+// neuron-step, from which the backward recomputes each kSeg-step segment in registers.
 #pragma once
 
 #include "../common/b200_common.cuh"
@@ -42,19 +46,25 @@ __device__ __forceinline__ float step(float& mem, float x, float beta, float th)
   return step_bit(mem, x, beta, th) ? 1.0f : 0.0f;
 }
 
+constexpr int kSeg = 32;                    // time steps per membrane checkpoint
 constexpr int kMaxDepth = 24;               // x slices in flight per CTA
 constexpr int kSmemBudget = 192 * 1024;      // bytes of the x ring
 constexpr int kMaxSlab = (1024 - 32) * 4;    // neurons per CTA: consumer threads + one producer warp
 
+// Spike outputs: fp32 [T, B*H] (the reference layout), bits (bit t % 32 of uint32 word
+// [t / 32][neuron], written 32 steps at a time), or none (checkpoints only).
+enum Out { kOutFloat = 0, kOutBits = 1, kOutNone = 2 };
+
 // Slab form (NB % 4 == 0, 16-byte aligned pointers): CTA c owns neurons [c*S, c*S + cnt); warp 0
-// produces, warps 1.. consume (thread 32 + i owns neurons 4i .. 4i + 3 of the slab).  kPacked:
-// spikes are bits, bit t % 32 of word [t / 32][neuron] (uint32), written 32 steps at a time.
-template <bool kPacked>
+// produces, warps 1.. consume (thread 32 + i owns neurons 4i .. 4i + 3 of the slab).  kCkpt: store
+// the checkpoints to ckpt [ceil(T / kSeg), B*H].
+template <int kOut, bool kCkpt>
 __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restrict__ x, const float* __restrict__ mem0,
                                                           const float* __restrict__ beta,
                                                           const float* __restrict__ th, int T, int64_t NB, int H,
                                                           int S, int depth, void* __restrict__ spikes,
-                                                          float* __restrict__ final_mem) {
+                                                          float* __restrict__ final_mem, float* __restrict__ ckpt) {
+  constexpr bool kPacked = kOut != kOutFloat;  // the lean loop (see the producer)
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   extern __shared__ __align__(128) float xr[];  // depth slices of S floats
   __shared__ uint64_t full[kMaxDepth], empty[kMaxDepth];
@@ -136,8 +146,14 @@ __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restri
     }
     if (!(kPacked ? mbar_wait_sleep(&full[d], ph) : mbar_wait(&full[d], ph))) break;
     if (mine) {
+      if (kCkpt && (t % kSeg) == 0) *reinterpret_cast<float4*>(ckpt + int64_t(t / kSeg) * NB + n0 + 4 * i) = m;
       const float4 xv = *reinterpret_cast<const float4*>(xs + d * S);
-      if (kPacked) {
+      if (kOut == kOutNone) {
+        step_bit(m.x, xv.x, bq[0], tq[0]);
+        step_bit(m.y, xv.y, bq[1], tq[1]);
+        step_bit(m.z, xv.z, bq[2], tq[2]);
+        step_bit(m.w, xv.w, bq[3], tq[3]);
+      } else if (kPacked) {
         const uint32_t bit = 1u << (t & 31);
         pk.x |= step_bit(m.x, xv.x, bq[0], tq[0]) ? bit : 0u;
         pk.y |= step_bit(m.y, xv.y, bq[1], tq[1]) ? bit : 0u;
@@ -164,17 +180,17 @@ __global__ void __launch_bounds__(1024, 1) lif_slab_kernel(const float* __restri
       ph ^= 1u;
     }
   }
-  if (mine) *reinterpret_cast<float4*>(final_mem + n0 + 4 * i) = m;
+  if (mine && final_mem != nullptr) *reinterpret_cast<float4*>(final_mem + n0 + 4 * i) = m;
 }
 
-// Scalar form: one neuron per thread, same per-neuron arithmetic (kPacked as the slab form).
-template <bool kPacked>
+// Scalar form: one neuron per thread, same per-neuron arithmetic (kOut, kCkpt as the slab form).
+template <int kOut, bool kCkpt>
 __global__ void __launch_bounds__(kThreads) lif_scalar_kernel(const float* __restrict__ x,
                                                               const float* __restrict__ mem0,
                                                               const float* __restrict__ beta,
                                                               const float* __restrict__ th, int T, int64_t NB, int H,
                                                               void* __restrict__ spikes,
-                                                              float* __restrict__ final_mem) {
+                                                              float* __restrict__ final_mem, float* __restrict__ ckpt) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   const int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x;
   if (i >= NB) return;
@@ -194,7 +210,10 @@ __global__ void __launch_bounds__(kThreads) lif_scalar_kernel(const float* __res
       if (t < T) {
         const float xv = ring[d];
         if (t + kDepth < T) ring[d] = ld_stream_f1(x + i + int64_t(t + kDepth) * NB);
-        if (kPacked) {
+        if (kCkpt && (t % kSeg) == 0) ckpt[int64_t(t / kSeg) * NB + i] = m;
+        if (kOut == kOutNone) {
+          step_bit(m, xv, b, tt);
+        } else if (kOut == kOutBits) {
           pk |= step_bit(m, xv, b, tt) ? (1u << (t & 31)) : 0u;
           if ((t & 31) == 31 || t == T - 1) {
             static_cast<uint32_t*>(spikes)[int64_t(t >> 5) * NB + i] = pk;
@@ -206,19 +225,22 @@ __global__ void __launch_bounds__(kThreads) lif_scalar_kernel(const float* __res
       }
     }
   }
-  final_mem[i] = m;
+  if (final_mem != nullptr) final_mem[i] = m;
 }
 
-template <bool kPacked>
+template <int kOut, bool kCkpt>
 inline int run_impl(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B,
-                    int32_t H, void* spikes, float* final_mem, cudaStream_t stream) {
+                    int32_t H, void* spikes, float* final_mem, float* ckpt, cudaStream_t stream) {
   if (T < 0 || B < 0 || H < 0) return kInvalidArgument;
   const int64_t NB = int64_t(B) * int64_t(H);
   if (NB == 0) return kOk;
-  if (mem0 == nullptr || beta == nullptr || th == nullptr || final_mem == nullptr) return kInvalidArgument;
-  if (T > 0 && (x == nullptr || spikes == nullptr)) return kInvalidArgument;
+  if (mem0 == nullptr || beta == nullptr || th == nullptr) return kInvalidArgument;
+  if (kOut != kOutNone && final_mem == nullptr) return kInvalidArgument;
+  if (T > 0 && (x == nullptr || (kOut != kOutNone && spikes == nullptr) || (kCkpt && ckpt == nullptr)))
+    return kInvalidArgument;
+  if (T == 0 && kOut == kOutNone) return kOk;
   const bool slab = T > 0 && (NB % 4 == 0) && aligned16(mem0) && aligned16(final_mem) && aligned16(x) &&
-                    aligned16(spikes);
+                    aligned16(spikes) && aligned16(ckpt);
   if (slab) {
     // Slab of S neurons per CTA: about one CTA per SM, S a multiple of 128 (whole consumer warps).
     const int sms = sm_count();
@@ -230,27 +252,41 @@ inline int run_impl(const float* x, const float* mem0, const float* beta, const 
     if (depth > kMaxDepth) depth = kMaxDepth;
     if (depth < 2) depth = 2;
     const size_t smem = size_t(depth) * size_t(S) * 4;
-    auto kern = lif_slab_kernel<kPacked>;
+    auto kern = lif_slab_kernel<kOut, kCkpt>;
     if (!ensure_dyn_smem(kern, int(smem))) return kCudaError;
     return launch_pdl(kern, unsigned(grid), unsigned(S / 4 + 32), smem, stream, x, mem0, beta, th, T, NB, H, int(S),
-                      depth, spikes, final_mem);
+                      depth, spikes, final_mem, ckpt);
   }
   const int64_t grid = (NB + kThreads - 1) / kThreads;
-  return launch_pdl(lif_scalar_kernel<kPacked>, unsigned(grid), kThreads, 0, stream, x, mem0, beta, th, T, NB, H,
-                    spikes, final_mem);
+  return launch_pdl(lif_scalar_kernel<kOut, kCkpt>, unsigned(grid), kThreads, 0, stream, x, mem0, beta, th, T, NB,
+                    H, spikes, final_mem, ckpt);
 }
 
 // spikes: fp32 [T, B*H], 0 or 1 (the reference layout).
 inline int run(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B, int32_t H,
                float* spikes, float* final_mem, cudaStream_t stream) {
-  return run_impl<false>(x, mem0, beta, th, T, B, H, spikes, final_mem, stream);
+  return run_impl<kOutFloat, false>(x, mem0, beta, th, T, B, H, spikes, final_mem, nullptr, stream);
 }
 
 // spike_bits: uint32 [ceil(T / 32), B*H]; bit t % 32 of word [t / 32][n] is the spike of neuron n
 // at step t (bits past T are zero).  1/32 of the fp32 layout's spike bytes.
 inline int run_packed(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B,
                       int32_t H, uint32_t* spike_bits, float* final_mem, cudaStream_t stream) {
-  return run_impl<true>(x, mem0, beta, th, T, B, H, spike_bits, final_mem, stream);
+  return run_impl<kOutBits, false>(x, mem0, beta, th, T, B, H, spike_bits, final_mem, nullptr, stream);
+}
+
+inline int64_t checkpoint_count(int32_t T) { return T <= 0 ? 0 : (int64_t(T) + kSeg - 1) / kSeg; }
+
+// The forward for training: run() plus the membrane checkpoints ckpt [ceil(T / kSeg), B*H].
+inline int run_train(const float* x, const float* mem0, const float* beta, const float* th, int32_t T, int32_t B,
+                     int32_t H, float* spikes, float* final_mem, float* ckpt, cudaStream_t stream) {
+  return run_impl<kOutFloat, true>(x, mem0, beta, th, T, B, H, spikes, final_mem, ckpt, stream);
+}
+
+// The checkpoints alone (after a forward that did not store them): reads x, writes ckpt.
+inline int run_checkpoints(const float* x, const float* mem0, const float* beta, const float* th, int32_t T,
+                           int32_t B, int32_t H, float* ckpt, cudaStream_t stream) {
+  return run_impl<kOutNone, true>(x, mem0, beta, th, T, B, H, nullptr, nullptr, ckpt, stream);
 }
 
 }  // namespace lif

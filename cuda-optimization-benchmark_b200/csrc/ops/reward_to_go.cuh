@@ -26,6 +26,12 @@
 //      error carried between runs) and writes the outputs over the rewards in shared memory,
 //      and the warp streams them out with 128-bit stores.
 // One warp per row and 40 warps per SM put every row of the BASELINE batch in flight at once.
+//
+// Done flags come as one byte per step (the reference layout) or, with kBits, as bits: uint32 words
+// [B, ceil(T / 32)], bit t % 32 of word [b, t / 32] set when done[b, t] (pack_kernel makes them).
+// Bits cut the flags' traffic from 1 byte to 1/8 byte per step and need no staging: kSeg is a
+// multiple of 32, so a lane's kLane-step run spans at most two words of its row, which the lane
+// loads when the pass is issued and funnels into its run mask.
 #pragma once
 
 #include "../common/b200_common.cuh"
@@ -93,7 +99,8 @@ __device__ __forceinline__ unsigned long long done_mask(const unsigned char* sd,
 }
 
 // Ragged-edge values a lane loaded for a prefetched pass; written to shared memory when the
-// pass's bulk copy has landed, so issuing a pass never waits on its own plain loads.
+// pass's bulk copy has landed, so issuing a pass never waits on its own plain loads.  With done
+// bits, dh and dt are instead the two words that cover the lane's run.
 struct Edges {
   float rh, rt;
   uint32_t dh, dt;
@@ -103,18 +110,26 @@ struct Edges {
 // sr + i of the reward buffer and byte sd + i of the done buffer; the lane grid starts gr floats
 // and gd bytes into them (sr = gr + kSeg - len).  gr and gd are chosen so that the aligned
 // interiors [ear, ebr) and [ead, ebd) land on 16-byte boundaries, as cp.async.bulk requires.
+// With done bits: dw is the row's first word, nw its word count, and slot 0 of the lane grid is
+// step tg = t0 - (kSeg - len) of the row (negative in the row's first pass: those slots reach no
+// output).
 struct Pass {
   const float* rs;
   const unsigned char* ds;
-  int len, pr, gr, gd, sr, sd, ear, ebr, ead, ebd;
+  const uint32_t* dw;
+  int len, pr, gr, gd, sr, sd, ear, ebr, ead, ebd, tg, nw;
 };
 
-__device__ __forceinline__ Pass make_pass(const float* rrow, const unsigned char* drow, int t0, int len) {
+template <bool kBits>
+__device__ __forceinline__ Pass make_pass(const float* rrow, const void* drow, int t0, int len, int nw) {
   Pass p;
   p.rs = rrow + t0;
-  p.ds = drow + t0;
+  p.ds = kBits ? nullptr : static_cast<const unsigned char*>(drow) + t0;
+  p.dw = kBits ? static_cast<const uint32_t*>(drow) : nullptr;
   p.len = len;
   const int pad = kSeg - len;
+  p.tg = t0 - pad;
+  p.nw = nw;
   p.pr = int((reinterpret_cast<uintptr_t>(p.rs) >> 2) & 3);
   const int pd = int(reinterpret_cast<uintptr_t>(p.ds) & 15);
   p.gr = (p.pr - pad) & 3;
@@ -125,6 +140,10 @@ __device__ __forceinline__ Pass make_pass(const float* rrow, const unsigned char
   p.ebr = len > p.ear ? p.ear + ((len - p.ear) & ~3) : p.ear;
   p.ead = (16 - pd) & 15;
   p.ebd = len > p.ead ? p.ead + ((len - p.ead) & ~15) : p.ead;
+  if (kBits) {  // no done bytes to stage
+    p.ead = 0;
+    p.ebd = 0;
+  }
   return p;
 }
 
@@ -134,8 +153,16 @@ __device__ __forceinline__ unsigned char ld_u8(const unsigned char* p) {
   return (unsigned char)v;
 }
 
+__device__ __forceinline__ uint32_t ld_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // Start moving a pass into a staging buffer: lane 0 arms the buffer's barrier and issues one bulk
-// copy per stream for the aligned interiors; every lane issues its ragged-edge loads.
+// copy per stream for the aligned interiors; every lane issues its ragged-edge loads (and, with
+// done bits, the two words covering its run: words before the row's start read as 0).
+template <bool kBits>
 __device__ __forceinline__ Edges issue_pass(const Pass& p, float* s_r, unsigned char* s_d, uint64_t* bar, int lane) {
   fence_proxy_async_smem();  // earlier ordinary accesses of this buffer come before the copy
   __syncwarp();
@@ -151,20 +178,29 @@ __device__ __forceinline__ Edges issue_pass(const Pass& p, float* s_r, unsigned 
   const int hd = min(p.len, p.ead), td = p.len - p.ebd;
   if (lane < hr) e.rh = ld_stream_f1(p.rs + lane);
   if (lane < tr) e.rt = ld_stream_f1(p.rs + p.ebr + lane);
-  if (lane < hd) e.dh = ld_u8(p.ds + lane);
-  if (lane < td) e.dt = ld_u8(p.ds + p.ebd + lane);
+  if (kBits) {
+    const int w = (p.tg + lane * kLane) >> 5;  // arithmetic shift: floor for negative steps
+    if (w >= 0 && w < p.nw) e.dh = ld_u32(p.dw + w);
+    if (w + 1 >= 0 && w + 1 < p.nw) e.dt = ld_u32(p.dw + w + 1);
+  } else {
+    if (lane < hd) e.dh = ld_u8(p.ds + lane);
+    if (lane < td) e.dt = ld_u8(p.ds + p.ebd + lane);
+  }
   return e;
 }
 
 // Finish staging a pass: write the ragged edges, wait for the bulk copies (phase `parity`).
+template <bool kBits>
 __device__ __forceinline__ void land_pass(const Pass& p, const Edges& e, float* s_r, unsigned char* s_d,
                                           uint64_t* bar, uint32_t parity, int lane) {
   const int hr = min(p.len, p.ear), tr = p.len - p.ebr;
-  const int hd = min(p.len, p.ead), td = p.len - p.ebd;
   if (lane < hr) s_r[p.sr + lane] = e.rh;
   if (lane < tr) s_r[p.sr + p.ebr + lane] = e.rt;
-  if (lane < hd) s_d[p.sd + lane] = (unsigned char)e.dh;
-  if (lane < td) s_d[p.sd + p.ebd + lane] = (unsigned char)e.dt;
+  if (!kBits) {
+    const int hd = min(p.len, p.ead), td = p.len - p.ebd;
+    if (lane < hd) s_d[p.sd + lane] = (unsigned char)e.dh;
+    if (lane < td) s_d[p.sd + p.ebd + lane] = (unsigned char)e.dt;
+  }
   mbar_wait_sleep(bar, parity);
   __syncwarp();
 }
@@ -183,11 +219,19 @@ __device__ __forceinline__ double gamma_run(double gamma) {
 // Scan one staged pass given the value entering it from the right (`carry`); writes the outputs
 // into the staging buffer and returns the value at the pass's first step (meaningful only for a
 // full pass, len == kSeg: a shorter pass is the first of its row, whose value is not needed).
-// gamma is the fp32 discount widened to fp64; g_run = gamma_run(gamma).
-__device__ __forceinline__ double scan_pass(const Pass& p, float* s_r, const unsigned char* s_d, double carry,
-                                            double gamma, double g_run, float gamma_f, int lane) {
+// gamma is the fp32 discount widened to fp64; g_run = gamma_run(gamma).  e: the lane's edges (its
+// run's done words with kBits).
+template <bool kBits>
+__device__ __forceinline__ double scan_pass(const Pass& p, const Edges& ed, float* s_r, const unsigned char* s_d,
+                                            double carry, double gamma, double g_run, float gamma_f, int lane) {
   const int lo = lane * kLane;
-  const unsigned long long dmask = done_mask(s_d, p.gd + lo);  // bit e: done at slot lo + e
+  unsigned long long dmask;  // bit e: done at slot lo + e
+  if (kBits) {
+    const unsigned long long w2 = (unsigned long long)ed.dt << 32 | ed.dh;
+    dmask = (w2 >> ((p.tg + lo) & 31)) & ((1ull << kLane) - 1ull);
+  } else {
+    dmask = done_mask(s_d, p.gd + lo);
+  }
   float* rl = s_r + p.gr + lo;
   // Composition of the run in fp64: y -> Bv + A*y (the factor of slot e is 0 at a done flag, else
   // gamma; Bv stays finite, so 0 * Bv is an exact zero).
@@ -229,7 +273,8 @@ __device__ __forceinline__ double scan_pass(const Pass& p, float* s_r, const uns
 // mbarriers (initialised here).  With nbuf = 2 the next pass is in flight in the second buffer
 // while the current one is scanned and written out; with nbuf = 1 passes are staged one after the
 // other (a smaller footprint, so more warps share an SM).
-__device__ __forceinline__ void warp_rows(const float* __restrict__ reward, const unsigned char* __restrict__ done,
+template <bool kBits>
+__device__ __forceinline__ void warp_rows(const float* __restrict__ reward, const void* __restrict__ done,
                                           float gamma, int64_t B, int T, float* __restrict__ out, int64_t first_row,
                                           int64_t row_stride, unsigned char* wbase, uint64_t* bars, int nbuf,
                                           int lane) {
@@ -245,10 +290,16 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
   int64_t row = first_row;
   if (row >= B) return;
   int t1 = T;
+  const int nw = (T + 31) >> 5;
+  // Row r's done flags: bytes from r * T, or words from r * nw.
+  auto drow = [&](int64_t r) -> const void* {
+    return kBits ? static_cast<const void*>(static_cast<const uint32_t*>(done) + r * int64_t(nw))
+                 : static_cast<const void*>(static_cast<const unsigned char*>(done) + r * int64_t(T));
+  };
   // Current pass and its staging state.
-  Pass cur = make_pass(reward + row * int64_t(T), done + row * int64_t(T), t1 > kSeg ? t1 - kSeg : 0,
-                       t1 > kSeg ? kSeg : t1);
-  Edges ecur = issue_pass(cur, s_rb(0), s_db(0), &bars[0], lane);
+  Pass cur = make_pass<kBits>(reward + row * int64_t(T), drow(row), t1 > kSeg ? t1 - kSeg : 0,
+                              t1 > kSeg ? kSeg : t1, nw);
+  Edges ecur = issue_pass<kBits>(cur, s_rb(0), s_db(0), &bars[0], lane);
   uint32_t k = 0;
   double carry = 0.0;
   for (;;) {
@@ -265,13 +316,13 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
     const uint32_t nb = (k + 1) & 1u;
     if (has_next && nbuf == 2) {
       const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
-      nxt = make_pass(reward + nrow * int64_t(T), done + nrow * int64_t(T), nt0, nt1 - nt0);
-      enxt = issue_pass(nxt, s_rb(nb), s_db(nb), &bars[nb], lane);
+      nxt = make_pass<kBits>(reward + nrow * int64_t(T), drow(nrow), nt0, nt1 - nt0, nw);
+      enxt = issue_pass<kBits>(nxt, s_rb(nb), s_db(nb), &bars[nb], lane);
     }
     const uint32_t cb = nbuf == 2 ? (k & 1u) : 0u;
     const uint32_t par = nbuf == 2 ? ((k >> 1) & 1u) : (k & 1u);
-    land_pass(cur, ecur, s_rb(cb), s_db(cb), &bars[cb], par, lane);
-    const double first = scan_pass(cur, s_rb(cb), s_db(cb), carry, g, g_run, gamma, lane);
+    land_pass<kBits>(cur, ecur, s_rb(cb), s_db(cb), &bars[cb], par, lane);
+    const double first = scan_pass<kBits>(cur, ecur, s_rb(cb), s_db(cb), carry, g, g_run, gamma, lane);
     const int t0 = t1 > kSeg ? t1 - kSeg : 0;
     if (k == 0) pdl_wait();  // first global write of this warp (no-op without PDL)
     drain_floats(out + row * int64_t(T) + t0, cur.len, s_rb(cb) + (cur.sr - cur.pr), cur.pr, lane);
@@ -279,8 +330,8 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
     if (!has_next) break;
     if (nbuf == 1) {
       const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
-      nxt = make_pass(reward + nrow * int64_t(T), done + nrow * int64_t(T), nt0, nt1 - nt0);
-      enxt = issue_pass(nxt, s_rb(0), s_db(0), &bars[0], lane);
+      nxt = make_pass<kBits>(reward + nrow * int64_t(T), drow(nrow), nt0, nt1 - nt0, nw);
+      enxt = issue_pass<kBits>(nxt, s_rb(0), s_db(0), &bars[0], lane);
     }
     carry = (nrow == row) ? first : 0.0;
     row = nrow;
@@ -291,57 +342,77 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
   }
 }
 
-// One warp computes one whole row through one staging buffer (kWarpSmem bytes at wbase) and one
-// initialised mbarrier whose completed-phase count the caller keeps in `phase`.  Passes run from
-// the end of the row to its start, exactly as warp_rows with nbuf = 1 (same bits).
-__device__ __forceinline__ void one_row(const float* __restrict__ reward, const unsigned char* __restrict__ done,
-                                        float gamma, int T, float* __restrict__ out, int64_t row,
-                                        unsigned char* wbase, uint64_t* bar, uint32_t& phase, int lane) {
-  float* s_r = reinterpret_cast<float*>(wbase);
-  unsigned char* s_d = wbase + kRewardBytes;
-  const float* rrow = reward + row * int64_t(T);
-  const unsigned char* drow = done + row * int64_t(T);
-  float* orow = out + row * int64_t(T);
-  const double g = double(gamma), g_run = gamma_run(g);
-  double carry = 0.0;
-  for (int t1 = T; t1 > 0; t1 -= kSeg) {
-    const int t0 = t1 > kSeg ? t1 - kSeg : 0;
-    const Pass p = make_pass(rrow, drow, t0, t1 - t0);
-    const Edges e = issue_pass(p, s_r, s_d, bar, lane);
-    land_pass(p, e, s_r, s_d, bar, phase & 1u, lane);
-    ++phase;
-    carry = scan_pass(p, s_r, s_d, carry, g, g_run, gamma, lane);
-    drain_floats(orow + t0, p.len, s_r + (p.sr - p.pr), p.pr, lane);
-    __syncwarp();
-  }
-}
-
 // Warp w of CTA c handles rows c*kWarps + w, + gridDim.x*kWarps, ...
+template <bool kBits>
 __global__ void __launch_bounds__(kThreads, 8) rtg_kernel(const float* __restrict__ reward,
-                                                       const unsigned char* __restrict__ done, float gamma,
+                                                       const void* __restrict__ done, float gamma,
                                                        int B, int T, int nbuf, float* __restrict__ out) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint64_t bars[kWarps][2];  // one barrier per staging buffer
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  warp_rows(reward, done, gamma, B, T, out, int64_t(blockIdx.x) * kWarps + warp, int64_t(gridDim.x) * kWarps,
-            smem + warp * nbuf * kWarpSmem, bars[warp], nbuf, lane);
+  warp_rows<kBits>(reward, done, gamma, B, T, out, int64_t(blockIdx.x) * kWarps + warp,
+                   int64_t(gridDim.x) * kWarps, smem + warp * nbuf * kWarpSmem, bars[warp], nbuf, lane);
 }
 
-inline int run(const float* reward, const unsigned char* done, float gamma, int32_t B, int32_t T, float* out,
-               cudaStream_t stream) {
+// Done bytes -> bits: word [b, w] of `bits` holds done[b, 32w .. 32w + 31] (bits past T zero).
+// One warp builds one word per step with a ballot over 32 consecutive flags of a row.
+constexpr int kPackThreads = 256;
+__global__ void __launch_bounds__(kPackThreads) pack_kernel(const unsigned char* __restrict__ done, int64_t B, int T,
+                                                            uint32_t* __restrict__ bits) {
+  pdl_begin();
+  const int nw = (T + 31) >> 5;
+  const int64_t words = B * int64_t(nw);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = int64_t(gridDim.x) * (kPackThreads / 32);
+  for (int64_t q = int64_t(blockIdx.x) * (kPackThreads / 32) + (threadIdx.x >> 5); q < words; q += warps) {
+    const int64_t b = q / nw;
+    const int t = int(q - b * nw) * 32 + lane;
+    const bool d = t < T && done[b * int64_t(T) + t] != 0;
+    const uint32_t w = __ballot_sync(0xffffffffu, d);
+    if (lane == 0) bits[q] = w;
+  }
+}
+
+inline int pack_done(const unsigned char* done, int32_t B, int32_t T, uint32_t* bits, cudaStream_t stream) {
+  if (B < 0 || T < 0) return kInvalidArgument;
+  if (B == 0 || T == 0) return kOk;
+  if (done == nullptr || bits == nullptr) return kInvalidArgument;
+  const int64_t words = int64_t(B) * ((int64_t(T) + 31) / 32);
+  const int64_t want = (words + kPackThreads / 32 - 1) / (kPackThreads / 32);
+  const int64_t cap = int64_t(sm_count()) * 8;
+  return launch_pdl(pack_kernel, unsigned(want < cap ? want : cap), kPackThreads, 0, stream, done, int64_t(B), T,
+                    bits);
+}
+
+template <bool kBits>
+inline int run_impl(const float* reward, const void* done, float gamma, int32_t B, int32_t T, float* out,
+                    cudaStream_t stream) {
   if (B < 0 || T < 0) return kInvalidArgument;
   if (B == 0 || T == 0) return kOk;
   if (reward == nullptr || done == nullptr || out == nullptr) return kInvalidArgument;
   // One row per warp in a single wave when the batch fits (10 CTAs = 40 warps per SM, one staging
   // buffer each); otherwise about 8 warps per SM streaming several rows through two buffers.
   const int64_t ctas_needed = (int64_t(B) + kWarps - 1) / kWarps;
-  const int64_t one_wave = int64_t(sm_count()) * resident_ctas_per_sm(rtg_kernel, kThreads, kSmemPerBuffer);
+  const int64_t one_wave = int64_t(sm_count()) * resident_ctas_per_sm(rtg_kernel<kBits>, kThreads, kSmemPerBuffer);
   const bool single = ctas_needed <= one_wave && T <= kSeg;
   const int nbuf = single ? 1 : 2;
   const int64_t cap = single ? one_wave : int64_t(sm_count()) * 2;
   const int grid = int(ctas_needed < cap ? ctas_needed : cap);
-  return launch_pdl(rtg_kernel, grid, kThreads, nbuf * kSmemPerBuffer, stream, reward, done, gamma, B, T, nbuf, out);
+  return launch_pdl(rtg_kernel<kBits>, grid, kThreads, nbuf * kSmemPerBuffer, stream, reward, done, gamma, B, T, nbuf,
+                    out);
+}
+
+// done: one byte per step, [B, T].
+inline int run(const float* reward, const unsigned char* done, float gamma, int32_t B, int32_t T, float* out,
+               cudaStream_t stream) {
+  return run_impl<false>(reward, done, gamma, B, T, out, stream);
+}
+
+// done_bits: uint32 [B, ceil(T / 32)] from pack_done.
+inline int run_bits(const float* reward, const uint32_t* done_bits, float gamma, int32_t B, int32_t T, float* out,
+                    cudaStream_t stream) {
+  return run_impl<true>(reward, done_bits, gamma, B, T, out, stream);
 }
 
 }  // namespace rtg

@@ -37,7 +37,7 @@ static_assert(ppo::kThreads == 256, "the reward-to-go role uses the CTA's 8 warp
 
 struct Args {
   const float* reward;
-  const unsigned char* done;
+  const void* done;  // bytes [B, T], or with kBits uint32 words [B, ceil(T / 32)] (rtg::pack_done)
   float gamma;
   int64_t B;
   int T;
@@ -68,7 +68,7 @@ __device__ __forceinline__ void step_prologue(const Args& a) {
   pdl_trigger();
 }
 
-template <bool kVec, bool kEnt, bool kFinish>
+template <bool kVec, bool kEnt, bool kFinish, bool kBits>
 __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_kernel(const Args a) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint64_t bars[kRows][2];
@@ -78,8 +78,8 @@ __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_kernel(const 
   const bool is_rtg = ((b + 1) * a.rtg_ctas) / G > rtg_before;
   if (is_rtg) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    rtg::warp_rows(a.reward, a.done, a.gamma, a.B, a.T, a.rtg_out, rtg_before * kRows + warp, a.rtg_ctas * kRows,
-                   smem + warp * rtg::kWarpSmem, bars[warp], 1, lane);
+    rtg::warp_rows<kBits>(a.reward, a.done, a.gamma, a.B, a.T, a.rtg_out, rtg_before * kRows + warp,
+                          a.rtg_ctas * kRows, smem + warp * rtg::kWarpSmem, bars[warp], 1, lane);
     return;
   }
   const int64_t pidx = b - rtg_before;  // index among the PPO CTAs
@@ -125,7 +125,7 @@ __device__ __forceinline__ ppo::Sums unpack_sums(const uint32_t (&w)[kRankWords]
 // ranks' totals from its own buffer (one thread per rank, each waiting until its record's epoch
 // has arrived) and adds all ranks' totals in rank order.  Every rank writes the same outputs; with
 // one rank they are bit-identical to the one-GPU step.
-template <bool kVec, bool kEnt>
+template <bool kVec, bool kEnt, bool kBits>
 __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_exchange_kernel(const Args a, const PeerView pv) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint64_t bars[kRows][2];
@@ -136,8 +136,8 @@ __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_exchange_kern
   const bool is_rtg = ((b + 1) * a.rtg_ctas) / G > rtg_before;
   if (is_rtg) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    rtg::warp_rows(a.reward, a.done, a.gamma, a.B, a.T, a.rtg_out, rtg_before * kRows + warp, a.rtg_ctas * kRows,
-                   smem + warp * rtg::kWarpSmem, bars[warp], 1, lane);
+    rtg::warp_rows<kBits>(a.reward, a.done, a.gamma, a.B, a.T, a.rtg_out, rtg_before * kRows + warp,
+                          a.rtg_ctas * kRows, smem + warp * rtg::kWarpSmem, bars[warp], 1, lane);
     return;
   }
   const int64_t pidx = b - rtg_before;
@@ -178,9 +178,9 @@ __global__ void __launch_bounds__(kThreads, B200_RL_MIN_CTAS) step_exchange_kern
   }
 }
 
-template <bool kVec, bool kEnt, bool kFinish>
+template <bool kVec, bool kEnt, bool kFinish, bool kBits>
 inline int launch(const Args& a, cudaStream_t stream) {
-  auto kern = step_kernel<kVec, kEnt, kFinish>;
+  auto kern = step_kernel<kVec, kEnt, kFinish, kBits>;
   if (!ensure_dyn_smem(kern, kSmem)) return kCudaError;
   return launch_pdl(kern, unsigned(a.rtg_ctas + a.ppo_ctas), kThreads, kSmem, stream, a);
 }
@@ -221,11 +221,16 @@ inline void split_roles(int64_t rows, int64_t row_bytes, int64_t chunks, int64_t
 // first call; left zero).  With finish == false the PPO chunk partials are written to
 // `partials_out` (one ppo::Partial per chunk) and ppo_out is untouched (the multi-GPU shard form).
 // early_reads: the caller declares that the kernel launched just before on the stream writes none
-// of the inputs, so they may be read before it completes.
-inline int run(const float* reward, const unsigned char* done, float gamma, int32_t B, int32_t T, float* rtg_out,
+// of the inputs, so they may be read before it completes.  done_bits: `done` holds the flags as
+// bits (rtg::pack_done), 1/8 byte per step instead of 1.
+inline int64_t row_bytes(int32_t T, bool done_bits) {
+  return done_bits ? 8 * int64_t(T) + 4 * ((int64_t(T) + 31) / 32) : 9 * int64_t(T);
+}
+
+inline int run(const float* reward, const void* done, float gamma, int32_t B, int32_t T, float* rtg_out,
                const float* cur, const float* old, const float* adv, const float* ent, int64_t n, float eps,
                float* ppo_out, void* workspace, size_t ws_bytes, bool finish, void* partials_out,
-               bool early_reads, cudaStream_t stream) {
+               bool early_reads, bool done_bits, cudaStream_t stream) {
   if (B < 0 || T < 0 || n < 0) return kInvalidArgument;
   if (int64_t(B) * T > 0 && (reward == nullptr || done == nullptr || rtg_out == nullptr)) return kInvalidArgument;
   if (n > 0 && (cur == nullptr || old == nullptr || adv == nullptr)) return kInvalidArgument;
@@ -256,26 +261,38 @@ inline int run(const float* reward, const unsigned char* done, float gamma, int3
   a.ppo_out = ppo_out;
   a.inv_n = ppo::inv_count(n);
   const int64_t slots = int64_t(sm_count()) * B200_RL_MIN_CTAS;
-  split_roles(a.B, 9 * int64_t(T), ppo::num_chunks(n), (ent != nullptr ? 16 : 12) * ppo::kChunk, slots, finish,
-              &a.rtg_ctas, &a.ppo_ctas);
+  split_roles(a.B, row_bytes(T, done_bits), ppo::num_chunks(n), (ent != nullptr ? 16 : 12) * ppo::kChunk, slots,
+              finish, &a.rtg_ctas, &a.ppo_ctas);
   if (a.rtg_ctas + a.ppo_ctas == 0) return kOk;
   const bool vec = aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
-  if (finish) {
-    if (ent != nullptr) return vec ? launch<true, true, true>(a, stream) : launch<false, true, true>(a, stream);
-    return vec ? launch<true, false, true>(a, stream) : launch<false, false, true>(a, stream);
+  if (done_bits) {
+    if (!finish) return ent != nullptr ? (vec ? launch<true, true, false, true>(a, stream)
+                                              : launch<false, true, false, true>(a, stream))
+                                       : (vec ? launch<true, false, false, true>(a, stream)
+                                              : launch<false, false, false, true>(a, stream));
+    return ent != nullptr ? (vec ? launch<true, true, true, true>(a, stream) : launch<false, true, true, true>(a, stream))
+                          : (vec ? launch<true, false, true, true>(a, stream)
+                                 : launch<false, false, true, true>(a, stream));
   }
-  if (ent != nullptr) return vec ? launch<true, true, false>(a, stream) : launch<false, true, false>(a, stream);
-  return vec ? launch<true, false, false>(a, stream) : launch<false, false, false>(a, stream);
+  if (finish) {
+    if (ent != nullptr)
+      return vec ? launch<true, true, true, false>(a, stream) : launch<false, true, true, false>(a, stream);
+    return vec ? launch<true, false, true, false>(a, stream) : launch<false, false, true, false>(a, stream);
+  }
+  if (ent != nullptr)
+    return vec ? launch<true, true, false, false>(a, stream) : launch<false, true, false, false>(a, stream);
+  return vec ? launch<true, false, false, false>(a, stream) : launch<false, false, false, false>(a, stream);
 }
 
 // The fused multi-GPU step: every rank calls this with its own batch (the same B, T and n on
 // every rank) and the same `epoch` (1 on the first step, peer_next_epoch() of the previous one
 // after); ppo_out receives the PPO outputs of all ranks' samples on every rank.  The exchange must
 // have been created with one slot of kExchangeRecordBytes bytes, and opened.  workspace as for run().
-inline int run_exchange(const float* reward, const unsigned char* done, float gamma, int32_t B, int32_t T,
+inline int run_exchange(const float* reward, const void* done, float gamma, int32_t B, int32_t T,
                         float* rtg_out, const float* cur, const float* old, const float* adv, const float* ent,
                         int64_t n, float eps, float* ppo_out, void* workspace, size_t ws_bytes,
-                        const PeerExchange* x, unsigned epoch, bool early_reads, cudaStream_t stream) {
+                        const PeerExchange* x, unsigned epoch, bool early_reads, bool done_bits,
+                        cudaStream_t stream) {
   if (B < 0 || T < 0 || n < 0 || x == nullptr || ppo_out == nullptr || epoch == 0) return kInvalidArgument;
   if (int64_t(B) * T > 0 && (reward == nullptr || done == nullptr || rtg_out == nullptr)) return kInvalidArgument;
   if (n > 0 && (cur == nullptr || old == nullptr || adv == nullptr)) return kInvalidArgument;
@@ -302,16 +319,22 @@ inline int run_exchange(const float* reward, const unsigned char* done, float ga
   a.ppo_out = ppo_out;
   a.inv_n = ppo::inv_count(int64_t(x->world) * n);
   const int64_t slots = int64_t(sm_count()) * B200_RL_MIN_CTAS;
-  split_roles(a.B, 9 * int64_t(T), ppo::num_chunks(n), (ent != nullptr ? 16 : 12) * ppo::kChunk, slots, true,
-              &a.rtg_ctas, &a.ppo_ctas);
+  split_roles(a.B, row_bytes(T, done_bits), ppo::num_chunks(n), (ent != nullptr ? 16 : 12) * ppo::kChunk, slots,
+              true, &a.rtg_ctas, &a.ppo_ctas);
   const PeerView pv = peer_view(*x, epoch);
   const bool vec = aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
   auto go = [&](auto kern) {
     if (!ensure_dyn_smem(kern, kSmem)) return int(kCudaError);
     return launch_pdl(kern, unsigned(a.rtg_ctas + a.ppo_ctas), kThreads, kSmem, stream, a, pv);
   };
-  if (ent != nullptr) return vec ? go(step_exchange_kernel<true, true>) : go(step_exchange_kernel<false, true>);
-  return vec ? go(step_exchange_kernel<true, false>) : go(step_exchange_kernel<false, false>);
+  if (done_bits) {
+    if (ent != nullptr)
+      return vec ? go(step_exchange_kernel<true, true, true>) : go(step_exchange_kernel<false, true, true>);
+    return vec ? go(step_exchange_kernel<true, false, true>) : go(step_exchange_kernel<false, false, true>);
+  }
+  if (ent != nullptr)
+    return vec ? go(step_exchange_kernel<true, true, false>) : go(step_exchange_kernel<false, true, false>);
+  return vec ? go(step_exchange_kernel<true, false, false>) : go(step_exchange_kernel<false, false, false>);
 }
 
 }  // namespace rl

@@ -156,8 +156,52 @@ def reward_to_go(reward, done, gamma, out=None):
     return out
 
 
+def pack_done(done, out=None):
+    """Done flags bool [B, T] -> bits int32 [B, ceil(T/32)]: bit t % 32 of word [b, t // 32] is
+    done[b, t], bits past T zero."""
+    _need(done, "done", torch.bool)
+    if done.dim() != 2:
+        raise ValueError("done must be (B, T)")
+    B, T = done.shape
+    out = torch.empty((B, (T + 31) // 32), dtype=torch.int32, device=done.device) if out is None else out
+    _native.check(_lib().b200_pack_done_async(_ptr(done), B, T, _ptr(out), _stream(done.device)), "pack_done")
+    return out
+
+
+def reward_to_go_bits(reward, done_bits, gamma, out=None):
+    """reward_to_go with the done flags as bits (pack_done): the same output bits."""
+    _need(reward, "reward", torch.float32)
+    if reward.dim() != 2:
+        raise ValueError("reward must be (B, T)")
+    B, T = reward.shape
+    _need(done_bits, "done_bits", torch.int32, reward.device)
+    if done_bits.shape != (B, (T + 31) // 32):
+        raise ValueError("done_bits must be (B, ceil(T/32))")
+    out = torch.empty_like(reward) if out is None else out
+    _native.check(_lib().b200_reward_to_go_bits_async(_ptr(reward), _ptr(done_bits), float(gamma), B, T, _ptr(out),
+                                                      _stream(reward.device)), "reward_to_go_bits")
+    return out
+
+
 # ---------------------------------------------------------------------------- fused RL loss step
 STEP_INPUTS_READY = 1  # B200_STEP_INPUTS_READY
+STEP_DONE_BITS = 2     # B200_STEP_DONE_BITS
+
+
+def _step_done_flags(reward, done, dev):
+    """The step's done argument: bool [B, T], or bits int32 [B, ceil(T/32)] (flag STEP_DONE_BITS)."""
+    if reward.dim() != 2:
+        raise ValueError("reward must be (B, T)")
+    B, T = reward.shape
+    if isinstance(done, torch.Tensor) and done.dtype == torch.int32:
+        _need(done, "done", torch.int32, dev)
+        if done.shape != (B, (T + 31) // 32):
+            raise ValueError("done bits must be (B, ceil(T/32))")
+        return STEP_DONE_BITS
+    _need(done, "done", torch.bool, dev)
+    if done.shape != reward.shape:
+        raise ValueError("reward and done must both be (B, T)")
+    return 0
 
 
 def rl_step(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_out=None, ppo_out=None,
@@ -166,12 +210,11 @@ def rl_step(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_
     separate calls.  Returns (returns [B, T], PPO outputs [6] or [7]).
 
     inputs_ready=True declares that the kernel launched just before on the stream writes none of
-    the inputs, so the step reads them while that kernel finishes (programmatic dependent launch)."""
+    the inputs, so the step reads them while that kernel finishes (programmatic dependent launch).
+    done: bool [B, T], or the flags as bits (pack_done)."""
     _need(reward, "reward", torch.float32)
     dev = reward.device
-    _need(done, "done", torch.bool, dev)
-    if reward.dim() != 2 or done.shape != reward.shape:
-        raise ValueError("reward and done must both be (B, T)")
+    flags = _step_done_flags(reward, done, dev)
     for t, nm in ((cur, "current_log_prob"), (old, "old_log_prob"), (adv, "advantage")):
         _need(t, nm, torch.float32, dev)
     if entropy is not None:
@@ -188,7 +231,8 @@ def rl_step(reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_
     _native.check(lib.b200_rl_step_ex_async(_ptr(reward), _ptr(done), float(gamma), B, T, _ptr(rtg_out), _ptr(cur),
                                             _ptr(old), _ptr(adv), _opt_ptr(entropy, ppo_out), n, float(clip_epsilon),
                                             _ptr(ppo_out), _ptr(ws), ws.numel(),
-                                            STEP_INPUTS_READY if inputs_ready else 0, _stream(dev)), "rl_step")
+                                            flags | (STEP_INPUTS_READY if inputs_ready else 0), _stream(dev)),
+                  "rl_step")
     return rtg_out, ppo_out
 
 
@@ -264,10 +308,10 @@ def rl_step_exchange(exchange, reward, done, gamma, cur, old, adv, clip_epsilon,
                      ppo_out=None, inputs_ready=False):
     """One rank's fused multi-GPU RL step: this rank's returns, and the PPO outputs over every
     rank's samples (the same bits on every rank).  Every rank must call it the same number of
-    times.  inputs_ready as for rl_step."""
+    times.  inputs_ready and done as for rl_step."""
     _need(reward, "reward", torch.float32)
     dev = reward.device
-    _need(done, "done", torch.bool, dev)
+    flags = _step_done_flags(reward, done, dev)
     for t, nm in ((cur, "current_log_prob"), (old, "old_log_prob"), (adv, "advantage")):
         _need(t, nm, torch.float32, dev)
     if entropy is not None:
@@ -286,7 +330,7 @@ def rl_step_exchange(exchange, reward, done, gamma, cur, old, adv, clip_epsilon,
                                                   _ptr(cur), _ptr(old), _ptr(adv), _opt_ptr(entropy, ppo_out), n,
                                                   float(clip_epsilon), _ptr(ppo_out), _ptr(ws), ws.numel(),
                                                   exchange.handle, exchange.epoch,
-                                                  STEP_INPUTS_READY if inputs_ready else 0, _stream(dev)),
+                                                  flags | (STEP_INPUTS_READY if inputs_ready else 0), _stream(dev)),
                   "rl_step_exchange")
     return rtg_out, ppo_out
 
@@ -339,6 +383,94 @@ def leaky(input_current, mem0, beta, threshold, spikes=None, final_mem=None):
     _native.check(_lib().b200_leaky_async(_ptr(input_current), _ptr(mem0), _ptr(beta), _ptr(threshold), T, B, H,
                                           _ptr(spikes), _ptr(final_mem), _stream(dev)), "leaky")
     return spikes, final_mem
+
+
+def _leaky_args(input_current, mem0, beta, threshold):
+    _need(input_current, "input_current", torch.float32)
+    dev = input_current.device
+    for t, nm in ((mem0, "mem0"), (beta, "beta"), (threshold, "threshold")):
+        _need(t, nm, torch.float32, dev)
+    T, B, H = input_current.shape
+    return dev, T, B, H
+
+
+def _checkpoint_buffer(T, B, H, dev):
+    return torch.empty(((T + 31) // 32, B, H), dtype=torch.float32, device=dev)
+
+
+def leaky_train(input_current, mem0, beta, threshold):
+    """The LIF forward for training: (spikes, final_mem, checkpoints), spikes and final_mem as leaky();
+    checkpoints [ceil(T/32), B, H] are the membrane state before every 32nd step, what
+    leaky_backward recomputes the trajectory from."""
+    dev, T, B, H = _leaky_args(input_current, mem0, beta, threshold)
+    spikes = torch.empty_like(input_current)
+    final_mem = torch.empty((B, H), dtype=torch.float32, device=dev)
+    ckpt = _checkpoint_buffer(T, B, H, dev)
+    _native.check(_lib().b200_leaky_train_async(_ptr(input_current), _ptr(mem0), _ptr(beta), _ptr(threshold), T, B,
+                                                H, _ptr(spikes), _ptr(final_mem), _ptr(ckpt), _stream(dev)),
+                  "leaky_train")
+    return spikes, final_mem, ckpt
+
+
+def leaky_checkpoints(input_current, mem0, beta, threshold):
+    """The membrane checkpoints alone, for a forward that ran through leaky()."""
+    dev, T, B, H = _leaky_args(input_current, mem0, beta, threshold)
+    ckpt = _checkpoint_buffer(T, B, H, dev)
+    _native.check(_lib().b200_leaky_checkpoints_async(_ptr(input_current), _ptr(mem0), _ptr(beta), _ptr(threshold),
+                                                      T, B, H, _ptr(ckpt), _stream(dev)), "leaky_checkpoints")
+    return ckpt
+
+
+def leaky_backward(input_current, checkpoints, beta, threshold, grad_spikes, grad_final_mem=None, alpha=2.0,
+                   need_params=True):
+    """Surrogate-gradient backward (arctangent surrogate, reset detached): returns (grad_input,
+    grad_mem0, grad_beta, grad_threshold); the last two are None unless need_params."""
+    _need(input_current, "input_current", torch.float32)
+    dev = input_current.device
+    T, B, H = input_current.shape
+    for t, nm in ((checkpoints, "checkpoints"), (beta, "beta"), (threshold, "threshold"),
+                  (grad_spikes, "grad_spikes")):
+        _need(t, nm, torch.float32, dev)
+    if grad_final_mem is not None:
+        _need(grad_final_mem, "grad_final_mem", torch.float32, dev)
+    if checkpoints.numel() != ((T + 31) // 32) * B * H or grad_spikes.shape != input_current.shape:
+        raise ValueError("leaky_backward: inconsistent shapes")
+    lib = _lib()
+    gx = torch.empty_like(input_current)
+    gm = torch.empty((B, H), dtype=torch.float32, device=dev)
+    gb = torch.empty(H, dtype=torch.float32, device=dev) if need_params else None
+    gt = torch.empty(H, dtype=torch.float32, device=dev) if need_params else None
+    ws = workspace("leaky_backward", lib.b200_leaky_backward_workspace_bytes(B, H), dev) if need_params else None
+    _native.check(lib.b200_leaky_backward_async(_ptr(input_current), _ptr(checkpoints), _ptr(beta), _ptr(threshold),
+                                                T, B, H, _ptr(grad_spikes),
+                                                None if grad_final_mem is None else _ptr(grad_final_mem),
+                                                float(alpha), _ptr(gx), _ptr(gm), _ptr(gb), _ptr(gt),
+                                                None if ws is None else _ptr(ws), 0 if ws is None else ws.numel(),
+                                                _stream(dev)), "leaky_backward")
+    return gx, gm, gb, gt
+
+
+class LeakyFunction(torch.autograd.Function):
+    """torch.autograd form of the layer: forward through leaky_train (keeps the 1/8-byte-per-step
+    checkpoints, not the trajectory), backward through leaky_backward."""
+
+    @staticmethod
+    def forward(ctx, input_current, mem0, beta, threshold, alpha=2.0):
+        spikes, final_mem, ckpt = leaky_train(input_current, mem0, beta, threshold)
+        ctx.save_for_backward(input_current, ckpt, beta, threshold)
+        ctx.alpha = float(alpha)
+        return spikes, final_mem
+
+    @staticmethod
+    def backward(ctx, grad_spikes, grad_final_mem):
+        x, ckpt, beta, threshold = ctx.saved_tensors
+        if grad_spikes is None:
+            grad_spikes = torch.zeros_like(x)
+        gs = grad_spikes.contiguous()
+        gf = None if grad_final_mem is None else grad_final_mem.contiguous()
+        need = ctx.needs_input_grad[2] or ctx.needs_input_grad[3]
+        gx, gm, gb, gt = leaky_backward(x, ckpt, beta, threshold, gs, gf, ctx.alpha, need_params=need)
+        return gx, gm, gb, gt, None
 
 
 # ----------------------------------------------------------------------------------------- KAN

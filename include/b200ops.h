@@ -127,6 +127,15 @@ void b200_reward_to_go(const float* reward, const bool* done, float gamma, int32
 int b200_reward_to_go_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
                             float* output, void* stream);
 
+/* Done flags as bits (no reference counterpart; the ABI fixes one bool per step): word [b, w] of
+ * done_bits (uint32 [B, ceil(T/32)]) holds done[b, 32w .. 32w + 31], bit t % 32 for step t, bits
+ * past T zero.  b200_pack_done_async packs the bool layout; b200_reward_to_go_bits_async is
+ * b200_reward_to_go_async reading the bits (the same output bits, 8 1/8 instead of 9 bytes moved
+ * per step). */
+int b200_pack_done_async(const uint8_t* done, int32_t B, int32_t T, uint32_t* done_bits, void* stream);
+int b200_reward_to_go_bits_async(const float* reward, const uint32_t* done_bits, float gamma, int32_t B, int32_t T,
+                                 float* output, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Fused RL loss step (no reference counterpart: the BASELINE RL pipeline, configs[1], runs
  * reward_to_go and ppo_clip back to back on independent inputs).  One launch computes both;
@@ -145,8 +154,11 @@ int b200_rl_step_async(const float* reward, const uint8_t* done, float gamma, in
  * (they were written by copies, or by kernels launched earlier): the inputs are then read while
  * that kernel finishes, and the step waits only before its own writes.  Steps over resident
  * batches issued back to back qualify; a step right after the kernel producing its log-probs does
- * not.  Other flag bits are rejected. */
+ * not.  With B200_STEP_DONE_BITS, `done` points to the flags as bits (uint32 words [B, ceil(T/32)],
+ * b200_pack_done_async) instead of bytes: same results, 1/8 of the flags' bytes.  Other flag bits
+ * are rejected. */
 #define B200_STEP_INPUTS_READY 1u
+#define B200_STEP_DONE_BITS 2u
 int b200_rl_step_ex_async(const float* reward, const uint8_t* done, float gamma, int32_t B, int32_t T,
                           float* rtg_out, const float* current_log_prob, const float* old_log_prob,
                           const float* advantage, const float* entropy, int64_t n, float clip_epsilon, float* ppo_out,
@@ -216,6 +228,38 @@ int b200_leaky_async(const float* input_current, const float* mem0, const float*
  * b200_leaky_async (so the same spikes and final_mem bits); 1/32 of its spike bytes. */
 int b200_leaky_packed_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
                             int32_t T, int32_t B, int32_t H, uint32_t* spike_bits, float* final_mem, void* stream);
+
+/* Training (no reference counterpart: the backward of snnTorch's Leaky, the layer the task
+ * restates, through its default arctangent spike surrogate with the reset detached).
+ *
+ * b200_leaky_train_async: b200_leaky_async (same spikes and final_mem bits) that also stores the
+ * membrane checkpoints [ceil(T / 32), B, H] fp32: checkpoint k is the state before step 32k
+ * (checkpoint 0 = mem0); b200_leaky_checkpoint_bytes gives their size (-1 for negative sizes).
+ * b200_leaky_checkpoints_async stores the checkpoints alone (after a forward that did not).
+ *
+ * b200_leaky_backward_async: from the checkpoints, the incoming grad_spikes [T, B, H] and
+ * grad_final_mem [B, H] (may be NULL: zero), with u[t] = mem[t] - threshold, r[t] = the reset at
+ * step t, s'(u) = (alpha / 2) / (1 + (pi / 2 * alpha * u)^2) and g[t] = grad_spikes[t] * s'(u[t])
+ * + beta * g[t + 1] (beta * g[T] := grad_final_mem):
+ *   grad_input[t] = g[t];  grad_mem0 = beta * g[0];
+ *   grad_beta[h] = [0 <= beta[h] <= 1] * sum_{b,t} g[t] * mem[t - 1];
+ *   grad_threshold[h] = -sum_{b,t} (grad_spikes[t] * s'(u[t]) + r[t] * g[t]).
+ * grad_mem0, grad_beta and grad_threshold may be NULL (not computed); grad_beta or grad_threshold
+ * need a workspace of b200_leaky_backward_workspace_bytes(B, H) bytes (status 4 if smaller).  The
+ * sums over b are taken in a fixed order: results do not depend on the launch shape. */
+int64_t b200_leaky_checkpoint_bytes(int32_t T, int32_t B, int32_t H);
+int b200_leaky_train_async(const float* input_current, const float* mem0, const float* beta, const float* threshold,
+                           int32_t T, int32_t B, int32_t H, float* spikes, float* final_mem, float* checkpoints,
+                           void* stream);
+int b200_leaky_checkpoints_async(const float* input_current, const float* mem0, const float* beta,
+                                 const float* threshold, int32_t T, int32_t B, int32_t H, float* checkpoints,
+                                 void* stream);
+int64_t b200_leaky_backward_workspace_bytes(int32_t B, int32_t H);
+int b200_leaky_backward_async(const float* input_current, const float* checkpoints, const float* beta,
+                              const float* threshold, int32_t T, int32_t B, int32_t H, const float* grad_spikes,
+                              const float* grad_final_mem, float alpha, float* grad_input, float* grad_mem0,
+                              float* grad_beta, float* grad_threshold, void* workspace, int64_t workspace_bytes,
+                              void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * KAN linear layer (task efficient_kan): out[B, O] = silu(x) . base_weight^T + bases(x) .

@@ -224,3 +224,77 @@ def gae(inp):
         a = delta[:, t] + g * lam * (~done[:, t]) * a
         adv[:, t] = a
     return {"advantage": adv, "value_target": adv + v}
+
+
+def atan_surrogate_grad(u, alpha):
+    """Derivative of the arctangent spike surrogate (Fang et al., "Incorporating Learnable
+    Membrane Time Constant to Enhance Learning of Spiking Neural Networks", 2021; snnTorch's
+    default surrogate for Leaky): d spike / d u = (alpha / 2) / (1 + (pi / 2 * alpha * u)^2)."""
+    return (alpha / 2.0) / (1.0 + (math.pi / 2.0 * alpha * u) ** 2)
+
+
+def leaky_backward(inp, grad_spikes, grad_final_mem=None, alpha=2.0):
+    """Surrogate-gradient backward of the leaky layer (no reference implementation in the reference
+    repository: snnTorch's Leaky, the layer tasks/leaky restates, trained through its arctangent
+    surrogate with the reset detached).  The forward is the reference's own fp32 loop
+    (tasks/leaky/reference.py:26-40, `leaky` above), so every reset and spike decision is the
+    reference's; the backward is then fp64 over those fp32 membrane values:
+
+        u[t] = mem[t] - th,   s'[t] = atan_surrogate_grad(u[t]),   r[t] = (mem[t-1] >= th)
+        g[t] = grad_spikes[t] * s'[t] + beta * g[t+1]         (beta * g[T] := grad_final_mem)
+        grad_x[t] = g[t];   grad_mem0 = beta * g[0]
+        grad_beta[h] = [0 <= beta_raw[h] <= 1] * sum_{b,t} g[t] * mem[t-1]
+        grad_threshold[h] = -sum_{b,t} (grad_spikes[t] * s'[t] + r[t] * g[t])
+
+    with mem[-1] = mem0 and beta the clamped value the forward uses."""
+    x = _np(inp["input_current"]).astype(np.float32)
+    T, B, H = x.shape
+    braw = _np(inp["beta"]).astype(np.float32)
+    beta32 = np.clip(braw, np.float32(0), np.float32(1)).reshape(1, H)
+    th32 = _np(inp["threshold"]).astype(np.float32).reshape(1, H)
+    mem = _np(inp["mem0"]).astype(np.float32).copy()
+    mems = np.empty((T + 1, B, H), dtype=np.float32)
+    mems[0] = mem
+    for t in range(T):
+        reset = (mem >= th32).astype(np.float32)
+        mem = (beta32 * mem + x[t]) - reset * th32
+        mems[t + 1] = mem
+    gs = _np(grad_spikes).astype(np.float64).reshape(T, B, H)
+    c = (np.zeros((B, H)) if grad_final_mem is None
+         else _np(grad_final_mem).astype(np.float64).reshape(B, H))
+    beta = beta32.astype(np.float64)
+    th = th32.astype(np.float64)
+    gx = np.empty((T, B, H))
+    gb = np.zeros((B, H))
+    gt = np.zeros((B, H))
+    gb_abs = np.zeros((B, H))
+    gt_abs = np.zeros((B, H))
+    for t in range(T - 1, -1, -1):
+        gsp = gs[t] * atan_surrogate_grad(mems[t + 1].astype(np.float64) - th, alpha)
+        g = gsp + c
+        gx[t] = g
+        prev = mems[t].astype(np.float64)
+        gb += g * prev
+        gb_abs += np.abs(g * prev)
+        term = gsp + (prev >= th) * g
+        gt -= term
+        gt_abs += np.abs(term)
+        c = beta * g
+    mask = ((braw >= 0) & (braw <= 1)).astype(np.float64)
+    # *_abs: the sums of the terms' magnitudes, the scale of a summation's rounding error.
+    return {"grad_input": gx, "grad_mem0": c, "grad_beta": mask * gb.sum(axis=0),
+            "grad_threshold": gt.sum(axis=0), "grad_beta_abs": gb_abs.sum(axis=0),
+            "grad_threshold_abs": gt_abs.sum(axis=0), "spikes": (mems[1:] >= th32).astype(np.float32),
+            "final_mem": mems[T], "checkpoints": mems[0:T:32]}
+
+
+def pack_done_bits(done):
+    """Done flags [B, T] -> uint32 words [B, ceil(T/32)]: bit t % 32 of word [b, t // 32] is
+    done[b, t], bits past T zero (the bit layout beside the reference's one-bool-per-step ABI)."""
+    d = _np(done).astype(bool)
+    B, T = d.shape
+    W = (T + 31) // 32
+    padded = np.zeros((B, W * 32), dtype=np.uint64)
+    padded[:, :T] = d
+    weights = np.left_shift(np.uint64(1), np.arange(32, dtype=np.uint64))
+    return (padded.reshape(B, W, 32) * weights).sum(axis=2).astype(np.uint32)

@@ -199,5 +199,6 @@ def test_step_flags_rejected(ops):
     x = torch.zeros(64, device="cuda")
     out = torch.zeros(8, device="cuda")
     p = x.data_ptr()
-    assert lib.b200_rl_step_ex_async(p, p, 0.9, 1, 4, p, p, p, p, None, 16, 0.2, out.data_ptr(), p, 4096, 2,
-                                     None) == 1
+    for flags in (4, 0x80000000):
+        assert lib.b200_rl_step_ex_async(p, p, 0.9, 1, 4, p, p, p, p, None, 16, 0.2, out.data_ptr(), p, 4096, flags,
+                                         None) == 1
