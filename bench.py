@@ -635,13 +635,13 @@ def other_ops(ops, dev, world, rank):
     res["leaky bit-packed spikes"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
                                       "frac_of_hbm": nbytes / ms / 1e6 / peak}
     del bits
-    # Training: the forward that also stores the membrane checkpoints (one per 32 steps), then the
+    # Training: the forward that also stores the membrane checkpoints (one per 16 steps), then the
     # surrogate-gradient backward: x and grad_spikes in, grad_input out (12 bytes per neuron-step)
     # plus the checkpoints, grad_final_mem in and grad_mem0 out.
     import ctypes
     lib, P = ops._lib(), ctypes.c_void_p
     T_, B_, H_ = xs.shape
-    ck = torch.empty(((T_ + 31) // 32, B_, H_), device=dev)
+    ck = torch.empty(((T_ + 15) // 16, B_, H_), device=dev)
     gs, gx = torch.randn_like(xs), torch.empty_like(xs)
     gf, gm = torch.randn_like(m0), torch.empty_like(m0)
     gb, gt = torch.empty_like(be), torch.empty_like(th)

@@ -22,7 +22,7 @@
 // 4, or unaligned pointers, take the one-neuron-per-thread form of the same loop.
 //
 // For training (lif_backward.cuh) the same loop also stores the membrane state every kSeg steps,
-// checkpoint k being the state before step k * kSeg (checkpoint 0 = mem0): 1/8 byte per
+// checkpoint k being the state before step k * kSeg (checkpoint 0 = mem0): 1/4 byte per
 // neuron-step, from which the backward recomputes each kSeg-step segment in registers.
 #pragma once
 
@@ -46,7 +46,7 @@ __device__ __forceinline__ float step(float& mem, float x, float beta, float th)
   return step_bit(mem, x, beta, th) ? 1.0f : 0.0f;
 }
 
-constexpr int kSeg = 32;                    // time steps per membrane checkpoint
+constexpr int kSeg = 16;                    // time steps per membrane checkpoint
 constexpr int kMaxDepth = 24;               // x slices in flight per CTA
 constexpr int kSmemBudget = 192 * 1024;      // bytes of the x ring
 constexpr int kMaxSlab = (1024 - 32) * 4;    // neurons per CTA: consumer threads + one producer warp

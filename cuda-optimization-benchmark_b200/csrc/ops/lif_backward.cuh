@@ -13,13 +13,17 @@
 //
 // B200 design.  The backward needs mem[t] for every step in reverse order; storing it would cost
 // the forward 4 more bytes per neuron-step and the backward 4 more to read it back.  Instead the
-// forward stores one checkpoint per kSeg steps (lif::run_train, 1/8 byte per neuron-step) and the
+// forward stores one checkpoint per kSeg steps (lif::run_train, 1/4 byte per neuron-step) and the
 // backward recomputes each kSeg-step segment from its checkpoint in registers, with the forward's
-// exact arithmetic (so every reset and spike decision is the forward's): per segment a thread
-// issues all kSeg loads of x and of grad_spikes at once, runs the segment forwards, then
-// backwards, streaming grad_x out.  12 bytes of HBM traffic per neuron-step (x, grad_spikes,
-// grad_x), the minimum for a backward that does not read a stored trajectory.  One neuron per
-// thread: a warp's loads and stores are 128 contiguous bytes per step.
+// exact arithmetic (so every reset and spike decision is the forward's), then runs it backwards.
+// 12 bytes of HBM traffic per neuron-step (x, grad_spikes, grad_x), the minimum for a backward
+// that does not read a stored trajectory.  One neuron per thread: per segment a thread issues all
+// kSeg loads of x and of grad_spikes at once (a warp's loads and stores are 128 contiguous bytes
+// per step), runs the segment forwards with the states in registers, then backwards, streaming
+// grad_x out.  kSeg = 16 keeps the kernel at 72 registers (28 warps per SM); with 32-step segments
+// it needed 128 (16 warps) and reached 0.68 of the HBM roofline instead of 0.82.  Staging [kSeg x
+// 128-neuron] tiles through shared memory (2-D TMA loads and stores, double-buffered) was slower
+// still: 96 KB per 128 neurons leaves 8 warps per SM, too few for the serial recurrences.
 //
 // grad_beta and grad_threshold sum over the batch: each thread writes its neuron's two fp32 sums
 // (over its T steps) to the workspace and reduce_kernel adds them over b in a fixed order in fp64,
@@ -35,10 +39,12 @@ namespace lif {
 constexpr int kBwdThreads = 128;
 constexpr int kReduceThreads = 256;
 
-// (alpha / 2) / (1 + (k u)^2) with k = pi / 2 * alpha: one multiply, one fma, one division.
+// (alpha / 2) / (1 + (k u)^2) with k = pi / 2 * alpha: one multiply, one fma and the fast
+// division (a hardware reciprocal and a multiply, within 2 ulp; the denominator is >= 1).  The
+// IEEE division's extra checking instructions made the special-function pipe the kernel's limit.
 __device__ __forceinline__ float atan_grad(float u, float half_alpha, float k) {
   const float z = k * u;
-  return half_alpha / fmaf(z, z, 1.0f);
+  return __fdividef(half_alpha, fmaf(z, z, 1.0f));
 }
 
 // One neuron per thread.  ckpt [ceil(T / kSeg), NB]; partials [2, NB] (beta, threshold) or null.
@@ -152,8 +158,8 @@ inline int backward(const float* x, const float* ckpt, const float* beta, const 
   const float half_alpha = float(0.5 * double(alpha));
   const float k = float(pi / 2.0 * double(alpha));
   const int64_t grid = (NB + kBwdThreads - 1) / kBwdThreads;
-  int st = launch_pdl(lif_backward_kernel, unsigned(grid), kBwdThreads, 0, stream, x, ckpt, beta, th, grad_spikes,
-                      grad_final_mem, half_alpha, k, T, NB, H, grad_x, grad_mem0, partials);
+  const int st = launch_pdl(lif_backward_kernel, unsigned(grid), kBwdThreads, 0, stream, x, ckpt, beta, th,
+                            grad_spikes, grad_final_mem, half_alpha, k, T, NB, H, grad_x, grad_mem0, partials);
   if (st != kOk || !sums) return st;
   return launch_pdl(lif_reduce_kernel, unsigned((H + kReduceThreads - 1) / kReduceThreads), kReduceThreads, 0, stream,
                     static_cast<const float*>(partials), beta, B, H, grad_beta, grad_th);

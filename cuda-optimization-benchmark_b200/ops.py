@@ -395,12 +395,12 @@ def _leaky_args(input_current, mem0, beta, threshold):
 
 
 def _checkpoint_buffer(T, B, H, dev):
-    return torch.empty(((T + 31) // 32, B, H), dtype=torch.float32, device=dev)
+    return torch.empty(((T + 15) // 16, B, H), dtype=torch.float32, device=dev)
 
 
 def leaky_train(input_current, mem0, beta, threshold):
     """The LIF forward for training: (spikes, final_mem, checkpoints), spikes and final_mem as leaky();
-    checkpoints [ceil(T/32), B, H] are the membrane state before every 32nd step, what
+    checkpoints [ceil(T/16), B, H] are the membrane state before every 16th step, what
     leaky_backward recomputes the trajectory from."""
     dev, T, B, H = _leaky_args(input_current, mem0, beta, threshold)
     spikes = torch.empty_like(input_current)
@@ -433,7 +433,7 @@ def leaky_backward(input_current, checkpoints, beta, threshold, grad_spikes, gra
         _need(t, nm, torch.float32, dev)
     if grad_final_mem is not None:
         _need(grad_final_mem, "grad_final_mem", torch.float32, dev)
-    if checkpoints.numel() != ((T + 31) // 32) * B * H or grad_spikes.shape != input_current.shape:
+    if checkpoints.numel() != ((T + 15) // 16) * B * H or grad_spikes.shape != input_current.shape:
         raise ValueError("leaky_backward: inconsistent shapes")
     lib = _lib()
     gx = torch.empty_like(input_current)
@@ -451,7 +451,7 @@ def leaky_backward(input_current, checkpoints, beta, threshold, grad_spikes, gra
 
 
 class LeakyFunction(torch.autograd.Function):
-    """torch.autograd form of the layer: forward through leaky_train (keeps the 1/8-byte-per-step
+    """torch.autograd form of the layer: forward through leaky_train (keeps the 1/4-byte-per-step
     checkpoints, not the trajectory), backward through leaky_backward."""
 
     @staticmethod

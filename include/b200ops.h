@@ -233,7 +233,7 @@ int b200_leaky_packed_async(const float* input_current, const float* mem0, const
  * restates, through its default arctangent spike surrogate with the reset detached).
  *
  * b200_leaky_train_async: b200_leaky_async (same spikes and final_mem bits) that also stores the
- * membrane checkpoints [ceil(T / 32), B, H] fp32: checkpoint k is the state before step 32k
+ * membrane checkpoints [ceil(T / 16), B, H] fp32: checkpoint k is the state before step 16k
  * (checkpoint 0 = mem0); b200_leaky_checkpoint_bytes gives their size (-1 for negative sizes).
  * b200_leaky_checkpoints_async stores the checkpoints alone (after a forward that did not).
  *

@@ -285,7 +285,7 @@ def leaky_backward(inp, grad_spikes, grad_final_mem=None, alpha=2.0):
     return {"grad_input": gx, "grad_mem0": c, "grad_beta": mask * gb.sum(axis=0),
             "grad_threshold": gt.sum(axis=0), "grad_beta_abs": gb_abs.sum(axis=0),
             "grad_threshold_abs": gt_abs.sum(axis=0), "spikes": (mems[1:] >= th32).astype(np.float32),
-            "final_mem": mems[T], "checkpoints": mems[0:T:32]}
+            "final_mem": mems[T], "checkpoints": mems[0:T:16]}
 
 
 def pack_done_bits(done):

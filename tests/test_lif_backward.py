@@ -13,10 +13,11 @@ GPU, through the C ABI:
 - the training forward gives spikes and final_mem bit-identical to b200_leaky_async and checkpoints
   bit-identical to the oracle's fp32 states; the checkpoints-only entry gives the same bits;
 - the backward meets the oracle on the golden leaky cases (beta outside [0, 1], H = 1021 and 129),
-  T not a multiple of 32, B*H not a multiple of 4, no grad_final_mem, alpha 1 and 4: grad_input and
+  T not a multiple of 16, B*H not a multiple of 4, no grad_final_mem, alpha 1 and 4: grad_input and
   grad_mem0 within atol 1e-5 + rtol 1e-4; grad_beta and grad_threshold within 1e-4 times the sum of
   their terms' magnitudes (plus 1e-6): an fp32 summation over T steps per neuron;
 - the BASELINE.json LIF size (T=256, B=64, H=4096), every output;
+- the outputs do not depend on the inputs' alignment (bit-identical from views one float off);
 - torch.autograd through LeakyFunction returns the C-ABI backward's tensors;
 - status codes.
 """
@@ -156,6 +157,29 @@ def test_shapes(ops, T, B, H, alpha, with_final):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("T,B,H", [(33, 4, 130), (64, 3, 256), (200, 2, 2052)])
+def test_alignment_does_not_matter(ops, T, B, H):
+    """Views one float off a 16-byte boundary give bit-identical outputs."""
+    inp, gs, gf = make(T, B, H, seed=T * 3 + H)
+    dev = {k: inp[k].cuda() for k in KEYS}
+    _, _, ckpt = ops.leaky_train(dev["input_current"], dev["mem0"], dev["beta"], dev["threshold"])
+
+    def shifted(t):
+        raw = torch.empty(t.numel() + 1, dtype=t.dtype, device="cuda")
+        v = raw[1:].view(t.shape)
+        v.copy_(t)
+        return v
+    aligned = ops.leaky_backward(dev["input_current"], ckpt, dev["beta"], dev["threshold"], gs.cuda(), gf.cuda(), 2.0)
+    aligned = [t.clone() for t in aligned]
+    off = ops.leaky_backward(shifted(dev["input_current"]), ckpt, dev["beta"], dev["threshold"], shifted(gs.cuda()),
+                             gf.cuda(), 2.0)
+    torch.cuda.synchronize()
+    for a, b in zip(aligned, off):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+    check_backward(ops, inp, gs, gf, 2.0, got=aligned)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("T,B,H", [(1, 1, 1), (33, 3, 5), (100, 4, 256), (64, 2, 1021)])
 def test_train_forward_and_checkpoints(ops, T, B, H):
     inp, _, _ = make(T, B, H, seed=T + B + H)
@@ -199,7 +223,7 @@ def test_status_codes(ops):
     x = torch.zeros(64, device="cuda")
     y = torch.zeros(64, device="cuda")
     p, q = x.data_ptr(), y.data_ptr()
-    assert lib.b200_leaky_checkpoint_bytes(33, 2, 3) == 2 * 2 * 3 * 4
+    assert lib.b200_leaky_checkpoint_bytes(33, 2, 3) == 3 * 2 * 3 * 4  # one checkpoint per 16 steps
     assert lib.b200_leaky_checkpoint_bytes(-1, 2, 3) == -1
     assert lib.b200_leaky_backward_workspace_bytes(2, 3) == 2 * 2 * 3 * 4
     # workspace too small for the parameter gradients; none needed without them
