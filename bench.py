@@ -675,6 +675,22 @@ def other_ops(ops, dev, world, rank):
                               "frac_of_hbm": nbytes / ms / 1e6 / peak}
     del r, dn, vv, nv, adv, tgt
 
+    # Long rows (T >> B): 8 rows of 2^21 steps (151 MB of reward and done flags), the one-warp-per-
+    # row scan against the chunked one (a warp per 1056-step chunk).  9 algorithmic bytes per step.
+    g = torch.Generator(device=dev).manual_seed(rank)
+    r = torch.rand(8, 1 << 21, device=dev, generator=g)
+    dn = torch.rand(8, 1 << 21, device=dev, generator=g) < 0.001
+    out = torch.empty_like(r)
+    nbytes = 9 * r.numel()
+    ms = timeit(lambda: ops.reward_to_go(r, dn, 0.99, out=out), reps=3)
+    res["reward_to_go B8 T2097152 (one warp per row)"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                                          "frac_of_hbm": nbytes / ms / 1e6 / peak}
+    ms = timeit(lambda: ops.reward_to_go_chunked(r, dn, 0.99, out=out))
+    res["reward_to_go B8 T2097152 (chunked along T)"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
+                                                         "frac_of_hbm": nbytes / ms / 1e6 / peak,
+                                                         "moved_bytes": 14 * r.numel()}
+    del r, dn, out
+
     # Tensor-core ops against the measured dense bf16 peak, burst and sustained (the long GEMMs run
     # at the power-capped clock); FP8 against twice those figures (the E4M3 rate of this part is
     # twice its bf16 rate).  KAN issues three fp16 GEMM passes per

@@ -44,6 +44,11 @@ SIGNATURES = {
     "b200_reward_to_go_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p]),
     "b200_pack_done_async": (c_int, [c_p, c_i32, c_i32, c_p, c_p]),
     "b200_reward_to_go_bits_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p]),
+    "b200_reward_to_go_chunked_workspace_bytes": (c_i64, [c_i32, c_i32]),
+    "b200_reward_to_go_chunked_async": (c_int, [c_p, c_p, c_int, c_f, c_i32, c_i32, c_p, c_p, c_i64, c_p]),
+    "b200_reward_to_go_slice_maps_async": (c_int, [c_p, c_p, c_int, c_f, c_i32, c_i32, c_p, c_p, c_i64, c_p]),
+    "b200_reward_to_go_slice_scan_async": (c_int, [c_p, c_p, c_int, c_f, c_i32, c_i32, c_p, c_int, c_int, c_p, c_p,
+                                                   c_i64, c_p]),
     # fused RL step (reward-to-go + PPO in one launch)
     "b200_rl_step_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p, c_sz,
                                    c_p]),

@@ -17,6 +17,7 @@
 #include "ops/gae.cuh"
 #include "ops/lif_backward.cuh"
 #include "ops/rl_step.cuh"
+#include "ops/rtg_chunked.cuh"
 
 namespace {
 thread_local int g_last_status = 0;
@@ -119,6 +120,35 @@ int b200_pack_done_async(const uint8_t* done, int32_t B, int32_t T, uint32_t* do
 int b200_reward_to_go_bits_async(const float* reward, const uint32_t* done_bits, float gamma, int32_t B, int32_t T,
                                  float* output, void* stream) {
   return b200::rtg::run_bits(reward, done_bits, gamma, B, T, output, as_stream(stream));
+}
+
+int64_t b200_reward_to_go_chunked_workspace_bytes(int32_t B, int32_t T) {
+  if (B < 0 || T < 0) return -1;
+  return b200::rtgc::workspace_bytes(B, T);
+}
+
+int b200_reward_to_go_chunked_async(const float* reward, const void* done, int done_is_bits, float gamma, int32_t B,
+                                    int32_t T, float* output, void* workspace, int64_t workspace_bytes,
+                                    void* stream) {
+  return b200::rtgc::run(reward, done, done_is_bits != 0, gamma, B, T, output, workspace, workspace_bytes,
+                         as_stream(stream));
+}
+
+int b200_reward_to_go_slice_maps_async(const float* reward, const void* done, int done_is_bits, float gamma,
+                                       int32_t B, int32_t T_local, double* slice_maps, void* workspace,
+                                       int64_t workspace_bytes, void* stream) {
+  return b200::rtgc::slice_maps(reward, done, done_is_bits != 0, gamma, B, T_local,
+                                reinterpret_cast<b200::rtgc::Map*>(slice_maps), workspace, workspace_bytes,
+                                as_stream(stream));
+}
+
+int b200_reward_to_go_slice_scan_async(const float* reward, const void* done, int done_is_bits, float gamma,
+                                       int32_t B, int32_t T_local, const double* all_slice_maps, int world,
+                                       int rank, float* output, void* workspace, int64_t workspace_bytes,
+                                       void* stream) {
+  return b200::rtgc::slice_scan(reward, done, done_is_bits != 0, gamma, B, T_local,
+                                reinterpret_cast<const b200::rtgc::Map*>(all_slice_maps), world, rank, output,
+                                workspace, workspace_bytes, as_stream(stream));
 }
 
 // ------------------------------------------------------------------------------ fused RL step

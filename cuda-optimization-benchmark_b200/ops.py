@@ -183,6 +183,82 @@ def reward_to_go_bits(reward, done_bits, gamma, out=None):
     return out
 
 
+def _done_layout(reward, done):
+    """(is_bits, T) for a done tensor: bool [B, T] or int32 bits [B, ceil(T/32)]."""
+    B, T = reward.shape
+    if done.dtype == torch.int32:
+        _need(done, "done_bits", torch.int32, reward.device)
+        if done.shape != (B, (T + 31) // 32):
+            raise ValueError("done bits must be (B, ceil(T/32))")
+        return 1
+    _need(done, "done", torch.bool, reward.device)
+    if done.shape != reward.shape:
+        raise ValueError("reward and done must both be (B, T)")
+    return 0
+
+
+def reward_to_go_chunked(reward, done, gamma, out=None):
+    """reward_to_go parallel along T (for few, long rows); done: bool [B, T] or pack_done bits."""
+    _need(reward, "reward", torch.float32)
+    if reward.dim() != 2:
+        raise ValueError("reward must be (B, T)")
+    bits = _done_layout(reward, done)
+    B, T = reward.shape
+    out = torch.empty_like(reward) if out is None else out
+    lib = _lib()
+    ws = workspace("rtg_chunked", lib.b200_reward_to_go_chunked_workspace_bytes(B, T), reward.device)
+    _native.check(lib.b200_reward_to_go_chunked_async(_ptr(reward), _ptr(done), bits, float(gamma), B, T, _ptr(out),
+                                                      _ptr(ws), ws.numel(), _stream(reward.device)),
+                  "reward_to_go_chunked")
+    return out
+
+
+def reward_to_go_slice_maps(reward, done, gamma, maps_out=None):
+    """First half of reward-to-go sharded over time: this rank's [B, 2] fp64 slice maps (a, b)."""
+    _need(reward, "reward", torch.float32)
+    bits = _done_layout(reward, done)
+    B, T = reward.shape
+    maps_out = torch.empty((B, 2), dtype=torch.float64, device=reward.device) if maps_out is None else maps_out
+    lib = _lib()
+    ws = workspace("rtg_slice", lib.b200_reward_to_go_chunked_workspace_bytes(B, T), reward.device)
+    _native.check(lib.b200_reward_to_go_slice_maps_async(_ptr(reward), _ptr(done), bits, float(gamma), B, T,
+                                                         _ptr(maps_out), _ptr(ws), ws.numel(),
+                                                         _stream(reward.device)), "reward_to_go_slice_maps")
+    return maps_out
+
+
+def reward_to_go_slice_scan(reward, done, gamma, all_maps, rank, out=None):
+    """Second half: this rank's outputs from every rank's slice maps all_maps [world, B, 2] (rank
+    order).  Uses the workspace reward_to_go_slice_maps filled on this stream."""
+    _need(reward, "reward", torch.float32)
+    bits = _done_layout(reward, done)
+    B, T = reward.shape
+    _need(all_maps, "all_maps", torch.float64, reward.device)
+    world = all_maps.shape[0]
+    if all_maps.shape != (world, B, 2):
+        raise ValueError("all_maps must be (world, B, 2)")
+    out = torch.empty_like(reward) if out is None else out
+    lib = _lib()
+    ws = workspace("rtg_slice", lib.b200_reward_to_go_chunked_workspace_bytes(B, T), reward.device)
+    _native.check(lib.b200_reward_to_go_slice_scan_async(_ptr(reward), _ptr(done), bits, float(gamma), B, T,
+                                                         _ptr(all_maps), int(world), int(rank), _ptr(out), _ptr(ws),
+                                                         ws.numel(), _stream(reward.device)),
+                  "reward_to_go_slice_scan")
+    return out
+
+
+def reward_to_go_time_sharded(reward, done, gamma, group=None, out=None):
+    """reward_to_go over rows whose steps are sharded across the ranks of `group` in rank order
+    (this rank holds steps [offset, offset + T_local) of every row): slice maps, one all-gather of
+    16 bytes per row per rank, then this rank's outputs."""
+    import torch.distributed as dist
+    maps = reward_to_go_slice_maps(reward, done, gamma)
+    world = dist.get_world_size(group)
+    all_maps = torch.empty((world,) + tuple(maps.shape), dtype=maps.dtype, device=maps.device)
+    dist.all_gather_into_tensor(all_maps, maps, group=group)
+    return reward_to_go_slice_scan(reward, done, gamma, all_maps, dist.get_rank(group), out=out)
+
+
 # ---------------------------------------------------------------------------- fused RL loss step
 STEP_INPUTS_READY = 1  # B200_STEP_INPUTS_READY
 STEP_DONE_BITS = 2     # B200_STEP_DONE_BITS
