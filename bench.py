@@ -706,7 +706,17 @@ def other_ops(ops, dev, world, rank):
                             "issued_tflops": 3 * flops / ms / 1e9,
                             "frac_of_bf16_peak_issued": 3 * flops / ms / 1e9 / bf16_peak,
                             "frac_of_bf16_sustained_issued": 3 * flops / ms / 1e9 / bf16_sus}
-    del t, kout
+    # The backward at the same size: two GEMMs of the forward's size (grad_out . W' and
+    # grad_out^T . A) plus the operand transposes and the basis derivatives.
+    gy = torch.randn(s["B"], s["O"], device=dev)
+    ms = timeit(lambda: ops.efficient_kan_backward(t["x"], t["grid"], t["base_weight"], t["spline_weight"],
+                                                   t["spline_scaler"], t["grid_size"], t["spline_order"], gy),
+                reps=5)
+    res["efficient_kan backward"] = {"us": ms * 1e3, "useful_tflops": 2 * flops / ms / 1e9,
+                                     "issued_tflops": 6 * flops / ms / 1e9,
+                                     "frac_of_bf16_peak_issued": 6 * flops / ms / 1e9 / bf16_peak,
+                                     "frac_of_bf16_sustained_issued": 6 * flops / ms / 1e9 / bf16_sus}
+    del t, kout, gy
     # FP8 at the four BASELINE shapes; inputs drawn on the device (the values do not change the
     # timing; parity is tested on the oracle's own inputs).
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
@@ -859,6 +869,13 @@ def run_profile(ops_list, reps):
             lib.b200_efficient_kan_async(t["x"].data_ptr(), t["grid"].data_ptr(), t["base_weight"].data_ptr(),
                                          t["spline_weight"].data_ptr(), t["spline_scaler"].data_ptr(), 5, 3, s["B"],
                                          s["I"], s["O"], out.data_ptr(), ws.data_ptr(), nb, None)
+    if "kan_backward" in ops_list:
+        s = inputs.baseline_inputs("kan", 0)
+        t = {k: s[k].to(dev) for k in ["x", "grid", "base_weight", "spline_weight", "spline_scaler"]}
+        gy = torch.randn(s["B"], s["O"], device=dev)
+        for _ in range(reps):
+            ops.efficient_kan_backward(t["x"], t["grid"], t["base_weight"], t["spline_weight"], t["spline_scaler"], 5, 3,
+                                       gy)
     for name in [x for x in ops_list if x in PROFILE_FP8]:
         M, N, K = PROFILE_FP8[name]
         s = inputs.baseline_inputs("fp8_linear", 0, shape=(M, N, K))
@@ -880,7 +897,7 @@ def main():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile", default=None,
-                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, lif_backward, robust_l1, kan, fp8_m16, fp8_m1024, "
+                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, lif_backward, robust_l1, kan, kan_backward, fp8_m16, fp8_m1024, "
                          "fp8_8192, "
                          "fp8_16384, fp8_ref_timed): run each --steps times for ncu, no timing")
     args = ap.parse_args()

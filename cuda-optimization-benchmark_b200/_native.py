@@ -82,6 +82,9 @@ SIGNATURES = {
     "b200_efficient_kan_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
     "b200_efficient_kan_async": (c_int, [c_p, c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p, c_sz,
                                          c_p]),
+    "b200_efficient_kan_backward_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "b200_efficient_kan_backward_async": (c_int, [c_p, c_p, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i32, c_i32, c_p, c_p,
+                                                  c_p, c_p, c_p, c_p, c_sz, c_p]),
     # FP8 linear
     "b200_fp8_linear": (None, [c_i32, c_i32, c_i32, c_p, c_f, c_p, c_f, c_p, c_p]),
     "b200_fp8_linear_async": (c_int, [c_i32, c_i32, c_i32, c_p, c_f, c_p, c_f, c_p, c_p, c_p]),

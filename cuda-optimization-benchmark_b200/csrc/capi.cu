@@ -15,6 +15,7 @@
 #include "dropin/reward_to_go.cuh"
 #include "ops/fp8_pipeline.cuh"
 #include "ops/gae.cuh"
+#include "ops/kan_backward.cuh"
 #include "ops/lif_backward.cuh"
 #include "ops/rl_step.cuh"
 #include "ops/rtg_chunked.cuh"
@@ -330,6 +331,23 @@ int b200_efficient_kan_async(const float* x, const float* grid, const float* bas
                              void* stream) {
   return b200::kan::run(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, B, I, O, out,
                         workspace, workspace_bytes, as_stream(stream));
+}
+
+size_t b200_efficient_kan_backward_workspace_bytes(int32_t grid_size, int32_t spline_order, int32_t B, int32_t I,
+                                                   int32_t O) {
+  if (grid_size < 1 || spline_order < 0 || B < 0 || I < 0 || O < 0) return 0;
+  return b200::kanb::workspace_bytes(B, I, O, grid_size + spline_order);
+}
+
+int b200_efficient_kan_backward_async(const float* x, const float* grid, const float* base_weight,
+                                      const float* spline_weight, const float* spline_scaler, int32_t grid_size,
+                                      int32_t spline_order, int32_t B, int32_t I, int32_t O, const float* grad_out,
+                                      float* grad_x, float* grad_base_weight, float* grad_spline_weight,
+                                      float* grad_spline_scaler, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+  return b200::kanb::backward(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, B, I, O,
+                              grad_out, grad_x, grad_base_weight, grad_spline_weight, grad_spline_scaler, workspace,
+                              workspace_bytes, as_stream(stream));
 }
 
 }  // extern "C"

@@ -572,6 +572,54 @@ def efficient_kan(x, grid, base_weight, spline_weight, spline_scaler, grid_size,
     return out
 
 
+def efficient_kan_backward(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order, grad_out,
+                           need_x=True, need_weights=True):
+    """Gradients of efficient_kan for grad_out [B, O]: (grad_x, grad_base_weight, grad_spline_weight,
+    grad_spline_scaler); the input gradient is None unless need_x, the weight gradients None
+    unless need_weights."""
+    _need(x, "x", torch.float32)
+    dev = x.device
+    for t, nm in ((grid, "grid"), (base_weight, "base_weight"), (spline_weight, "spline_weight"),
+                  (spline_scaler, "spline_scaler"), (grad_out, "grad_out")):
+        _need(t, nm, torch.float32, dev)
+    B, I = x.shape
+    O = base_weight.shape[0]
+    G, K = int(grid_size), int(spline_order)
+    if grid.shape != (I, G + 2 * K + 1) or base_weight.shape != (O, I) or spline_weight.shape != (O, I, G + K) \
+            or spline_scaler.shape != (O, I) or grad_out.shape != (B, O):
+        raise ValueError("efficient_kan_backward: inconsistent shapes")
+    gx = torch.empty_like(x) if need_x else None
+    gwb = torch.empty_like(base_weight) if need_weights else None
+    gsw = torch.empty_like(spline_weight) if need_weights else None
+    gsc = torch.empty_like(spline_scaler) if need_weights else None
+    lib = _lib()
+    ws = workspace("kan_backward", lib.b200_efficient_kan_backward_workspace_bytes(G, K, B, I, O), dev)
+    _native.check(lib.b200_efficient_kan_backward_async(_ptr(x), _ptr(grid), _ptr(base_weight), _ptr(spline_weight),
+                                                        _ptr(spline_scaler), G, K, B, I, O, _ptr(grad_out), _ptr(gx),
+                                                        _ptr(gwb), _ptr(gsw), _ptr(gsc), _ptr(ws), ws.numel(),
+                                                        _stream(dev)), "efficient_kan_backward")
+    return gx, gwb, gsw, gsc
+
+
+class KANLinearFunction(torch.autograd.Function):
+    """torch.autograd form of the KAN layer: forward through efficient_kan, backward through
+    efficient_kan_backward (the knot grid gets no gradient, as a KANLinear buffer)."""
+
+    @staticmethod
+    def forward(ctx, x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order):
+        ctx.save_for_backward(x, grid, base_weight, spline_weight, spline_scaler)
+        ctx.gk = (int(grid_size), int(spline_order))
+        return efficient_kan(x, grid, base_weight, spline_weight, spline_scaler, grid_size, spline_order)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x, grid, wb, sw, sc = ctx.saved_tensors
+        need_x = ctx.needs_input_grad[0]
+        need_w = any(ctx.needs_input_grad[2:5])
+        gx, gwb, gsw, gsc = efficient_kan_backward(x, grid, wb, sw, sc, *ctx.gk, grad_out.contiguous(), need_x, need_w)
+        return gx, None, gwb, gsw, gsc, None, None
+
+
 # ---------------------------------------------------------------------------------- FP8 linear
 def fp8_quantize(x, q=None, scale=None):
     """Per-tensor E4M3 quantisation of an fp32 or bf16 tensor (tasks/fp8_linear/reference.py:15-18):

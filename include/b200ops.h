@@ -306,6 +306,21 @@ int b200_efficient_kan_async(const float* x, const float* grid, const float* bas
                              int32_t I, int32_t O, float* out, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* Backward of the layer (no reference counterpart: the gradients torch autograd forms through
+ * tasks/efficient_kan/reference.py:33-46) for grad_out [B, O]: grad_x [B, I], grad_base_weight
+ * [O, I], grad_spline_weight [O, I, G+K], grad_spline_scaler [O, I]; any of them may be NULL (not
+ * computed).  The two GEMMs (grad_out . W' and grad_out^T . A) run on the forward's split-fp16
+ * tensor-core kernel.  Workspace: b200_efficient_kan_backward_workspace_bytes(...) bytes (no
+ * initialisation); status 5 when G + 2K + 1 > 64 or the (1 + G + K)-row tiles exceed shared memory. */
+size_t b200_efficient_kan_backward_workspace_bytes(int32_t grid_size, int32_t spline_order, int32_t B, int32_t I,
+                                                   int32_t O);
+int b200_efficient_kan_backward_async(const float* x, const float* grid, const float* base_weight,
+                                      const float* spline_weight, const float* spline_scaler, int32_t grid_size,
+                                      int32_t spline_order, int32_t B, int32_t I, int32_t O, const float* grad_out,
+                                      float* grad_x, float* grad_base_weight, float* grad_spline_weight,
+                                      float* grad_spline_scaler, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * FP8 E4M3 linear layer (task fp8_linear): output[M, N] (bf16) =
  * (x_fp8[M, K] . w_fp8[N, K]^T) / (scale_x * scale_w) + bias[N].

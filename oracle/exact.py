@@ -298,3 +298,61 @@ def pack_done_bits(done):
     padded[:, :T] = d
     weights = np.left_shift(np.uint64(1), np.arange(32, dtype=np.uint64))
     return (padded.reshape(B, W, 32) * weights).sum(axis=2).astype(np.uint32)
+
+
+def efficient_kan_backward(inp, grad_out, rows=None):
+    """Backward of the KAN layer in fp64 (no reference implementation in the reference repository:
+    the gradients of tasks/efficient_kan/reference.py:33-46, the KANLinear forward, that torch
+    autograd forms through it).  With W_spl = spline_weight * spline_scaler and the bases B_c(x)
+    and their derivatives from forward-mode differentiation of the same Cox-de Boor recurrence:
+
+        grad_x[b,i]      = silu'(x) * (G @ W_base)[b,i] + sum_c B'_c(x[b,i]) * (G @ W_spl)[b,i,c]
+        grad_W_base      = G^T @ silu(x)
+        grad_W_spl       = G^T @ B(x)                       ([O, I, C])
+        grad_sw          = grad_W_spl * spline_scaler;  grad_scaler = sum_c grad_W_spl * sw
+
+    `rows` limits grad_x to a subset of batch rows (the weight gradients always use every row).
+    *_abs: the same sums over the terms' magnitudes (the scale of a summation's rounding error)."""
+    x = _np(inp["x"]).astype(np.float64)
+    g = _np(inp["grid"]).astype(np.float64)
+    wb = _np(inp["base_weight"]).astype(np.float64)
+    sw = _np(inp["spline_weight"]).astype(np.float64)
+    sc = _np(inp["spline_scaler"]).astype(np.float64)
+    G = _np(grad_out).astype(np.float64)
+    K = int(inp["spline_order"])
+    B, I = x.shape
+    O = wb.shape[0]
+    C = sw.shape[2]
+    xe = x[:, :, None]
+    bases = ((xe >= g[None, :, :-1]) & (xe < g[None, :, 1:])).astype(np.float64)
+    dbases = np.zeros_like(bases)
+    for k in range(1, K + 1):
+        dl = 1.0 / (g[None, :, k:-1] - g[None, :, :-(k + 1)])
+        dr = -1.0 / (g[None, :, k + 1:] - g[None, :, 1:-k])
+        left = (xe - g[None, :, :-(k + 1)]) * dl
+        right = (g[None, :, k + 1:] - xe) * -dr
+        nb = left * bases[:, :, :-1] + right * bases[:, :, 1:]
+        dbases = dl * bases[:, :, :-1] + left * dbases[:, :, :-1] + dr * bases[:, :, 1:] + right * dbases[:, :, 1:]
+        bases = nb
+    s = 1.0 / (1.0 + np.exp(-x))
+    silu = x * s
+    dsilu = s * (1.0 + x * (1.0 - s))
+    wspl = (sw * sc[:, :, None]).reshape(O, I * C)
+    xr = slice(None) if rows is None else rows
+    Gr = G[xr]
+    ga_base = Gr @ wb
+    ga_spl = (Gr @ wspl).reshape(-1, I, C)
+    ga_base_abs = np.abs(Gr) @ np.abs(wb)
+    ga_spl_abs = (np.abs(Gr) @ np.abs(wspl)).reshape(-1, I, C)
+    grad_x = ga_base * dsilu[xr] + (ga_spl * dbases[xr]).sum(axis=2)
+    grad_x_abs = ga_base_abs * np.abs(dsilu[xr]) + (ga_spl_abs * np.abs(dbases[xr])).sum(axis=2)
+    gw_base = G.T @ silu
+    gw_base_abs = np.abs(G).T @ np.abs(silu)
+    bflat = bases.reshape(B, I * C)
+    gw_spl = (G.T @ bflat).reshape(O, I, C)
+    gw_spl_abs = (np.abs(G).T @ bflat).reshape(O, I, C)
+    return {"grad_x": grad_x, "grad_base_weight": gw_base, "grad_spline_weight": gw_spl * sc[:, :, None],
+            "grad_spline_scaler": (gw_spl * sw).sum(axis=2),
+            "grad_x_abs": grad_x_abs, "grad_base_weight_abs": gw_base_abs,
+            "grad_spline_weight_abs": gw_spl_abs * np.abs(sc[:, :, None]),
+            "grad_spline_scaler_abs": (gw_spl_abs * np.abs(sw)).sum(axis=2)}
