@@ -31,14 +31,14 @@ constexpr int kTile = 32;              // transpose tiles: 32 x 32, 32 x 8 threa
 constexpr int kTileRows = 8;
 constexpr int kSplitThreads = 256;
 constexpr int kColThreads = 256;
-constexpr int kColChunk = 512;         // rows per CTA of the column-max pass
+constexpr int kColChunk = 32;          // rows per CTA of the column-max pass
 constexpr int kGradThreads = 256;
 constexpr int kMaxTileSmem = 200 * 1024;
 
 inline int64_t pad64(int64_t v) { return (v + 63) / 64 * 64; }
 
 struct Layout {
-  size_t g_hi, g_lo, rg, wt_hi, wt_lo, cwt, gt_hi, gt_lo, rgt, at_hi, at_lo, cat, amax_wt, amax_gt, amax_silu, grad_a,
+  size_t g_hi, g_lo, rg, wt_hi, wt_lo, cwt, gt_hi, gt_lo, rgt, at_hi, at_lo, cat, amax_wt, amax_gt, amax_x, grad_a,
       grad_w, total;
 };
 
@@ -65,7 +65,7 @@ inline Layout layout(int B, int I, int O, int C) {
   L.cat = take(size_t(nk) * 4);
   L.amax_wt = take(size_t(nk) * 4);
   L.amax_gt = take(size_t(O) * 4);
-  L.amax_silu = take(size_t(I) * 4);
+  L.amax_x = take(size_t(I) * 4);
   L.grad_a = take(size_t(B) * nk * 4);
   L.grad_w = take(size_t(O) * nk * 4);
   L.total = off;
@@ -92,9 +92,8 @@ __global__ void __launch_bounds__(kSplitThreads) split_rows_kernel(const float* 
   }
 }
 
-// amax[c] = max over rows of |f(src[row, c])| (f = identity, or silu): a thread per column, a
-// block of kColChunk rows per CTA row, combined with atomicMax on the non-negative float bits.
-template <bool kSilu>
+// amax[c] = max over rows of |src[row, c]|: a thread per column, a block of kColChunk rows per CTA
+// row, combined with atomicMax on the non-negative float bits.
 __global__ void __launch_bounds__(kColThreads) colmax_kernel(const float* __restrict__ src, int64_t rows, int cols,
                                                              uint32_t* __restrict__ amax) {
   pdl_begin();
@@ -103,10 +102,7 @@ __global__ void __launch_bounds__(kColThreads) colmax_kernel(const float* __rest
   const int64_t r0 = int64_t(blockIdx.y) * kColChunk;
   const int64_t r1 = r0 + kColChunk < rows ? r0 + kColChunk : rows;
   float m = 0.0f;
-  for (int64_t r = r0; r < r1; ++r) {
-    const float v = src[r * cols + c];
-    m = fmaxf(m, fabsf(kSilu ? kan::silu(v) : v));
-  }
+  for (int64_t r = r0; r < r1; ++r) m = fmaxf(m, fabsf(src[r * cols + c]));
   atomicMax(amax + c, __float_as_uint(m));
 }
 
@@ -205,11 +201,14 @@ __global__ void __launch_bounds__(kTile * kTileRows) wt_split_kernel(const float
 
 // A transposed into planes [I(1+C), kp = pad64(B)]: a tile of 32 inputs x 32 batch rows; each
 // thread evaluates silu and the bases of one x (the forward's recurrence) into shared memory.
-// Plane rows p = 0 take the factor of the input's max |silu| over the batch; bases lie in [0, 1].
+// Plane rows p = 0 take the factor of the input's max |x| over the batch (|silu(x)| <= |x|); bases
+// lie in [0, 1].  Only the K + 1 bases that can be non-zero are formed (kan::bases_local).
+// NK, KO > 0: knot count and order known at compile time (the recurrence unrolled in registers).
+template <int NK, int KO>
 __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float* __restrict__ x,
                                                                      const float* __restrict__ grid, int B, int I,
                                                                      int C, int K, int64_t kp,
-                                                                     const uint32_t* __restrict__ amax_silu,
+                                                                     const uint32_t* __restrict__ amax_x,
                                                                      __half* __restrict__ hi, __half* __restrict__ lo,
                                                                      float* __restrict__ unscale) {
   pdl_begin();
@@ -218,16 +217,26 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
   const int i0 = blockIdx.x * kTile, b0 = blockIdx.y * kTile;
   const int i = i0 + tx;
   const int nk = C + K + 1;
-  float g[kMaxKnots], bs[kMaxKnots];
-  if (i < I)
-    for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
   for (int y = ty; y < kTile; y += kTileRows) {
     const int b = b0 + y;
     const bool ok = i < I && b < B;
     const float xv = ok ? x[int64_t(b) * I + i] : 0.0f;
     s_t[(0 * kTile + tx) * (kTile + 1) + y] = ok ? kan::silu(xv) : 0.0f;
-    if (ok) kan::bases_of(xv, g, nk, K, bs);
-    for (int c = 0; c < C; ++c) s_t[((1 + c) * kTile + tx) * (kTile + 1) + y] = ok ? bs[c] : 0.0f;
+    if (NK > 0) {
+      float bs[NK > 0 ? NK : 1];
+      if (ok && !kan::bases_local<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs))
+        kan::bases_fixed<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs);
+#pragma unroll
+      for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c)
+        s_t[((1 + c) * kTile + tx) * (kTile + 1) + y] = ok ? bs[c] : 0.0f;
+    } else {
+      float g[kMaxKnots], bs[kMaxKnots];
+      if (ok) {
+        for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
+        kan::bases_of(xv, g, nk, K, bs);
+      }
+      for (int c = 0; c < C; ++c) s_t[((1 + c) * kTile + tx) * (kTile + 1) + y] = ok ? bs[c] : 0.0f;
+    }
   }
   __syncthreads();
   const int rows = (1 + C) * kTile;
@@ -235,7 +244,7 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
     const int p = rr / kTile, ii = rr - p * kTile;
     if (i0 + ii >= I) continue;
     const int64_t kr = int64_t(p) * I + i0 + ii;
-    const float f = p == 0 ? kan::fp16_row_factor(__uint_as_float(amax_silu[i0 + ii])) : 1.0f;
+    const float f = p == 0 ? kan::fp16_row_factor(__uint_as_float(amax_x[i0 + ii])) : 1.0f;
     if (blockIdx.y == 0 && tx == 0) unscale[kr] = 1.0f / f;
     const int64_t b = b0 + tx;
     if (b < kp) kan::split_store(s_t[(p * kTile + ii) * (kTile + 1) + tx] * f, hi + kr * kp + b, lo + kr * kp + b);
@@ -262,7 +271,103 @@ __device__ __forceinline__ void bases_dual(float x, const float* g, int nk, int 
   }
 }
 
-// grad_x[b, i] from grad_A [B, I(1+C)]: a thread per (b, i), i fastest.
+// The same with the knot count NK and order KO known at compile time (registers only).
+template <int NK, int KO>
+__device__ __forceinline__ void bases_dual_fixed(float x, const float* __restrict__ gsrc, float* b, float* db) {
+  float g[NK];
+#pragma unroll
+  for (int j = 0; j < NK; ++j) g[j] = __ldg(gsrc + j);
+#pragma unroll
+  for (int j = 0; j < NK - 1; ++j) {
+    b[j] = (x >= g[j] && x < g[j + 1]) ? 1.0f : 0.0f;
+    db[j] = 0.0f;
+  }
+#pragma unroll
+  for (int k = 1; k <= KO; ++k) {
+#pragma unroll
+    for (int j = 0; j < NK - 1 - k; ++j) {
+      const float dl = 1.0f / (g[j + k] - g[j]);
+      const float dr = -1.0f / (g[j + k + 1] - g[j + 1]);
+      const float l = (x - g[j]) * dl;
+      const float r = (g[j + k + 1] - x) * -dr;
+      const float nb = l * b[j] + r * b[j + 1];
+      db[j] = dl * b[j] + l * db[j] + dr * b[j + 1] + r * db[j + 1];
+      b[j] = nb;
+    }
+  }
+}
+
+// Only the bases that can be non-zero, with their derivatives (as kan::bases_local: for strictly
+// increasing knots and g[j0] <= x < g[j0+1], the order-k bases j0-k .. j0).  out / dout receive all
+// NK - KO - 1 order-KO bases and derivatives.  Returns false when the knots are not increasing.
+template <int NK, int KO>
+__device__ __forceinline__ bool bases_dual_local(float x, const float* __restrict__ gsrc, float* out, float* dout) {
+  constexpr int C = NK - KO - 1;
+  float g[NK];
+#pragma unroll
+  for (int j = 0; j < NK; ++j) g[j] = __ldg(gsrc + j);
+  bool inc = true;
+  int j0 = -1;
+#pragma unroll
+  for (int j = 0; j < NK - 1; ++j) {
+    inc = inc && (g[j] < g[j + 1]);
+    if (x >= g[j] && x < g[j + 1]) j0 = j;
+  }
+  if (!inc) return false;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    out[c] = 0.0f;
+    dout[c] = 0.0f;
+  }
+  if (j0 < 0) return true;
+  float nb[KO + 1], nd[KO + 1];
+  nb[0] = 1.0f;
+  nd[0] = 0.0f;
+#pragma unroll
+  for (int k = 1; k <= KO; ++k) {
+    float nn[KO + 1], nnd[KO + 1];
+#pragma unroll
+    for (int m = 0; m <= k; ++m) {
+      const int j = j0 - k + m;
+      float v = 0.0f, dv = 0.0f;
+      if (j >= 0 && j <= NK - 2 - k) {
+        if (m >= 1) {  // (x - g[j]) / (g[j+k] - g[j]) * b_{k-1}[j]
+          const float il = __frcp_rn(g[j + k] - g[j]);
+          const float l = (x - g[j]) * il;
+          v = l * nb[m - 1];
+          dv = il * nb[m - 1] + l * nd[m - 1];
+        }
+        if (m <= k - 1) {  // (g[j+k+1] - x) / (g[j+k+1] - g[j+1]) * b_{k-1}[j+1]
+          const float ir = __frcp_rn(g[j + k + 1] - g[j + 1]);
+          const float r = (g[j + k + 1] - x) * ir;
+          v += r * nb[m];
+          dv += r * nd[m] - ir * nb[m];
+        }
+      }
+      nn[m] = v;
+      nnd[m] = dv;
+    }
+#pragma unroll
+    for (int m = 0; m <= k; ++m) {
+      nb[m] = nn[m];
+      nd[m] = nnd[m];
+    }
+  }
+#pragma unroll
+  for (int m = 0; m <= KO; ++m) {
+    const int j = j0 - KO + m;
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+      if (c == j) {
+        out[c] = nb[m];
+        dout[c] = nd[m];
+      }
+  }
+  return true;
+}
+
+// grad_x[b, i] from grad_A [B, I(1+C)]: a thread per (b, i), i fastest.  NK, KO as at_split_kernel.
+template <int NK, int KO>
 __global__ void __launch_bounds__(kGradThreads) grad_x_kernel(const float* __restrict__ x,
                                                               const float* __restrict__ grid,
                                                               const float* __restrict__ ga, int64_t B, int I, int C,
@@ -273,16 +378,24 @@ __global__ void __launch_bounds__(kGradThreads) grad_x_kernel(const float* __res
   const int64_t b = q / I;
   const int i = int(q - b * I);
   const int nk = C + K + 1;
-  float g[kMaxKnots], bs[kMaxKnots], dbs[kMaxKnots];
-  for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
   const float xv = x[q];
-  bases_dual(xv, g, nk, K, bs, dbs);
   const float s = 1.0f / (1.0f + expf(-xv));
   const float dsilu = s * (1.0f + xv * (1.0f - s));
   const int64_t nkp = int64_t(I) * (1 + C);
   const float* row = ga + b * nkp + i;
   float acc = row[0] * dsilu;
-  for (int c = 0; c < C; ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
+  if (NK > 0) {
+    float bs[NK > 0 ? NK : 1], dbs[NK > 0 ? NK : 1];
+    if (!bases_dual_local<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs, dbs))
+      bases_dual_fixed<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs, dbs);
+#pragma unroll
+    for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
+  } else {
+    float g[kMaxKnots], bs[kMaxKnots], dbs[kMaxKnots];
+    for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
+    bases_dual(xv, g, nk, K, bs, dbs);
+    for (int c = 0; c < C; ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
+  }
   gx[q] = acc;
 }
 
@@ -359,7 +472,11 @@ inline int backward(const float* x, const float* grid, const float* wb, const fl
   const int64_t nkp = int64_t(I) * (1 + C), op = pad64(O), bp = pad64(B);
   if (nkp > 0x7fffffff) return kUnsupported;
   const size_t tsm = tile_smem(C);
-  if (!ensure_dyn_smem(wt_split_kernel, int(tsm)) || !ensure_dyn_smem(at_split_kernel, int(tsm))) return kCudaError;
+  // The cubic cases of the reference (G = 5 and G = 8) take the unrolled recurrences.
+  const int form = K == 3 && G == 5 ? 1 : (K == 3 && G == 8 ? 2 : 0);
+  auto at_kern = form == 1 ? at_split_kernel<12, 3> : (form == 2 ? at_split_kernel<15, 3> : at_split_kernel<0, 0>);
+  auto gx_kern = form == 1 ? grad_x_kernel<12, 3> : (form == 2 ? grad_x_kernel<15, 3> : grad_x_kernel<0, 0>);
+  if (!ensure_dyn_smem(wt_split_kernel, int(tsm)) || !ensure_dyn_smem(at_kern, int(tsm))) return kCudaError;
   const dim3 tb(kTile, kTileRows);
   int st = kOk;
   if (need_x) {
@@ -377,26 +494,26 @@ inline int backward(const float* x, const float* grid, const float* wb, const fl
     st = gemm(half_at(L.g_hi), half_at(L.g_lo), B, half_at(L.wt_hi), half_at(L.wt_lo), int(nkp), op, float_at(L.rg),
               float_at(L.cwt), float_at(L.grad_a), stream);
     if (st != kOk) return st;
-    st = launch_pdl(grad_x_kernel, unsigned((int64_t(B) * I + kGradThreads - 1) / kGradThreads), kGradThreads, 0,
-                    stream, x, grid, static_cast<const float*>(float_at(L.grad_a)), int64_t(B), I, C, K, grad_x);
+    st = launch_pdl(gx_kern, unsigned((int64_t(B) * I + kGradThreads - 1) / kGradThreads), kGradThreads, 0, stream, x,
+                    grid, static_cast<const float*>(float_at(L.grad_a)), int64_t(B), I, C, K, grad_x);
     if (st != kOk) return st;
   }
   if (need_w) {
     cudaMemsetAsync(u32_at(L.amax_gt), 0, size_t(O) * 4, stream);
-    cudaMemsetAsync(u32_at(L.amax_silu), 0, size_t(I) * 4, stream);
+    cudaMemsetAsync(u32_at(L.amax_x), 0, size_t(I) * 4, stream);
     const unsigned chunks = unsigned((int64_t(B) + kColChunk - 1) / kColChunk);
-    st = launch_pdl(colmax_kernel<false>, dim3(unsigned((O + kColThreads - 1) / kColThreads), chunks), kColThreads,
+    st = launch_pdl(colmax_kernel, dim3(unsigned((O + kColThreads - 1) / kColThreads), chunks), kColThreads,
                     0, stream, grad_out, int64_t(B), O, u32_at(L.amax_gt));
     if (st != kOk) return st;
     st = launch_pdl(split_cols_kernel, dim3(unsigned(bp / kTile), unsigned((O + kTile - 1) / kTile)), tb, 0, stream,
                     grad_out, B, O, bp, static_cast<const uint32_t*>(u32_at(L.amax_gt)), half_at(L.gt_hi),
                     half_at(L.gt_lo), float_at(L.rgt));
     if (st != kOk) return st;
-    st = launch_pdl(colmax_kernel<true>, dim3(unsigned((I + kColThreads - 1) / kColThreads), chunks), kColThreads, 0,
-                    stream, x, int64_t(B), I, u32_at(L.amax_silu));
+    st = launch_pdl(colmax_kernel, dim3(unsigned((I + kColThreads - 1) / kColThreads), chunks), kColThreads, 0,
+                    stream, x, int64_t(B), I, u32_at(L.amax_x));
     if (st != kOk) return st;
-    st = launch_pdl(at_split_kernel, dim3(unsigned((I + kTile - 1) / kTile), unsigned(bp / kTile)), tb, tsm, stream,
-                    x, grid, B, I, C, K, bp, static_cast<const uint32_t*>(u32_at(L.amax_silu)), half_at(L.at_hi),
+    st = launch_pdl(at_kern, dim3(unsigned((I + kTile - 1) / kTile), unsigned(bp / kTile)), tb, tsm, stream,
+                    x, grid, B, I, C, K, bp, static_cast<const uint32_t*>(u32_at(L.amax_x)), half_at(L.at_hi),
                     half_at(L.at_lo), float_at(L.cat));
     if (st != kOk) return st;
     st = gemm(half_at(L.gt_hi), half_at(L.gt_lo), O, half_at(L.at_hi), half_at(L.at_lo), int(nkp), bp,
