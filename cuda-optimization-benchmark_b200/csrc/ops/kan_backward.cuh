@@ -199,6 +199,42 @@ __global__ void __launch_bounds__(kTile * kTileRows) wt_split_kernel(const float
   }
 }
 
+// One input's knots g[0..NK) and reciprocal knot differences rk[k-1][j] = 1 / (g[j+k] - g[j])
+// (j < NK - k), in registers: the same input's recurrence then runs on multiplies for every row a
+// thread handles.
+template <int NK, int KO>
+__device__ __forceinline__ void load_knots(const float* __restrict__ gsrc, float (&g)[NK], float (&rk)[KO][NK]) {
+#pragma unroll
+  for (int j = 0; j < NK; ++j) g[j] = __ldg(gsrc + j);
+#pragma unroll
+  for (int k = 1; k <= KO; ++k)
+#pragma unroll
+    for (int j = 0; j < NK - k; ++j) rk[k - 1][j] = 1.0f / (g[j + k] - g[j]);
+}
+
+// The Cox-de Boor recurrence (every basis, unrolled) on the reciprocals; with kDeriv the
+// derivatives d/dx ride along (b'[j] = l' b[j] + l b'[j] + r' b[j+1] + r b'[j+1]).
+template <int NK, int KO, bool kDeriv>
+__device__ __forceinline__ void bases_recip(float x, const float (&g)[NK], const float (&rk)[KO][NK], float* b,
+                                            float* db) {
+#pragma unroll
+  for (int j = 0; j < NK - 1; ++j) {
+    b[j] = (x >= g[j] && x < g[j + 1]) ? 1.0f : 0.0f;
+    if (kDeriv) db[j] = 0.0f;
+  }
+#pragma unroll
+  for (int k = 1; k <= KO; ++k) {
+#pragma unroll
+    for (int j = 0; j < NK - 1 - k; ++j) {
+      const float il = rk[k - 1][j], ir = rk[k - 1][j + 1];
+      const float l = (x - g[j]) * il, r = (g[j + k + 1] - x) * ir;
+      const float nb = l * b[j] + r * b[j + 1];
+      if (kDeriv) db[j] = il * b[j] + l * db[j] - ir * b[j + 1] + r * db[j + 1];
+      b[j] = nb;
+    }
+  }
+}
+
 // A transposed into planes [I(1+C), kp = pad64(B)]: a tile of 32 inputs x 32 batch rows; each
 // thread evaluates silu and the bases of one x (the forward's recurrence) into shared memory.
 // Plane rows p = 0 take the factor of the input's max |x| over the batch (|silu(x)| <= |x|); bases
@@ -217,15 +253,17 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
   const int i0 = blockIdx.x * kTile, b0 = blockIdx.y * kTile;
   const int i = i0 + tx;
   const int nk = C + K + 1;
+  constexpr int NKr = NK > 0 ? NK : 2, KOr = KO > 0 ? KO : 1;
+  float gr[NKr], rk[KOr][NKr];
+  if (NK > 0 && i < I) load_knots<NKr, KOr>(grid + int64_t(i) * nk, gr, rk);
   for (int y = ty; y < kTile; y += kTileRows) {
     const int b = b0 + y;
     const bool ok = i < I && b < B;
     const float xv = ok ? x[int64_t(b) * I + i] : 0.0f;
     s_t[(0 * kTile + tx) * (kTile + 1) + y] = ok ? kan::silu(xv) : 0.0f;
     if (NK > 0) {
-      float bs[NK > 0 ? NK : 1];
-      if (ok && !kan::bases_local<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs))
-        kan::bases_fixed<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs);
+      float bs[NKr];
+      if (ok) bases_recip<NKr, KOr, false>(xv, gr, rk, bs, nullptr);
 #pragma unroll
       for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c)
         s_t[((1 + c) * kTile + tx) * (kTile + 1) + y] = ok ? bs[c] : 0.0f;
@@ -271,132 +309,49 @@ __device__ __forceinline__ void bases_dual(float x, const float* g, int nk, int 
   }
 }
 
-// The same with the knot count NK and order KO known at compile time (registers only).
-template <int NK, int KO>
-__device__ __forceinline__ void bases_dual_fixed(float x, const float* __restrict__ gsrc, float* b, float* db) {
-  float g[NK];
-#pragma unroll
-  for (int j = 0; j < NK; ++j) g[j] = __ldg(gsrc + j);
-#pragma unroll
-  for (int j = 0; j < NK - 1; ++j) {
-    b[j] = (x >= g[j] && x < g[j + 1]) ? 1.0f : 0.0f;
-    db[j] = 0.0f;
-  }
-#pragma unroll
-  for (int k = 1; k <= KO; ++k) {
-#pragma unroll
-    for (int j = 0; j < NK - 1 - k; ++j) {
-      const float dl = 1.0f / (g[j + k] - g[j]);
-      const float dr = -1.0f / (g[j + k + 1] - g[j + 1]);
-      const float l = (x - g[j]) * dl;
-      const float r = (g[j + k + 1] - x) * -dr;
-      const float nb = l * b[j] + r * b[j + 1];
-      db[j] = dl * b[j] + l * db[j] + dr * b[j + 1] + r * db[j + 1];
-      b[j] = nb;
-    }
-  }
-}
-
-// Only the bases that can be non-zero, with their derivatives (as kan::bases_local: for strictly
-// increasing knots and g[j0] <= x < g[j0+1], the order-k bases j0-k .. j0).  out / dout receive all
-// NK - KO - 1 order-KO bases and derivatives.  Returns false when the knots are not increasing.
-template <int NK, int KO>
-__device__ __forceinline__ bool bases_dual_local(float x, const float* __restrict__ gsrc, float* out, float* dout) {
-  constexpr int C = NK - KO - 1;
-  float g[NK];
-#pragma unroll
-  for (int j = 0; j < NK; ++j) g[j] = __ldg(gsrc + j);
-  bool inc = true;
-  int j0 = -1;
-#pragma unroll
-  for (int j = 0; j < NK - 1; ++j) {
-    inc = inc && (g[j] < g[j + 1]);
-    if (x >= g[j] && x < g[j + 1]) j0 = j;
-  }
-  if (!inc) return false;
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-    out[c] = 0.0f;
-    dout[c] = 0.0f;
-  }
-  if (j0 < 0) return true;
-  float nb[KO + 1], nd[KO + 1];
-  nb[0] = 1.0f;
-  nd[0] = 0.0f;
-#pragma unroll
-  for (int k = 1; k <= KO; ++k) {
-    float nn[KO + 1], nnd[KO + 1];
-#pragma unroll
-    for (int m = 0; m <= k; ++m) {
-      const int j = j0 - k + m;
-      float v = 0.0f, dv = 0.0f;
-      if (j >= 0 && j <= NK - 2 - k) {
-        if (m >= 1) {  // (x - g[j]) / (g[j+k] - g[j]) * b_{k-1}[j]
-          const float il = __frcp_rn(g[j + k] - g[j]);
-          const float l = (x - g[j]) * il;
-          v = l * nb[m - 1];
-          dv = il * nb[m - 1] + l * nd[m - 1];
-        }
-        if (m <= k - 1) {  // (g[j+k+1] - x) / (g[j+k+1] - g[j+1]) * b_{k-1}[j+1]
-          const float ir = __frcp_rn(g[j + k + 1] - g[j + 1]);
-          const float r = (g[j + k + 1] - x) * ir;
-          v += r * nb[m];
-          dv += r * nd[m] - ir * nb[m];
-        }
-      }
-      nn[m] = v;
-      nnd[m] = dv;
-    }
-#pragma unroll
-    for (int m = 0; m <= k; ++m) {
-      nb[m] = nn[m];
-      nd[m] = nnd[m];
-    }
-  }
-#pragma unroll
-  for (int m = 0; m <= KO; ++m) {
-    const int j = j0 - KO + m;
-#pragma unroll
-    for (int c = 0; c < C; ++c)
-      if (c == j) {
-        out[c] = nb[m];
-        dout[c] = nd[m];
-      }
-  }
-  return true;
-}
-
-// grad_x[b, i] from grad_A [B, I(1+C)]: a thread per (b, i), i fastest.  NK, KO as at_split_kernel.
+// grad_x[b, i] from grad_A [B, I(1+C)]: a thread per input i (i fastest across the CTA) and
+// kGradRows batch rows, so each input's knots and reciprocals are set up once.  NK, KO as
+// at_split_kernel.
+constexpr int kGradRows = 8;
 template <int NK, int KO>
 __global__ void __launch_bounds__(kGradThreads) grad_x_kernel(const float* __restrict__ x,
                                                               const float* __restrict__ grid,
                                                               const float* __restrict__ ga, int64_t B, int I, int C,
                                                               int K, float* __restrict__ gx) {
   pdl_begin();
-  const int64_t q = int64_t(blockIdx.x) * kGradThreads + threadIdx.x;
-  if (q >= B * I) return;
-  const int64_t b = q / I;
-  const int i = int(q - b * I);
+  const int i = blockIdx.x * kGradThreads + threadIdx.x;
+  if (i >= I) return;
   const int nk = C + K + 1;
-  const float xv = x[q];
-  const float s = 1.0f / (1.0f + expf(-xv));
-  const float dsilu = s * (1.0f + xv * (1.0f - s));
   const int64_t nkp = int64_t(I) * (1 + C);
-  const float* row = ga + b * nkp + i;
-  float acc = row[0] * dsilu;
+  constexpr int NKr = NK > 0 ? NK : 2, KOr = KO > 0 ? KO : 1;
+  float gr[NKr], rk[KOr][NKr];
+  float g[NK > 0 ? 1 : kMaxKnots];
   if (NK > 0) {
-    float bs[NK > 0 ? NK : 1], dbs[NK > 0 ? NK : 1];
-    if (!bases_dual_local<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs, dbs))
-      bases_dual_fixed<(NK > 0 ? NK : 2), KO>(xv, grid + int64_t(i) * nk, bs, dbs);
-#pragma unroll
-    for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
+    load_knots<NKr, KOr>(grid + int64_t(i) * nk, gr, rk);
   } else {
-    float g[kMaxKnots], bs[kMaxKnots], dbs[kMaxKnots];
     for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
-    bases_dual(xv, g, nk, K, bs, dbs);
-    for (int c = 0; c < C; ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
   }
-  gx[q] = acc;
+  const int64_t b0 = int64_t(blockIdx.y) * kGradRows;
+  for (int r = 0; r < kGradRows; ++r) {
+    const int64_t b = b0 + r;
+    if (b >= B) break;
+    const float xv = x[b * I + i];
+    const float s = 1.0f / (1.0f + expf(-xv));
+    const float dsilu = s * (1.0f + xv * (1.0f - s));
+    const float* row = ga + b * nkp + i;
+    float acc = row[0] * dsilu;
+    if (NK > 0) {
+      float bs[NKr], dbs[NKr];
+      bases_recip<NKr, KOr, true>(xv, gr, rk, bs, dbs);
+#pragma unroll
+      for (int c = 0; c < NKr - KOr - 1; ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
+    } else {
+      float bs[kMaxKnots], dbs[kMaxKnots];
+      bases_dual(xv, g, nk, K, bs, dbs);
+      for (int c = 0; c < C; ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
+    }
+    gx[b * I + i] = acc;
+  }
 }
 
 // Weight gradients from grad_W [O, I(1+C)]: a thread per (o, i), i fastest.
@@ -494,8 +449,10 @@ inline int backward(const float* x, const float* grid, const float* wb, const fl
     st = gemm(half_at(L.g_hi), half_at(L.g_lo), B, half_at(L.wt_hi), half_at(L.wt_lo), int(nkp), op, float_at(L.rg),
               float_at(L.cwt), float_at(L.grad_a), stream);
     if (st != kOk) return st;
-    st = launch_pdl(gx_kern, unsigned((int64_t(B) * I + kGradThreads - 1) / kGradThreads), kGradThreads, 0, stream, x,
-                    grid, static_cast<const float*>(float_at(L.grad_a)), int64_t(B), I, C, K, grad_x);
+    st = launch_pdl(gx_kern, dim3(unsigned((I + kGradThreads - 1) / kGradThreads),
+                                  unsigned((int64_t(B) + kGradRows - 1) / kGradRows)),
+                    kGradThreads, 0, stream, x, grid, static_cast<const float*>(float_at(L.grad_a)), int64_t(B), I, C,
+                    K, grad_x);
     if (st != kOk) return st;
   }
   if (need_w) {
