@@ -66,3 +66,9 @@ def ppo(ops, cur, old, adv, clip_epsilon, n_total, entropy=None, group=None):
     parts = ops.ppo_partials(cur, old, adv, clip_epsilon, entropy)
     rows = gather_rows(parts, shard_chunks(n_total, chunk, world), group)
     return ops.ppo_finish(rows, n_total, entropy is not None)
+
+
+def time_range(T, world, rank):
+    """[t0, t1) steps of every row that `rank` holds when rows are sharded over time (contiguous,
+    split as evenly as possible; every rank gets at least one step when T >= world)."""
+    return (T * rank) // world, (T * (rank + 1)) // world

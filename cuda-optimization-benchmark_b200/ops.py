@@ -254,9 +254,9 @@ def reward_to_go_time_sharded(reward, done, gamma, group=None, out=None):
     import torch.distributed as dist
     maps = reward_to_go_slice_maps(reward, done, gamma)
     world = dist.get_world_size(group)
-    all_maps = torch.empty((world,) + tuple(maps.shape), dtype=maps.dtype, device=maps.device)
+    all_maps = torch.empty((world * maps.shape[0], 2), dtype=maps.dtype, device=maps.device)  # rank-major
     dist.all_gather_into_tensor(all_maps, maps, group=group)
-    return reward_to_go_slice_scan(reward, done, gamma, all_maps, dist.get_rank(group), out=out)
+    return reward_to_go_slice_scan(reward, done, gamma, all_maps.view(world, -1, 2), dist.get_rank(group), out=out)
 
 
 # ---------------------------------------------------------------------------- fused RL loss step
