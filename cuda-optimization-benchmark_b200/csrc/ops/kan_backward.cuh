@@ -235,7 +235,12 @@ __device__ __forceinline__ void bases_recip(float x, const float (&g)[NK], const
   }
 }
 
-// A transposed into planes [I(1+C), kp = pad64(B)]: a tile of 32 inputs x 32 batch rows; each
+__host__ __device__ constexpr int at_tile_rows(int nk) { return nk > 0 ? 64 : kTile; }
+inline size_t at_tile_smem(int C, int nk) {
+  return size_t(1 + C) * kTile * (at_tile_rows(nk) + 1) * sizeof(float);
+}
+
+// A transposed into planes [I(1+C), kp = pad64(B)]: a tile of 32 inputs x 32 (or 64) batch rows; each
 // thread evaluates silu and the bases of one x (the forward's recurrence) into shared memory.
 // Plane rows p = 0 take the factor of the input's max |x| over the batch (|silu(x)| <= |x|); bases
 // lie in [0, 1].  Only the K + 1 bases that can be non-zero are formed (kan::bases_local).
@@ -248,32 +253,35 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
                                                                      __half* __restrict__ hi, __half* __restrict__ lo,
                                                                      float* __restrict__ unscale) {
   pdl_begin();
-  extern __shared__ float s_t[];  // [1 + C][kTile][kTile + 1]
+  // The cubic forms take 64 batch rows per tile (each input's reciprocals serve 8 rows per thread;
+  // plane rows are written as half2 pairs, 128 bytes per warp); the general form 32.
+  constexpr int kW = at_tile_rows(NK);
+  extern __shared__ float s_t[];  // [1 + C][kTile][kW + 1]
   const int tx = threadIdx.x, ty = threadIdx.y;
-  const int i0 = blockIdx.x * kTile, b0 = blockIdx.y * kTile;
+  const int i0 = blockIdx.x * kTile, b0 = blockIdx.y * kW;
   const int i = i0 + tx;
   const int nk = C + K + 1;
   constexpr int NKr = NK > 0 ? NK : 2, KOr = KO > 0 ? KO : 1;
   float gr[NKr], rk[KOr][NKr];
   if (NK > 0 && i < I) load_knots<NKr, KOr>(grid + int64_t(i) * nk, gr, rk);
-  for (int y = ty; y < kTile; y += kTileRows) {
+  for (int y = ty; y < kW; y += kTileRows) {
     const int b = b0 + y;
     const bool ok = i < I && b < B;
     const float xv = ok ? x[int64_t(b) * I + i] : 0.0f;
-    s_t[(0 * kTile + tx) * (kTile + 1) + y] = ok ? kan::silu(xv) : 0.0f;
+    s_t[(0 * kTile + tx) * (kW + 1) + y] = ok ? kan::silu(xv) : 0.0f;
     if (NK > 0) {
       float bs[NKr];
       if (ok) bases_recip<NKr, KOr, false>(xv, gr, rk, bs, nullptr);
 #pragma unroll
       for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c)
-        s_t[((1 + c) * kTile + tx) * (kTile + 1) + y] = ok ? bs[c] : 0.0f;
+        s_t[((1 + c) * kTile + tx) * (kW + 1) + y] = ok ? bs[c] : 0.0f;
     } else {
       float g[kMaxKnots], bs[kMaxKnots];
       if (ok) {
         for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
         kan::bases_of(xv, g, nk, K, bs);
       }
-      for (int c = 0; c < C; ++c) s_t[((1 + c) * kTile + tx) * (kTile + 1) + y] = ok ? bs[c] : 0.0f;
+      for (int c = 0; c < C; ++c) s_t[((1 + c) * kTile + tx) * (kW + 1) + y] = ok ? bs[c] : 0.0f;
     }
   }
   __syncthreads();
@@ -284,8 +292,14 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
     const int64_t kr = int64_t(p) * I + i0 + ii;
     const float f = p == 0 ? kan::fp16_row_factor(__uint_as_float(amax_x[i0 + ii])) : 1.0f;
     if (blockIdx.y == 0 && tx == 0) unscale[kr] = 1.0f / f;
-    const int64_t b = b0 + tx;
-    if (b < kp) kan::split_store(s_t[(p * kTile + ii) * (kTile + 1) + tx] * f, hi + kr * kp + b, lo + kr * kp + b);
+    const float* srow = s_t + (p * kTile + ii) * (kW + 1);
+    if (kW == 64) {  // b0 + 64 <= kp (kp is a multiple of 64)
+      const int64_t b = b0 + 2 * tx;
+      kan::split_store2(srow[2 * tx] * f, srow[2 * tx + 1] * f, hi + kr * kp + b, lo + kr * kp + b);
+    } else {
+      const int64_t b = b0 + tx;
+      if (b < kp) kan::split_store(srow[tx] * f, hi + kr * kp + b, lo + kr * kp + b);
+    }
   }
 }
 
@@ -431,7 +445,9 @@ inline int backward(const float* x, const float* grid, const float* wb, const fl
   const int form = K == 3 && G == 5 ? 1 : (K == 3 && G == 8 ? 2 : 0);
   auto at_kern = form == 1 ? at_split_kernel<12, 3> : (form == 2 ? at_split_kernel<15, 3> : at_split_kernel<0, 0>);
   auto gx_kern = form == 1 ? grad_x_kernel<12, 3> : (form == 2 ? grad_x_kernel<15, 3> : grad_x_kernel<0, 0>);
-  if (!ensure_dyn_smem(wt_split_kernel, int(tsm)) || !ensure_dyn_smem(at_kern, int(tsm))) return kCudaError;
+  const int at_nk = form == 1 ? 12 : (form == 2 ? 15 : 0);
+  const size_t at_sm = at_tile_smem(C, at_nk);
+  if (!ensure_dyn_smem(wt_split_kernel, int(tsm)) || !ensure_dyn_smem(at_kern, int(at_sm))) return kCudaError;
   const dim3 tb(kTile, kTileRows);
   int st = kOk;
   if (need_x) {
@@ -469,7 +485,7 @@ inline int backward(const float* x, const float* grid, const float* wb, const fl
     st = launch_pdl(colmax_kernel, dim3(unsigned((I + kColThreads - 1) / kColThreads), chunks), kColThreads, 0,
                     stream, x, int64_t(B), I, u32_at(L.amax_x));
     if (st != kOk) return st;
-    st = launch_pdl(at_kern, dim3(unsigned((I + kTile - 1) / kTile), unsigned(bp / kTile)), tb, tsm, stream,
+    st = launch_pdl(at_kern, dim3(unsigned((I + kTile - 1) / kTile), unsigned(bp / at_tile_rows(at_nk))), tb, at_sm, stream,
                     x, grid, B, I, C, K, bp, static_cast<const uint32_t*>(u32_at(L.amax_x)), half_at(L.at_hi),
                     half_at(L.at_lo), float_at(L.cat));
     if (st != kOk) return st;
