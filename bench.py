@@ -9,8 +9,17 @@ in one launch of the fused kernel (b200_rl_step_async).  `value` is samples (tra
 per second over all GPUs, inputs resident in HBM; the per-op microseconds and roofline fractions
 that BASELINE.json's metric names are reported beside it (the two ops also timed as separate
 launches).  With N > 1 each rank processes its own batch (weak scaling) and the PPO reduction is
-global: the fused shard launch writes per-chunk partials, the ranks exchange them with one NCCL
-all-gather and all finish identically.
+global: each rank's step kernel stores its PPO totals into every peer's buffer over NVLink (CUDA
+IPC peer memory) and adds all ranks' totals in rank order, so every rank writes the same outputs;
+where CUDA IPC cannot be set up, the shard kernel's chunk partials are all-gathered with NCCL and
+finished on every rank instead.  After the timed steps the N > 1 results are checked on the same
+box (`parity`: bitwise across ranks, against the finish over the gathered partials, returns
+against the one-op entry); a failed check exits non-zero.  `exchange_us` is the step with no
+samples (the exchange alone at N > 1, the step's fixed cost at N = 1).
+
+`ops_sharded`: robust-L1, LIF, KAN and FP8 at their BASELINE sizes split over the N ranks (strong
+scaling: element ranges with an NCCL all-gather of chunk partials; batch rows; batch rows; rows of
+M with W replicated), each checked against the same op run whole on one GPU.
 
 Timing: W untimed warm-up steps, then exactly K steps between barriers and device syncs, timed
 with CUDA events on the launching stream, max over ranks.  Each step reads a different one of
@@ -40,6 +49,7 @@ B, T = 4096, 1000
 N_SAMPLES = B * T
 ROTATE = 4
 READY = 1  # B200_STEP_INPUTS_READY (include/b200ops.h)
+REPEAT_BATCHES = 10  # extra timed batches of K steps after the headline region (run-to-run spread)
 # Algorithmic bytes per call (reads + writes of each op's inputs and outputs).
 RTG_BYTES = (4 + 1 + 4) * N_SAMPLES                 # reward f32 + done u8 -> output f32
 PPO_BYTES = 16 * N_SAMPLES + 7 * 4                  # cur, old, adv, entropy f32 -> 7 f32
@@ -189,6 +199,14 @@ def profiled_traffic(kernel):
     return int(m.group(1)) if m else None
 
 
+def workload_config(world):
+    """The workload both arms run (identical dicts, so the two JSON lines name the same config)."""
+    return {"workload": "rl_pipeline: reward_to_go + ppo_clip_ext", "B": B, "T": T, "H": 1,
+            "samples_per_gpu": N_SAMPLES, "gamma": 0.99, "done_p": 0.01, "clip_epsilon": 0.2,
+            "parallelism": f"dp{world}: one batch per rank, PPO outputs over all ranks' samples"
+            if world > 1 else "1 GPU"}
+
+
 def make_sets(dev, rank, n_sets):
     from oracle import inputs  # seeded synthetic inputs of BASELINE.json configs[1]
     sets = []
@@ -334,6 +352,23 @@ def run_b200(args, world, rank, local):
     if status[0] != 0:
         raise RuntimeError(f"rl_step returned status {status[0]}")
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+
+    # Run-to-run spread of the same measurement: REPEAT_BATCHES more batches of K steps, each timed
+    # on its own between synchronizes (the region above stays the headline).
+    batch_us = []
+    for _ in range(REPEAT_BATCHES):
+        barrier(world)
+        batch_us.append(max_over_ranks(loop_ms(step, args.steps), world) * 1e3)
+    if status[0] != 0:
+        raise RuntimeError(f"rl_step returned status {status[0]}")
+
+    parity = None
+    exchange_us = None
+    if world > 1:
+        parity = multi_gpu_parity(ops, lib, dev, stream, world, sets, step, rtg_out, ppo_out, status)
+        exchange_us = zero_work_step_us(lib, dev, stream, world, sets, ws, exchange, args, status, loop_ms)
+    else:
+        exchange_us = zero_work_step_us(lib, dev, stream, world, sets, ws, None, args, status, loop_ms)
     del step_graphs  # graphs holding NCCL work are released before the process group is destroyed
 
     # Average duration of the fused kernel alone (the roofline's kernel): at N = 1 the timed step is
@@ -501,9 +536,18 @@ def run_b200(args, world, rank, local):
     barrier(world)
     e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps, world)
 
-    extra = {}
+    extra, sharded, cpu_ops = {}, None, None
     if not args.no_ops:
         extra = other_ops(ops, dev, world, rank)
+        sharded = sharded_ops(ops, lib, dev, world, rank)
+        # The E4M3 peak is measured last: its 1.5 s sustained loop heats the part and runs into the
+        # power cap, which would slow whatever were timed right after it.
+        fp8_fractions(extra, dev)
+        if rank == 0 and world == 1 and not args.no_cpu:
+            cpu_ops = cpu_op_baselines()
+            for name, cb in cpu_ops.items():
+                if name in extra:
+                    extra[name]["cpu_baseline"] = cb
 
     peak, peak_kind = peaks()
     step_bytes = RTG_BYTES + PPO_BYTES
@@ -525,16 +569,24 @@ def run_b200(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded; BASELINE.json configs[1] distributions)",
-        "config": {"workload": "rl_pipeline: reward_to_go + ppo_clip_ext", "B": B, "T": T, "H": 1,
-                   "samples_per_gpu": N_SAMPLES, "gamma": 0.99, "done_p": 0.01, "clip_epsilon": 0.2,
-                   "launch": "programmatic dependent launch; back-to-back steps over resident batches declare "
-                             "their inputs ready (B200_STEP_INPUTS_READY)",
-                   "l2": f"rotating {ROTATE} input sets of {(RTG_BYTES - 4 * N_SAMPLES + PPO_BYTES) / 1e6:.0f} MB "
-                         f"(> 126 MB L2)",
-                   "parallelism": (f"dp{world}: one batch per rank; PPO chunk partials exchanged over NVLink "
-                                   f"peer memory inside the fused kernel" if exchange is not None else
-                                   f"dp{world}: one batch per rank, PPO chunk partials all-gathered (NCCL); "
-                                   f"each step replayed from a CUDA graph") if world > 1 else "1 GPU"},
+        "config": workload_config(world),
+        "launch": "programmatic dependent launch; back-to-back steps over resident batches declare their inputs "
+                  "ready (B200_STEP_INPUTS_READY)",
+        "l2": f"rotating {ROTATE} input sets of {(RTG_BYTES - 4 * N_SAMPLES + PPO_BYTES) / 1e6:.0f} MB (> 126 MB L2)",
+        "exchange": (("PPO totals exchanged over NVLink peer memory inside the fused kernel" if exchange is not None
+                      else "PPO chunk partials all-gathered (NCCL); each step replayed from a CUDA graph")
+                     if world > 1 else None),
+        "repeat_batches": {"n": len(batch_us), "steps_each": args.steps,
+                           "median_us_per_step": statistics.median(batch_us),
+                           "min_us_per_step": min(batch_us), "max_us_per_step": max(batch_us),
+                           "spread": max(batch_us) / min(batch_us) - 1.0,
+                           "how": "after the headline region, batches of K steps each timed alone between device "
+                                  "synchronizes (max over ranks)"},
+        "exchange_us": exchange_us,
+        "exchange_us_note": ("the step with no samples (B = T = n = 0): at N > 1 one launch whose finishing CTA "
+                             "stores this rank's totals to every peer and waits for every peer's; at N = 1 the "
+                             "launch, election and finish alone"),
+        "parity": parity,
         "per_op": {
             "rl_step (fused)": {"us": fused_ms * 1e3, "bytes": step_bytes,
                                 "gbs": achieved, "frac_of_hbm": achieved / peak},
@@ -574,6 +626,11 @@ def run_b200(args, world, rank, local):
     }
     if extra:
         line["ops"] = extra
+    if sharded:
+        line["ops_sharded"] = sharded
+    if cpu_ops:
+        for name in ("reward_to_go", "ppo_clip_ext"):
+            line["per_op"][name]["cpu_baseline"] = cpu_ops[name]
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args)
     if exchange is not None:
@@ -582,6 +639,89 @@ def run_b200(args, world, rank, local):
         exchange.close()
         barrier(world)
     return line
+
+
+def multi_gpu_parity(ops, lib, dev, stream, world, sets, step, rtg_out, ppo_out, status):
+    """Correctness of the N > 1 step on the box that times it.  One more step on input set 0, then:
+    (a) every rank's 7 PPO outputs are the same bits (all-gathered and compared with rank 0's);
+    (b) they meet, at the ppo_clip tolerance, the library's fixed-order finish over all ranks'
+        chunk partials of the same batches, gathered with NCCL (the single-GPU semantics of
+        reference/ppo_clip/solution.cu:66-74,112-161 over the concatenated samples);
+    (c) each rank's returns are the bits of the one-op reward_to_go entry on its own batch.
+    Every rank computes the verdict; a failure raises on every rank (exit status 1), never a hang."""
+    import torch.distributed as dist
+    step(0)
+    torch.cuda.synchronize(dev)
+    mine = ppo_out.clone()
+    rtg_step = rtg_out.clone()
+    s = sets[0]
+    parts = ops.ppo_partials(s["current_log_prob"], s["old_log_prob"], s["advantage"], s["clip_epsilon"],
+                             s["entropy"])
+    allp = torch.empty((world * parts.shape[0], parts.shape[1]), dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(allp, parts)
+    ref = ops.ppo_finish(allp, world * N_SAMPLES, True)
+    outs = torch.empty((world, 7), dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(outs, mine)
+    rtg_single = ops.reward_to_go(s["reward"], s["done"], s["gamma"])
+    torch.cuda.synchronize(dev)
+    if status[0] != 0:
+        raise RuntimeError(f"rl_step returned status {status[0]}")
+    bits = outs.view(torch.int32)
+    identical = bool((bits == bits[0:1]).all())
+    atol, rtol = 1e-5, 1e-4  # tasks/ppo_clip/tests/task.json tolerance
+    diff = (mine.double() - ref.double()).abs()
+    within = bool((diff <= atol + rtol * ref.double().abs()).all())
+    same_bits_as_finish = bool(torch.equal(mine.view(torch.int32), ref.view(torch.int32)))
+    rtg_same = bool(torch.equal(rtg_step.view(torch.int32), rtg_single.view(torch.int32)))
+    ok = torch.tensor([int(identical and within and rtg_same)], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    res = {"ranks_identical": identical, "vs_gathered_finish": within,
+           "vs_gathered_finish_bit_identical": same_bits_as_finish,
+           "vs_gathered_finish_max_abs_diff": float(diff.max()),
+           "rtg_matches_single_op_bits": rtg_same, "all_ranks_ok": bool(int(ok.item()) == 1),
+           "tolerance": {"atol": atol, "rtol": rtol},
+           "how": "one exchange step on input set 0 after the timed steps: the 7 outputs all-gathered and "
+                  "compared bitwise across ranks; against b200_ppo_finish over the NCCL-gathered chunk partials "
+                  "of every rank's batch; returns against b200_reward_to_go_async on the rank's own batch"}
+    if not res["all_ranks_ok"]:
+        raise RuntimeError(f"multi-GPU parity failed: {res}")
+    return res
+
+
+def zero_work_step_us(lib, dev, stream, world, sets, ws, exchange, args, status, loop_ms):
+    """Device µs of the step with no samples: at N > 1 the exchange step alone (launch, the
+    finishing CTA's record stores to every peer over NVLink, the wait for every peer's record and
+    the rank-order sum); at N = 1 the one-GPU step's fixed cost (launch, election, finish).  The
+    compute part of a full step is the one-GPU step time; this is the part added per step."""
+    import ctypes
+    P = ctypes.c_void_p
+    cs = P(stream.cuda_stream)
+    s = sets[0]
+    tmp = torch.empty(7, device=dev)
+    base = (P(s["reward"].data_ptr()), P(s["done"].data_ptr()), s["gamma"], 0, 0, P(tmp.data_ptr()),
+            P(s["current_log_prob"].data_ptr()), P(s["old_log_prob"].data_ptr()), P(s["advantage"].data_ptr()),
+            P(s["entropy"].data_ptr()), 0, s["clip_epsilon"], P(tmp.data_ptr()), P(ws.data_ptr()), ws.numel())
+    if exchange is not None:
+        f = lib.b200_rl_step_exchange_async
+
+        def one(i):
+            exchange.epoch = lib.b200_peer_next_epoch(exchange.epoch)
+            status[0] |= f(*base, exchange.handle, exchange.epoch, READY, cs)
+    elif world == 1:
+        f = lib.b200_rl_step_ex_async
+
+        def one(i):
+            status[0] |= f(*base, READY, cs)
+    else:
+        return None
+    for i in range(args.warmup):
+        one(i)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    us = max_over_ranks(loop_ms(one, args.steps), world) * 1e3
+    if status[0] != 0:
+        raise RuntimeError(f"zero-work step returned status {status[0]}")
+    return us
 
 
 def other_ops(ops, dev, world, rank):
@@ -662,18 +802,28 @@ def other_ops(ops, dev, world, rank):
     del xs, m0, be, th, sp, fm, ck, gs, gx, gf, gm, gb, gt, wsb
 
     # GAE over the configs[1] batch: reward, value, next_value (f32), done, terminated (u8) in,
-    # advantage and value target (f32) out: 22 bytes per element of algorithmic traffic.
+    # advantage and value target (f32) out: 22 bytes per element of algorithmic traffic.  Two input
+    # sets (2 x 74 MB of inputs, 2 x 33 MB of outputs) alternate, so a call never finds its inputs
+    # in the 126 MB L2.
     s = inputs.baseline_inputs("rl_pipeline", seed=rank)
-    r = s["reward"].to(dev)
-    dn = s["done"].to(dev)
-    vv = torch.randn(r.shape, device=dev) * 0.5
-    nv = torch.roll(vv, -1, dims=1)
-    adv, tgt = torch.empty_like(r), torch.empty_like(r)
-    ms = timeit(lambda: ops.gae(r, vv, nv, dn, dn, 0.99, 0.95, advantage=adv, value_target=tgt))
-    nbytes = 22 * r.numel()
+    gsets = []
+    for k in range(2):
+        r = s["reward"].to(dev) if k == 0 else torch.roll(s["reward"].to(dev), 1, dims=0)
+        dn = s["done"].to(dev)
+        vv = torch.randn(r.shape, device=dev) * 0.5
+        nv = torch.roll(vv, -1, dims=1)
+        gsets.append((r, vv, nv, dn, torch.empty_like(r), torch.empty_like(r)))
+    it = [0]
+
+    def gae_call():
+        r, vv, nv, dn, adv, tgt = gsets[it[0] % 2]
+        it[0] += 1
+        ops.gae(r, vv, nv, dn, dn, 0.99, 0.95, advantage=adv, value_target=tgt)
+    ms = timeit(gae_call)
+    nbytes = 22 * s["reward"].numel()
     res["gae B4096 T1000"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
-                              "frac_of_hbm": nbytes / ms / 1e6 / peak}
-    del r, dn, vv, nv, adv, tgt
+                              "frac_of_hbm": nbytes / ms / 1e6 / peak, "l2": "2 alternating input sets (213 MB)"}
+    del gsets, s
 
     # Long rows (T >> B): 8 rows of 2^21 steps (151 MB of reward and done flags), the one-warp-per-
     # row scan against the chunked one (a warp per 1056-step chunk).  9 algorithmic bytes per step.
@@ -718,22 +868,37 @@ def other_ops(ops, dev, world, rank):
                                      "frac_of_bf16_sustained_issued": 6 * flops / ms / 1e9 / bf16_sus}
     del t, kout, gy
     # FP8 at the four BASELINE shapes; inputs drawn on the device (the values do not change the
-    # timing; parity is tested on the oracle's own inputs).
+    # timing; parity is tested on the oracle's own inputs).  Where one call's operands and output
+    # fit in L2 (M = 16: 17 MB, M = 1024: 29 MB) the calls rotate over copies whose total exceeds it,
+    # so the W stream comes from HBM.  Fractions are of the E4M3 dense peak measured on this GPU
+    # (torch._scaled_mm, i.e. cuBLASLt, at 8192^3: best of 10 and sustained over 1.5 s).
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    fp8_rows = []
     for M, N, K in inputs.BASELINE_SHAPES["fp8_linear"]:
-        x8, w8 = (torch.randn(r, K, device=dev, generator=g).clamp_(-448, 448).to(torch.float8_e4m3fn)
-                  for r in (M, N))
-        bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        yout = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-        ms = timeit(lambda: ops.fp8_linear(x8, 1.0, w8, 1.0, bias, out=yout), reps=10 if M * N * K > 1 << 36 else 50)
+        one = M * K + N * K + 2 * N + 2 * M * N
+        copies = 1 if one > (128 << 20) else (200 << 20) // one + 1
+        sets8 = []
+        for _ in range(copies):
+            x8, w8 = (torch.randn(r, K, device=dev, generator=g).clamp_(-448, 448).to(torch.float8_e4m3fn)
+                      for r in (M, N))
+            bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            sets8.append((x8, w8, bias, torch.empty((M, N), dtype=torch.bfloat16, device=dev)))
+        it = [0]
+
+        def fp8_call():
+            x8, w8, bias, yout = sets8[it[0] % copies]
+            it[0] += 1
+            ops.fp8_linear(x8, 1.0, w8, 1.0, bias, out=yout)
+        ms = timeit(fp8_call, reps=10 if M * N * K > 1 << 36 else max(50, 2 * copies))
+        fp8_rows.append((M, N, K, one, copies, ms))
+        del sets8
+    for M, N, K, one, copies, ms in fp8_rows:
         flops = 2 * M * N * K
-        nbytes = M * K + N * K + 2 * N + 2 * M * N
         res[f"fp8_linear M{M} N{N} K{K}"] = {
-            "us": ms * 1e3, "tflops": flops / ms / 1e9, "frac_of_fp8_peak": flops / ms / 1e9 / (2 * bf16_peak),
-            "frac_of_fp8_sustained": flops / ms / 1e9 / (2 * bf16_sus),
-            "gbs": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / peak,
-            "bound": "hbm" if flops / nbytes < 2 * bf16_peak * 1e3 / peak else "fp8 tensor"}
-        del x8, w8, bias, yout
+            "us": ms * 1e3, "tflops": flops / ms / 1e9, "flops": flops, "bytes": one,
+            "gbs": one / ms / 1e6, "frac_of_hbm": one / ms / 1e6 / peak,
+            "l2": (f"{copies} rotating operand sets ({copies * one / 1e6:.0f} MB)" if copies > 1
+                   else f"one operand set of {one / 1e6:.0f} MB (> L2)")}
     # E4M3 quantisation of the largest BASELINE activation (bf16 16384 x 8192): a per-tensor amax
     # needs every value before the first byte can be written, so the op reads x twice (the second
     # pass partly from L2) and writes one byte per value; those 5 bytes per value are its traffic.
@@ -749,6 +914,249 @@ def other_ops(ops, dev, world, rank):
     return res
 
 
+def graph_ms(fn, dev, world, reps):
+    """Device ms per call of `fn` on every rank, max over ranks: `reps` calls captured in one CUDA
+    graph (collectives included, captured in the same order on every rank), replayed once between
+    events after a warm replay, so the host cost of a call stays out of the number."""
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):  # warm-up on the capture stream: its scratch exists before capture
+        for _ in range(3):
+            fn()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / reps
+    del g  # graphs holding NCCL work are released before the process group is destroyed
+    return max_over_ranks(ms, world)
+
+
+def sharded_ops(ops, lib, dev, world, rank):
+    """robust-L1, LIF, KAN and FP8 at their BASELINE sizes split over the ranks (strong scaling),
+    each rank holding only its shard in its own tensors, against the same op run whole on one GPU.
+
+    - robust-L1 2^26: contiguous chunk-aligned element ranges; each rank writes one fp64 partial per
+      8192-element chunk, the ranks all-gather the partials (NCCL, rank order = chunk order) and
+      every rank runs the same fixed-order finish: the result must be the bits of the one-GPU call.
+    - LIF [256, 64, 4096]: batch rows split (neurons are independent): spikes and final membrane
+      must be the bits of the one-GPU call's rows.
+    - KAN B8192 I1024 O1024 G5: batch rows split, weights replicated (each rank prepares its own
+      weight planes): within the task tolerance of the one-GPU call's rows.
+    - FP8 8192^3 and 16384 x 28672 x 8192: rows of M split, W and bias replicated: within the task
+      tolerance of the one-GPU call's rows.  (M = 16 does not shard: its cost is the W stream, which
+      every rank would read whole.)
+    Every rank draws the same full inputs from the same seed, keeps its shard, and also runs the
+    whole op once for the check and for `us_whole_1gpu`.  Times: graph-replayed calls, max over
+    ranks; `speedup` = whole-op µs / sharded µs, `efficiency` = speedup / N.  A failed check raises
+    on every rank."""
+    import importlib as _il
+    pdist = _il.import_module("cuda-optimization-benchmark_b200.dist")
+    if world > 1:
+        import torch.distributed as dist
+    g = torch.Generator(device=dev).manual_seed(4321)  # the same full inputs on every rank
+    res, oks = {}, []
+
+    def entry(name, us, us_whole, checks, partition, extra=None):
+        sp = us_whole / us
+        e = {"n_gpus": world, "us": us, "us_whole_1gpu": us_whole, "speedup": sp, "efficiency": sp / world,
+             "partition": partition, "parity": checks}
+        if extra:
+            e.update(extra)
+        res[name] = e
+        oks.append(all(v for k, v in checks.items() if isinstance(v, bool)))
+
+    # robust-L1
+    n = 1 << 26
+    x = torch.randn(n, device=dev, generator=g)
+    y = torch.randn(n, device=dev, generator=g)
+    whole = ops.robust_l1(x, y).clone()
+    us_whole = graph_ms(lambda: ops.robust_l1(x, y), dev, 1, 20) * 1e3
+    chunk = lib.b200_robust_l1_chunk_elems()
+    counts = pdist.shard_chunks(n, chunk, world)
+    if len(set(counts)) != 1:
+        raise RuntimeError("robust-L1 shards must hold the same number of chunks")
+    lo, hi = pdist.shard_range(n, chunk, world, rank)
+    xs, ys = x[lo:hi].clone(), y[lo:hi].clone()
+    del x, y
+    parts = torch.empty(counts[rank], dtype=torch.float64, device=dev)
+    allp = torch.empty(sum(counts), dtype=torch.float64, device=dev) if world > 1 else parts
+    out = torch.empty((), device=dev)
+    import ctypes
+    P = ctypes.c_void_p
+
+    def shard_step():
+        cs = P(torch.cuda.current_stream(dev).cuda_stream)
+        lib.b200_robust_l1_shard_partials(P(xs.data_ptr()), P(ys.data_ptr()), hi - lo, P(parts.data_ptr()), cs)
+        if world > 1:
+            dist.all_gather_into_tensor(allp, parts)
+        lib.b200_robust_l1_finish(P(allp.data_ptr()), sum(counts), n, P(out.data_ptr()), cs)
+
+    def partials_only():
+        cs = P(torch.cuda.current_stream(dev).cuda_stream)
+        lib.b200_robust_l1_shard_partials(P(xs.data_ptr()), P(ys.data_ptr()), hi - lo, P(parts.data_ptr()), cs)
+    shard_step()
+    torch.cuda.synchronize(dev)
+    same = bool(torch.equal(out.view(torch.int32), whole.view(torch.int32)))
+    us = graph_ms(shard_step, dev, world, 20) * 1e3
+    us_part = graph_ms(partials_only, dev, world, 20) * 1e3
+    entry("robust_l1 2^26", us, us_whole, {"bit_identical_to_1gpu": same},
+          f"{counts[rank]} chunks of {chunk} elements per rank; chunk partials all-gathered "
+          + ("(NCCL, in the graph)" if world > 1 else "(one rank: none)"),
+          {"us_partials_kernel": us_part, "us_exchange_and_finish": us - us_part,
+           "bytes_per_rank": 8 * (hi - lo), "frac_of_hbm_partials": 8 * (hi - lo) / (us_part * 1e-6) / 1e9
+           / peaks()[0]})
+    del xs, ys, parts, allp
+
+    # LIF
+    T_, B_, H_ = 256, 64, 4096
+    xl = torch.randn(T_, B_, H_, device=dev, generator=g) * 0.5 + 0.3
+    m0 = torch.zeros(B_, H_, device=dev)
+    be, th = torch.full((H_,), 0.9, device=dev), torch.full((H_,), 1.0, device=dev)
+    sp_w, fm_w = ops.leaky(xl, m0, be, th)
+    us_whole = graph_ms(lambda: ops.leaky(xl, m0, be, th, spikes=sp_w, final_mem=fm_w), dev, 1, 10) * 1e3
+    b0, b1 = (B_ * rank) // world, (B_ * (rank + 1)) // world
+    xsl, m0s = xl[:, b0:b1].contiguous(), m0[b0:b1].contiguous()
+    del xl
+    sp_s, fm_s = ops.leaky(xsl, m0s, be, th)
+    torch.cuda.synchronize(dev)
+    same_sp = bool(torch.equal(sp_s, sp_w[:, b0:b1]))
+    same_fm = bool(torch.equal(fm_s.view(torch.int32), fm_w[b0:b1].view(torch.int32)))
+    del sp_w, fm_w
+    us = graph_ms(lambda: ops.leaky(xsl, m0s, be, th, spikes=sp_s, final_mem=fm_s), dev, world, 10) * 1e3
+    nb = 8 * xsl.numel() + 8 * m0s.numel() + 8 * H_
+    entry("leaky T256 B64 H4096", us, us_whole, {"spikes_bit_identical_to_1gpu": same_sp,
+                                                 "final_mem_bit_identical_to_1gpu": same_fm},
+          f"batch rows [{b0}, {b1}) of {B_} on this rank", {"frac_of_hbm": nb / (us * 1e-6) / 1e9 / peaks()[0]})
+    del xsl, m0s, sp_s, fm_s
+
+    # KAN
+    Bk, Ik, Ok, G, K = 8192, 1024, 1024, 5, 3
+    xk = torch.rand(Bk, Ik, device=dev, generator=g) * 2.0 - 1.0
+    knots = torch.arange(-K, G + K + 1, dtype=torch.float32, device=dev)
+    grid = (knots * (2.0 / G) - 1.0).expand(Ik, -1).contiguous()
+    std = 1.0 / Ik ** 0.5
+    bw = torch.randn(Ok, Ik, device=dev, generator=g) * std
+    sw = torch.randn(Ok, Ik, G + K, device=dev, generator=g) * std
+    sc = torch.ones(Ok, Ik, device=dev)
+    out_w = ops.efficient_kan(xk, grid, bw, sw, sc, G, K)
+    us_whole = graph_ms(lambda: ops.efficient_kan(xk, grid, bw, sw, sc, G, K, out=out_w), dev, 1, 5) * 1e3
+    b0, b1 = (Bk * rank) // world, (Bk * (rank + 1)) // world
+    xks = xk[b0:b1].contiguous()
+    del xk
+    out_s = ops.efficient_kan(xks, grid, bw, sw, sc, G, K)
+    torch.cuda.synchronize(dev)
+    ref = out_w[b0:b1].double()
+    ok_tol = bool(((out_s.double() - ref).abs() <= 1e-5 + 1e-5 * ref.abs()).all())
+    same = bool(torch.equal(out_s.view(torch.int32), out_w[b0:b1].view(torch.int32)))
+    del out_w, ref
+    us = graph_ms(lambda: ops.efficient_kan(xks, grid, bw, sw, sc, G, K, out=out_s), dev, world, 5) * 1e3
+    entry("efficient_kan B8192 I1024 O1024 G5", us, us_whole,
+          {"within_task_tolerance_of_1gpu": ok_tol, "bit_identical_to_1gpu": same},
+          f"batch rows [{b0}, {b1}) of {Bk} on this rank, weights replicated")
+    del xks, out_s, bw, sw, sc, grid
+
+    # FP8
+    for M, N, Kf in ((8192, 8192, 8192), (16384, 28672, 8192)):
+        x8 = torch.randn(M, Kf, device=dev, generator=g).to(torch.float8_e4m3fn)
+        w8 = torch.randn(N, Kf, device=dev, generator=g).to(torch.float8_e4m3fn)
+        bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        y_w = ops.fp8_linear(x8, 1.0, w8, 1.0, bias)
+        us_whole = graph_ms(lambda: ops.fp8_linear(x8, 1.0, w8, 1.0, bias, out=y_w), dev, 1, 5) * 1e3
+        m0_, m1_ = (M * rank) // world, (M * (rank + 1)) // world
+        xs8 = x8[m0_:m1_].contiguous()
+        del x8
+        y_s = ops.fp8_linear(xs8, 1.0, w8, 1.0, bias)
+        torch.cuda.synchronize(dev)
+        ref = y_w[m0_:m1_].float()
+        ok_tol = bool(((y_s.float() - ref).abs() <= 1e-2 + 1e-2 * ref.abs()).all())
+        same = bool(torch.equal(y_s.view(torch.int16), y_w[m0_:m1_].view(torch.int16)))
+        del y_w, ref
+        us = graph_ms(lambda: ops.fp8_linear(xs8, 1.0, w8, 1.0, bias, out=y_s), dev, world, 5) * 1e3
+        entry(f"fp8_linear M{M} N{N} K{Kf}", us, us_whole,
+              {"within_task_tolerance_of_1gpu": ok_tol, "bit_identical_to_1gpu": same},
+              f"rows [{m0_}, {m1_}) of M = {M} on this rank, W and bias replicated",
+              {"tflops_all_ranks": 2.0 * M * N * Kf / (us * 1e-6) / 1e12})
+        del xs8, w8, bias, y_s
+    torch.cuda.synchronize(dev)
+    ok = torch.tensor([int(all(oks))], device=dev)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if int(ok.item()) != 1:
+        raise RuntimeError(f"sharded-op parity failed: {res}")
+    res["note"] = ("strong scaling: the BASELINE size split over the N ranks; us = max over ranks of one sharded "
+                   "call (exchange included), us_whole_1gpu = the whole op on one GPU; fp8 M16 is replicas only")
+    return res
+
+
+_FP8_PEAK = {}
+
+
+def fp8_fractions(res, dev):
+    """Roofline fractions of the FP8 lines against the E4M3 peak measured on this GPU."""
+    fp8_peak, fp8_sus = fp8_peaks(dev)
+    hbm = peaks()[0]
+    for name, e in res.items():
+        if not name.startswith("fp8_linear M"):
+            continue
+        flops, one = e["flops"], e["bytes"]
+        e["frac_of_fp8_peak"] = e["tflops"] / fp8_peak
+        e["frac_of_fp8_sustained"] = e["tflops"] / fp8_sus
+        e["bound"] = "hbm" if flops / one < fp8_peak * 1e3 / hbm else "fp8 tensor"
+        e["fp8_peak_tflops"] = {"burst": fp8_peak, "sustained": fp8_sus,
+                                "source": "measured here after the timings: torch._scaled_mm (cuBLASLt) e4m3 "
+                                          "8192^3 -> bf16, best of 10 / mean over 1.5 s"}
+
+
+def fp8_peaks(dev):
+    """Dense E4M3 TFLOP/s of this GPU, measured with the vendor library (torch._scaled_mm, which
+    calls cuBLASLt) at 8192^3 into bf16: (best of 10 single calls, mean over 1.5 s back to back).
+    The roofline denominator of the FP8 GEMM, measured the way MEASURED_PEAKS.json measures bf16."""
+    if dev.index in _FP8_PEAK:
+        return _FP8_PEAK[dev.index]
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(7)
+    a = torch.randn(n, n, device=dev, generator=g).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev, generator=g).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=dev)
+
+    def mm():
+        torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    for _ in range(3):
+        mm()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = None
+    for _ in range(10):
+        e0.record()
+        mm()
+        e1.record()
+        e1.synchronize()
+        t = e0.elapsed_time(e1)
+        best = t if best is None else min(best, t)
+    flops = 2.0 * n ** 3
+    k = max(10, int(1500.0 / best))
+    e0.record()
+    for _ in range(k):
+        mm()
+    e1.record()
+    e1.synchronize()
+    sus = e0.elapsed_time(e1) / k
+    _FP8_PEAK[dev.index] = (flops / best / 1e9, flops / sus / 1e9)
+    del a, b
+    return _FP8_PEAK[dev.index]
+
+
 # -------------------------------------------------------------------------------- CPU baseline
 def cpu_step_fn():
     from oracle import eager, inputs
@@ -758,6 +1166,84 @@ def cpu_step_fn():
         eager.reward_to_go(s["reward"], s["done"], s["gamma"])
         eager.ppo_clip(s["current_log_prob"], s["old_log_prob"], s["advantage"], s["clip_epsilon"], s["entropy"])
     return run
+
+
+def cpu_op_baselines():
+    """CPU-eager µs of each op at its BASELINE size on this host's cores: oracle/eager.py, the
+    PyTorch-eager fp32 restatement of each task's reference() (tasks/<task>/reference.py), median of
+    3 after one warm-up.  KAN and the large FP8 shapes run on a row subset and are scaled to the
+    full batch linearly (each row's work is independent; the per-call weight preparation is then
+    counted once per subset, so the scaled figure is an upper bound of a whole call)."""
+    from oracle import eager
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(99)
+    res = {}
+
+    def med(fn, reps=3):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t)
+        return statistics.median(ts)
+
+    def put(name, sec, scale, sample):
+        res[name] = {"us": sec * scale * 1e6, "cores": cores, "kind": "port",
+                     "sample": sample, "sample_us": sec * 1e6, "scale": scale,
+                     "what": "oracle/eager.py (PyTorch-eager fp32 restatement of the reference's reference())"}
+
+    from oracle import inputs
+    r = inputs.baseline_inputs("rl_pipeline", seed=0)
+    put("reward_to_go", med(lambda: eager.reward_to_go(r["reward"], r["done"], r["gamma"])), 1, "full [4096, 1000]")
+    put("ppo_clip_ext", med(lambda: eager.ppo_clip(r["current_log_prob"], r["old_log_prob"], r["advantage"],
+                                                    r["clip_epsilon"], r["entropy"])), 1, "full 4,096,000 samples")
+    del r
+    x = torch.randn(1 << 26, generator=g)
+    y = torch.randn(1 << 26, generator=g)
+    put("robust_l1", med(lambda: eager.pow_abs_sqrt_mean(x, y)), 1, "full 2^26 elements")
+    del x, y
+    xl = torch.randn(256, 64, 4096, generator=g) * 0.5 + 0.3
+    m0 = torch.zeros(64, 4096)
+    be, th = torch.full((4096,), 0.9), torch.full((4096,), 1.0)
+    put("leaky", med(lambda: eager.leaky(xl, m0, be, th)), 1, "full [256, 64, 4096]")
+    del xl
+    def fitted(name, run, rows, full, reps=3):
+        """Two row counts r and 2r: time = fixed + per_row * rows, extrapolated to the full batch
+        (the per-call weight preparation is the fixed part, the rows' work the slope)."""
+        t1 = med(lambda: run(rows), reps)
+        t2 = med(lambda: run(2 * rows), reps)
+        per_row = max(t2 - t1, 0.0) / rows
+        fixed = max(t1 - per_row * rows, 0.0)
+        sec = fixed + per_row * full
+        res[name] = {"us": sec * 1e6, "cores": cores, "kind": "port",
+                     "sample": f"{rows} and {2 * rows} of {full} rows, extrapolated linearly in rows "
+                               f"(fixed {fixed * 1e3:.1f} ms + {per_row * 1e6:.1f} us per row)",
+                     "sample_us": [t1 * 1e6, t2 * 1e6],
+                     "what": "oracle/eager.py (PyTorch-eager fp32 restatement of the reference's reference())"}
+
+    Bk, I, O, G, K = 8192, 1024, 1024, 5, 3
+    xk = torch.rand(1024, I, generator=g) * 2 - 1
+    knots = torch.arange(-K, G + K + 1, dtype=torch.float32)
+    grid = (knots * (2.0 / G) - 1.0).expand(I, -1).contiguous()
+    bw = torch.randn(O, I, generator=g) / 32
+    sw = torch.randn(O, I, G + K, generator=g) / 32
+    sc = torch.ones(O, I)
+    fitted("efficient_kan", lambda r: eager.efficient_kan(xk[:r], grid, bw, sw, sc, K), 512, Bk)
+    del xk, bw, sw, sc
+    for (M, N, Kf), rows in (((16, 4096, 4096), 16), ((1024, 4096, 4096), 1024), ((8192, 8192, 8192), 256),
+                             ((16384, 28672, 8192), 64)):
+        xq = torch.randint(0, 0x7E, (min(M, 2 * rows), Kf), dtype=torch.uint8, generator=g).view(torch.float8_e4m3fn)
+        wq = torch.randint(0, 0x7E, (N, Kf), dtype=torch.uint8, generator=g).view(torch.float8_e4m3fn)
+        bias = torch.zeros(N, dtype=torch.bfloat16)
+        name = f"fp8_linear M{M} N{N} K{Kf}"
+        if rows == M:
+            put(name, med(lambda: eager.fp8_linear(xq, 2.0, wq, 2.0, bias)), 1, "full call")
+        else:
+            fitted(name, lambda r: eager.fp8_linear(xq[:r], 2.0, wq, 2.0, bias), rows, M, reps=2)
+        del xq, wq
+    return res
 
 
 def cpu_cores():
@@ -803,8 +1289,7 @@ def run_reference(args, world, rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; BASELINE.json configs[1] distributions)",
-            "config": {"workload": "rl_pipeline: reward_to_go + ppo_clip_ext", "B": B, "T": T, "H": 1,
-                       "samples_per_gpu": N_SAMPLES},
+            "config": workload_config(world),
             "cpu_baseline": {"value": v, "unit": "samples/s", "cores": cores, "kind": "port",
                              "sample": f"full configs[1] batch per step, {args.steps} steps after {args.warmup} "
                                        f"warm-up; PyTorch-eager fp32 restatement of the reference's reference()"},
@@ -817,7 +1302,7 @@ PROFILE_FP8 = {"fp8_m16": (16, 4096, 4096), "fp8_m1024": (1024, 4096, 4096), "fp
 
 def run_profile(ops_list, reps):
     """Run each listed op `reps` times at its BASELINE size on cuda:0 and print nothing but the
-    device fault word: the workload for `ncu` launch lists and captures (profiles/*.md)."""
+    device fault word: the workload for `ncu` launch lists and captures (profiles/*.txt)."""
     from oracle import inputs
     pkg = importlib.import_module("cuda-optimization-benchmark_b200")
     lib = pkg.load()
@@ -869,6 +1354,13 @@ def run_profile(ops_list, reps):
             lib.b200_efficient_kan_async(t["x"].data_ptr(), t["grid"].data_ptr(), t["base_weight"].data_ptr(),
                                          t["spline_weight"].data_ptr(), t["spline_scaler"].data_ptr(), 5, 3, s["B"],
                                          s["I"], s["O"], out.data_ptr(), ws.data_ptr(), nb, None)
+    if "kan_timed" in ops_list:  # the reference's timed case (tasks/efficient_kan/tests/task.json, G = 8)
+        s = inputs.task_inputs("efficient_kan", {"B": 4096, "I": 256, "O": 512}, 305)
+        t = {k: s[k].to(dev) for k in ["x", "grid", "base_weight", "spline_weight", "spline_scaler"]}
+        out = torch.empty(s["B"], s["O"], device=dev)
+        for _ in range(reps):
+            ops.efficient_kan(t["x"], t["grid"], t["base_weight"], t["spline_weight"], t["spline_scaler"], 8, 3,
+                              out=out)
     if "kan_backward" in ops_list:
         s = inputs.baseline_inputs("kan", 0)
         t = {k: s[k].to(dev) for k in ["x", "grid", "base_weight", "spline_weight", "spline_scaler"]}
@@ -897,7 +1389,8 @@ def main():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile", default=None,
-                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, lif_backward, robust_l1, kan, kan_backward, fp8_m16, fp8_m1024, "
+                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, lif_backward, robust_l1, kan, kan_timed, "
+                         "kan_backward, fp8_m16, fp8_m1024, "
                          "fp8_8192, "
                          "fp8_16384, fp8_ref_timed): run each --steps times for ncu, no timing")
     args = ap.parse_args()

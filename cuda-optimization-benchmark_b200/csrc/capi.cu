@@ -367,7 +367,9 @@ int b200_efficient_kan_backward_async(const float* x, const float* grid, const f
 // library holds the array until the process exits.  All calls on a device share it, so calls that
 // overlap on the GPU (different streams, no ordering) race on it; calls on one stream are safe.
 // The first call on each device looks up the array's device address (cudaGetSymbolAddress with
-// that device current) and caches it; make that first call before any stream capture begins.
+// that device current) and caches it with the context's id; make that first call before any
+// stream capture begins.  A later call in another context of the device (after cudaDeviceReset)
+// looks the address up again.
 // Each call clears the counter block on its stream before launching, so a call never depends on
 // what an earlier call left there; the partials are fully rewritten by every call.
 namespace {
@@ -381,9 +383,41 @@ constexpr size_t kNoAllocScratchBytes =
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
+// The unique id of the calling thread's current context (cuCtxGetCurrent + cuCtxGetId, fetched
+// through the runtime so the library needs no -lcuda link), or 0 when there is none yet.  Ids are
+// never reused within a process, so a context re-created after cudaDeviceReset has a new one.
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    looked_up = true;
+  }
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != 0 || ctx == nullptr) return 0;
+  return get_id(ctx, &id) == 0 ? id : 0;
+}
+
+// Device address of g_noalloc_scratch on the current device: looked up once per device and
+// context (cudaGetSymbolAddress with that device current), and looked up again when the device's
+// context has changed since (a primary context re-created after cudaDeviceReset may map the
+// library's module at another address).
 void* noalloc_scratch(int* status) {
   static void* addr[64] = {nullptr};
+  static unsigned long long ctx_id[64] = {0};
   static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
@@ -391,13 +425,15 @@ void* noalloc_scratch(int* status) {
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  const unsigned long long id = current_context_id();
+  if (addr[dev] == nullptr || id == 0 || id != ctx_id[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
       *status = b200::kCudaError;
       return nullptr;
     }
     addr[dev] = p;
+    ctx_id[dev] = current_context_id();  // the lookup has made the device's context current
   }
   *status = b200::kOk;
   return addr[dev];

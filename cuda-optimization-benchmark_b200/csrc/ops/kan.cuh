@@ -296,10 +296,19 @@ __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x
 // block of rows, with every basis step a multiply:
 //   row_scale_kernel: per row the power-of-two factor that keeps silu and the bases inside fp16
 //     (the same rule as prep_a_kernel), and the row's zero K padding;
-//   prep_a2_kernel: a thread owns two adjacent inputs (i, i + 1) and kPrepRows rows; it writes the
-//     hi / lo planes with 4-byte half2 stores (each warp a contiguous 128 bytes per plane).
+//   prep_a2_kernel: a thread owns two adjacent inputs (i, i + 1) and a block of up to kPrepRows
+//     rows; it writes the hi / lo planes with 4-byte half2 stores (each warp a contiguous 128 bytes
+//     per plane).  The rows per block shrink (prep_rows) until the grid has about three CTAs per SM,
+//     so narrow layers (few inputs) still fill the GPU.
 constexpr int kPrepRows = 32;
 constexpr int kPrepThreads = 128;
+
+inline int prep_rows(int B, int I) {
+  const int64_t xblocks = (I + 2 * kPrepThreads - 1) / (2 * kPrepThreads);
+  int rows = kPrepRows;
+  while (rows > 4 && xblocks * ((B + rows - 1) / rows) < 3 * int64_t(sm_count())) rows /= 2;
+  return rows;
+}
 
 // One warp per row.  The amax takes silu with fast intrinsics: the factor is a power of two chosen
 // with a 4x margin below the fp16 maximum (kFp16Safe), so an amax a few ulps low can at most double
@@ -343,13 +352,13 @@ __device__ __forceinline__ void split_store2(float v0, float v1, __half* hi, __h
                                                    __float2half_rn((v1 - __half2float(h1)) * kLoScale));
 }
 
-// grid = (ceil(I / (2 * kPrepThreads)), ceil(B / kPrepRows)); I even.  rs from row_scale_kernel.
+// grid = (ceil(I / (2 * kPrepThreads)), ceil(B / rows)); I even.  rs from row_scale_kernel.
 template <int NK, int KO>
 __global__ void __launch_bounds__(kPrepThreads) prep_a2_kernel(const float* __restrict__ x,
                                                                const float* __restrict__ grid, int B, int I,
                                                                int64_t kp, const float* __restrict__ rs,
                                                                __half* __restrict__ a_hi,
-                                                               __half* __restrict__ a_lo) {
+                                                               __half* __restrict__ a_lo, int rows) {
   pdl_begin();  // the row scales are written by row_scale_kernel just before this kernel
   constexpr int C = NK - KO - 1;
   const int i = 2 * (int(blockIdx.x) * kPrepThreads + int(threadIdx.x));
@@ -365,8 +374,8 @@ __global__ void __launch_bounds__(kPrepThreads) prep_a2_kernel(const float* __re
 #pragma unroll
       for (int j = 0; j + k < NK; ++j) rc[u][k - 1][j] = 1.0f / __fsub_rn(g[u][j + k], g[u][j]);
   }
-  const int b0 = int(blockIdx.y) * kPrepRows;
-  for (int bb = 0; bb < kPrepRows; ++bb) {
+  const int b0 = int(blockIdx.y) * rows;
+  for (int bb = 0; bb < rows; ++bb) {
     const int b = b0 + bb;
     if (b >= B) break;
     const float f = 1.0f / __ldg(rs + b);  // a power of two: exact
@@ -588,11 +597,12 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   if (K == 3 && (G == 5 || G == 8) && I % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) {
     launch_pdl(row_scale_kernel, unsigned((B + kScaleRowsPerCta - 1) / kScaleRowsPerCta), 32 * kScaleRowsPerCta, 0,
                stream, x, B, I, C, kp, rs, a_hi, a_lo);
-    const dim3 pg(unsigned((I + 2 * kPrepThreads - 1) / (2 * kPrepThreads)), unsigned((B + kPrepRows - 1) / kPrepRows));
+    const int rows = prep_rows(B, I);
+    const dim3 pg(unsigned((I + 2 * kPrepThreads - 1) / (2 * kPrepThreads)), unsigned((B + rows - 1) / rows));
     if (G == 5) launch_pdl(prep_a2_kernel<12, 3>, pg, kPrepThreads, 0, stream, x, grid, B, I, kp,
-                           static_cast<const float*>(rs), a_hi, a_lo);
+                           static_cast<const float*>(rs), a_hi, a_lo, rows);
     else launch_pdl(prep_a2_kernel<15, 3>, pg, kPrepThreads, 0, stream, x, grid, B, I, kp,
-                    static_cast<const float*>(rs), a_hi, a_lo);
+                    static_cast<const float*>(rs), a_hi, a_lo, rows);
   } else if (G == 5 && K == 3) {
     launch_pdl(prep_a_kernel<12, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
   } else if (G == 8 && K == 3) {

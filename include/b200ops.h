@@ -68,7 +68,8 @@ int b200_robust_l1_async(const float* inp, const float* target, int64_t n, float
  * 131,328-byte device array inside the library, held by every GPU that loads it until exit, so a
  * call may cover at most B200_NOALLOC_MAX_ELEMS elements (batch_size*4*height*width); larger calls
  * return B200_WORKSPACE_TOO_SMALL without launching.  The first call on a device looks up the
- * array's device address; make it before any stream capture begins.  All calls on a device share
+ * array's device address; make it before any stream capture begins (the lookup is repeated once
+ * when the device's context changes, e.g. after cudaDeviceReset).  All calls on a device share
  * the array: calls that overlap on the GPU race, calls ordered on one stream do not. */
 #define B200_NOALLOC_MAX_ELEMS 134217728LL
 int b200_pow_abs_sqrt_mean_noalloc(const float* inp, const float* target, int64_t batch_size, int64_t height,

@@ -15,6 +15,12 @@ tests/test_expert_gpu.py runs them on the same inputs as the B200 kernels: their
 the fp64 oracle pin the oracle to the reference's own GPU implementation, and their times, taken
 with the grader's timing rule, are the expert column beside the B200 kernels' times.
 
+The reference grader's call counter (graders/interpose.c, an LD_PRELOAD library that counts the
+CUDA runtime calls a graded call makes: allocations, host copies, device-wide synchronizations,
+launches, work off the caller's stream) is compiled the same way, with the grader's own command
+(graders/grade.py:256-262: gcc -O2 -shared -fPIC -I<cuda include> ... -ldl), into
+oracle/_ref/interpose.so; tests/test_call_counts_gpu.py preloads it around the drop-ins.
+
     python oracle/ref_build.py          # build every task (skips when the checkout is absent)
 """
 import importlib.util
@@ -75,6 +81,34 @@ def build_one(task, nvcc="nvcc", verbose=False):
     return lib
 
 
+def counter_library():
+    return OUT / "interpose.so"
+
+
+def build_counter(nvcc="nvcc", verbose=False):
+    """Compile graders/interpose.c from the reference checkout into oracle/_ref/interpose.so."""
+    src = REFERENCE / "graders" / "interpose.c"
+    if not src.exists():
+        raise FileNotFoundError(src)
+    OUT.mkdir(parents=True, exist_ok=True)
+    lib = counter_library()
+    if lib.exists() and lib.stat().st_mtime >= src.stat().st_mtime:
+        return lib
+    import shutil
+    nv = shutil.which(nvcc) or "/usr/local/cuda/bin/nvcc"
+    inc = Path(nv).resolve().parent.parent / "include"
+    cmd = [os.environ.get("CC", "gcc"), "-O2", "-shared", "-fPIC", f"-I{inc}", "-o", str(lib) + ".tmp", str(src),
+           "-ldl"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError(f"gcc failed building the reference's call counter (exit {r.returncode})")
+    os.replace(str(lib) + ".tmp", lib)
+    return lib
+
+
 def build(nvcc="nvcc", verbose=False):
     """Build every task's expert library when the reference checkout is present; returns the
     library paths (an empty list when it is absent)."""
@@ -82,7 +116,8 @@ def build(nvcc="nvcc", verbose=False):
         return []
     from concurrent.futures import ThreadPoolExecutor
     with ThreadPoolExecutor(max_workers=6) as ex:
-        return list(ex.map(lambda t: build_one(t, nvcc, verbose), tasks()))
+        libs = list(ex.map(lambda t: build_one(t, nvcc, verbose), tasks()))
+    return libs + [build_counter(nvcc, verbose)]
 
 
 if __name__ == "__main__":

@@ -6,15 +6,21 @@ that cannot take cudaMalloc's implicit synchronisation); its scratch is a fixed 
 the library.  Each test calls it through the C ABI twice in a row, on different inputs, and checks
 every result against the regular entry point on the same inputs, within the task tolerance
 (graders' pass rule, atol 1e-3 / rtol 1e-3, tasks/pow_abs_sqrt_mean/tests/task.json) and the
-BASELINE rtol of 1e-5.  The file is named so pytest collects it last.
+BASELINE rtol of 1e-5.  A last test checks, in a fresh process, the property the entry point exists
+for: its calls leave the device's free memory unchanged, while the regular entry point's first call
+(which allocates its scratch) lowers it.  The file is named so pytest collects it last.
 """
 import ctypes
+import json
+import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import pkg
+from conftest import REPO, pkg
 from oracle import exact, inputs
 
 pytestmark = pytest.mark.gpu
@@ -77,3 +83,43 @@ def test_rejects_problems_above_the_static_scratch(lib):
     torch.cuda.synchronize()
     assert st == 0
     assert abs(float(out.item()) - 1e-3) < 1e-9  # every element is sqrt(0 + 1e-6)
+
+
+# Run in a fresh process with every kernel module loaded when the context is created, so the only
+# device memory a call could take is memory the call itself allocates.
+_FRESH = r"""
+import importlib, json, sys, torch
+sys.path.insert(0, sys.argv[1])
+lib = importlib.import_module("cuda-optimization-benchmark_b200").load()
+shape = (16, 4, 512, 512)
+a = torch.randn(shape, device="cuda")
+b = torch.randn(shape, device="cuda")
+out = torch.empty((), device="cuda")
+torch.cuda.synchronize()
+fault = lib.b200_device_fault()          # touches the library's module: loaded into the context now
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+sts = [lib.b200_pow_abs_sqrt_mean_noalloc(a.data_ptr(), b.data_ptr(), 16, 512, 512, out.data_ptr(), None)
+       for _ in range(3)]
+torch.cuda.synchronize()
+got = float(out.item())
+free1 = torch.cuda.mem_get_info()[0]
+lib.b200_pow_abs_sqrt_mean(a.data_ptr(), b.data_ptr(), 16, 512, 512, out.data_ptr())
+torch.cuda.synchronize()
+free2 = torch.cuda.mem_get_info()[0]
+print(json.dumps({"fault": fault, "status": sts, "free": [free0, free1, free2], "noalloc": got,
+                  "regular": float(out.item())}))
+"""
+
+
+def test_allocates_nothing_in_a_fresh_process(lib):
+    env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
+    r = subprocess.run([sys.executable, "-c", _FRESH, str(REPO)], capture_output=True, text=True, timeout=300,
+                       env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    assert d["fault"] == 0 and d["status"] == [0, 0, 0], d
+    free0, free1, free2 = d["free"]
+    assert free1 == free0, f"three no-allocation calls changed the free device memory by {free0 - free1} bytes"
+    assert free2 < free1, "the regular entry point's arena allocation was not visible: the check is not sensitive"
+    assert abs(d["noalloc"] - d["regular"]) <= 1e-5 * abs(d["regular"]), d
