@@ -97,11 +97,37 @@ __device__ __forceinline__ void store_row32(const uint32_t (&r)[32], int row, in
   }
 }
 
+// Operands of at most kPrefetchBytes together are brought into L2 at kernel start, before the
+// wait for the previous kernel: each CTA asks for its 1/gridDim share of x and w (contiguous
+// [M, K] and [N, K] bytes), so a call whose operands are not yet in L2 streams them from HBM at
+// the full rate while the tile pipeline starts, instead of at the rate of the first tiles' TMA
+// loads.  L2 is the point of coherence, so this is safe even when the previous kernel writes them.
+constexpr int64_t kPrefetchBytes = int64_t(48) << 20;
+
+__device__ __forceinline__ void prefetch_share(const uint8_t* x, int64_t xb, const uint8_t* w, int64_t wb) {
+#if B200_TCGEN05
+  const int64_t total = xb + wb;
+  if (total == 0 || total > kPrefetchBytes) return;
+  const int64_t share = ((total + gridDim.x - 1) / gridDim.x + 15) & ~int64_t(15);
+  int64_t lo = int64_t(blockIdx.x) * share;
+  const int64_t hi = lo + share < total ? lo + share : total;
+  while (lo < hi) {
+    const bool in_x = lo < xb;
+    const int64_t seg_end = in_x ? (xb < hi ? xb : hi) : hi;
+    const uint8_t* p = in_x ? x + lo : w + (lo - xb);
+    const int64_t n = seg_end - lo;
+    if (n >= 16) tc::prefetch_l2(p, uint32_t(n & ~int64_t(15)));
+    lo = seg_end;
+  }
+#endif
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
                 float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
-                uint16_t* __restrict__ out, int vec_ok) {
+                uint16_t* __restrict__ out, int vec_ok, const uint8_t* pf_x, const uint8_t* pf_w) {
+  if (threadIdx.x == 0) prefetch_share(pf_x, pf_x ? int64_t(M) * K : 0, pf_w, pf_w ? int64_t(N) * K : 0);
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   if (scale_ptr != nullptr) scale = *scale_ptr;  // written on the device by the quantisation kernels
   using C = Cfg<BN>;
@@ -236,7 +262,8 @@ struct Cfg2 {
 __global__ void __launch_bounds__(kThreads2, 1)
     gemm256_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                    int K, float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
-                   uint16_t* __restrict__ out, int vec_ok) {
+                   uint16_t* __restrict__ out, int vec_ok, const uint8_t* pf_x, const uint8_t* pf_w) {
+  if (threadIdx.x == 0) prefetch_share(pf_x, pf_x ? int64_t(M) * K : 0, pf_w, pf_w ? int64_t(N) * K : 0);
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   if (scale_ptr != nullptr) scale = *scale_ptr;
   using C = Cfg2;
@@ -386,38 +413,46 @@ struct SmallCfg {
   static constexpr int kATile = kBM * kBK;   // 128 rows of W x 128 bytes of K
   static constexpr int kBTile = BNX * kBK;   // BNX rows of x x 128 bytes of K
   static constexpr int kStage = kATile + kBTile;
-  static constexpr int kStages = (192 * 1024) / kStage;
+  static constexpr int kStages = (192 * 1024) / kStage;  // most stages a CTA may use
   static constexpr int kTmemCols = BNX < 32 ? 32 : BNX;
   static constexpr int kSmem = kStages * kStage + 1024;
+  static constexpr int kMinStages = (kBM * BNX * 4 + kStage - 1) / kStage;  // the partial tile fits
   static_assert(kStage % 1024 == 0, "stages keep the 1024-byte swizzle-atom alignment");
-  static_assert(kBM * BNX * 4 <= kStages * kStage, "the partial tile fits in the stage ring");
+  static_assert(kMinStages <= kStages, "the partial tile fits in the stage ring");
 };
 
 // grid = (SK, ceil(N / 128)), cluster (SK, 1, 1).  tmW: map over w [N, K], 128-row box; tmX: map
-// over x [M, K], BNX-row box.
+// over x [M, K], BNX-row box.  S stages (the dynamic shared memory holds S * kStage + 1024 bytes):
+// as many as this CTA has K blocks, so a CTA issues its whole W slice at once and a small ring
+// lets two or three CTAs share an SM.  Before waiting for the previous kernel, thread 0 asks L2
+// for this CTA's W boxes (safe: L2 is coherent; it only starts the HBM reads early), so back to
+// back calls overlap the W stream with the previous call's tail.
 template <int BNX>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N, int K,
                 float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
-                uint16_t* __restrict__ out) {
+                uint16_t* __restrict__ out, int S) {
+  using C = SmallCfg<BNX>;
+  const uint32_t rank = cluster_ctarank(), SK = gridDim.x;
+  const int nb = blockIdx.y;
+  const int nkb = (K + kBK - 1) / kBK;
+  const int kb0 = int((int64_t(nkb) * rank) / SK), kb1 = int((int64_t(nkb) * (rank + 1)) / SK);
+#if B200_TCGEN05
+  if (threadIdx.x == 0)
+    for (int kb = kb0; kb < kb1; ++kb) tc::tma_prefetch_2d(&tmW, kb * kBK, nb * kBM);
+#endif
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   if (scale_ptr != nullptr) scale = *scale_ptr;
-  using C = SmallCfg<BNX>;
-  constexpr int S = C::kStages;
 #if !B200_TCGEN05
   if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
   return;
 #else
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[S], empty[S], tfull;
+  __shared__ uint64_t full[C::kStages], empty[C::kStages], tfull;
   __shared__ uint32_t tmem_base_s;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* part = reinterpret_cast<float*>(smem);  // [128][BNX] fp32 partial tile, after the MMAs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank(), SK = gridDim.x;
-  const int nb = blockIdx.y;
-  const int nkb = (K + kBK - 1) / kBK;
-  const int kb0 = int((int64_t(nkb) * rank) / SK), kb1 = int((int64_t(nkb) * (rank + 1)) / SK);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -427,10 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&tfull, 1);
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) {
-    tc::prefetch_tensormap(&tmW);
-    tc::prefetch_tensormap(&tmX);
-  }
+  if (warp == 0 && lane == 0) tc::prefetch_tensormap(&tmX);
   if (warp == 1) {
     tc::tmem_alloc(&tmem_base_s, C::kTmemCols);
     tc::tmem_relinquish();
@@ -443,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {  // TMA producer over this CTA's K range
       for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
-        const uint32_t s = uint32_t(i) % S, ph = (uint32_t(i) / S) & 1u;
+        const uint32_t s = uint32_t(i) % uint32_t(S), ph = (uint32_t(i) / uint32_t(S)) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u)) break;
         mbar_arrive_expect_tx(&full[s], C::kStage);
         uint8_t* a = smem + s * C::kStage;
@@ -456,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // MMA issuer
       const uint32_t id = tc::idesc(kBM, BNX, 0);
       for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
-        const uint32_t s = uint32_t(i) % S, ph = (uint32_t(i) / S) & 1u;
+        const uint32_t s = uint32_t(i) % uint32_t(S), ph = (uint32_t(i) / uint32_t(S)) & 1u;
         if (!mbar_wait(&full[s], ph)) break;
         tc::fence_after_sync();
         const uint32_t a_addr = smem_addr(smem + s * C::kStage);
@@ -646,7 +678,7 @@ inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, fl
   const int n_tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   const int vec_ok = (N % 8 == 0) && aligned16(out);
-  launch_pdl(kern, grid, kThreads, Cfg<BN>::kSmem, stream, a, b, M, N, K, scale, scale_ptr, bias, out, vec_ok);
+  launch_pdl(kern, grid, kThreads, Cfg<BN>::kSmem, stream, a, b, M, N, K, scale, scale_ptr, bias, out, vec_ok, x, w);
   return launch_status();
 }
 
@@ -659,15 +691,15 @@ inline int launch_tc256(int M, int N, int K, const uint8_t* x, const uint8_t* w,
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   const int vec_ok = (N % 8 == 0) && aligned16(out);
   launch_pdl(gemm256_kernel, grid, kThreads2, Cfg2::kSmem, stream, a, b, M, N, K, scale, scale_ptr, bias, out,
-             vec_ok);
+             vec_ok, x, w);
   return launch_status();
 }
 
-// Split-K factor of the small-M kernel: enough clusters x CTAs to cover the SMs, at most 8 (the
+// Split-K factor of the small-M kernel: enough clusters x CTAs for two CTAs per SM, at most 8 (the
 // portable cluster size) and at most one CTA per 128-byte K block.
 inline int small_split(int N, int K) {
   const int n_tiles = (N + kBM - 1) / kBM, nkb = (K + kBK - 1) / kBK;
-  int sk = sm_count() / n_tiles;
+  int sk = 2 * sm_count() / n_tiles;
   if (sk > 8) sk = 8;
   if (sk > nkb) sk = nkb;
   return sk < 1 ? 1 : sk;
@@ -678,13 +710,17 @@ inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w,
                         const uint16_t* bias, uint16_t* out, cudaStream_t stream) {
   CUtensorMap mw, mx;
   if (!get_maps(w, x, N, M, K, kBM, BNX, &mw, &mx)) return kUnsupported;
+  using SC = SmallCfg<BNX>;
   auto kern = gemv_kernel<BNX>;
-  if (!ensure_dyn_smem(kern, SmallCfg<BNX>::kSmem)) return kCudaError;
+  if (!ensure_dyn_smem(kern, SC::kSmem)) return kCudaError;
   const int sk = small_split(N, K);
+  const int per_cta = ((K + kBK - 1) / kBK + sk - 1) / sk;  // K blocks of the busiest CTA
+  int stages = per_cta < SC::kStages ? per_cta : SC::kStages;
+  if (stages < SC::kMinStages) stages = SC::kMinStages;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(sk), unsigned((N + kBM - 1) / kBM));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = SmallCfg<BNX>::kSmem;
+  cfg.dynamicSmemBytes = size_t(stages) * SC::kStage + 1024;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -695,7 +731,8 @@ inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w,
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (cudaLaunchKernelEx(&cfg, kern, mw, mx, M, N, K, scale, scale_ptr, bias, out) != cudaSuccess) return kCudaError;
+  if (cudaLaunchKernelEx(&cfg, kern, mw, mx, M, N, K, scale, scale_ptr, bias, out, stages) != cudaSuccess)
+    return kCudaError;
   return launch_status();
 }
 
@@ -703,6 +740,9 @@ inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w,
 // 512 = the 256 x 256 tiles of gemm256_kernel, for problems with at least four waves of them.
 inline int plan_bn(int M, int N, int K, const void* x, const void* w) {
   if (K % 16 != 0 || !aligned16(x) || !aligned16(w)) return 0;
+#ifdef B200_FP8_FORCE_BN  // tuning builds only: one tile width for every tensor-core shape with M > 64
+  if (M > 64) return B200_FP8_FORCE_BN;
+#endif
   const int n_m = (M + kBM - 1) / kBM;
   const int sms = sm_count();
   if (((M + kBM2 - 1) / kBM2) * ((N + kBN2 - 1) / kBN2) >= 4 * sms) return 512;
