@@ -149,15 +149,10 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
-// Bring the box at (c0, c1) of a tensor map into L2 (no shared memory, no completion to wait
-// for).  L2 is the device's point of coherence, so this is safe to issue before the kernel has
-// waited for the previous one: a line that kernel writes later is updated in L2.
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(c0), "r"(c1)
-               : "memory");
-}
-
-// Bring `bytes` (a multiple of 16, address 16-byte aligned) of global memory into L2.
+// Bring `bytes` of global memory into L2 (no shared memory, no completion to wait for).  L2 is
+// the device's point of coherence, so this is safe to issue before the kernel has waited for the
+// previous one: a line that kernel writes later is updated in L2.
+// `bytes` is a multiple of 16 and the address 16-byte aligned.
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }

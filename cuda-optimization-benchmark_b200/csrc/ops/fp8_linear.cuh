@@ -413,46 +413,38 @@ struct SmallCfg {
   static constexpr int kATile = kBM * kBK;   // 128 rows of W x 128 bytes of K
   static constexpr int kBTile = BNX * kBK;   // BNX rows of x x 128 bytes of K
   static constexpr int kStage = kATile + kBTile;
-  static constexpr int kStages = (192 * 1024) / kStage;  // most stages a CTA may use
+  static constexpr int kStages = (192 * 1024) / kStage;
   static constexpr int kTmemCols = BNX < 32 ? 32 : BNX;
   static constexpr int kSmem = kStages * kStage + 1024;
-  static constexpr int kMinStages = (kBM * BNX * 4 + kStage - 1) / kStage;  // the partial tile fits
   static_assert(kStage % 1024 == 0, "stages keep the 1024-byte swizzle-atom alignment");
-  static_assert(kMinStages <= kStages, "the partial tile fits in the stage ring");
+  static_assert(kBM * BNX * 4 <= kStages * kStage, "the partial tile fits in the stage ring");
 };
 
 // grid = (SK, ceil(N / 128)), cluster (SK, 1, 1).  tmW: map over w [N, K], 128-row box; tmX: map
-// over x [M, K], BNX-row box.  S stages (the dynamic shared memory holds S * kStage + 1024 bytes):
-// as many as this CTA has K blocks, so a CTA issues its whole W slice at once and a small ring
-// lets two or three CTAs share an SM.  Before waiting for the previous kernel, thread 0 asks L2
-// for this CTA's W boxes (safe: L2 is coherent; it only starts the HBM reads early), so back to
-// back calls overlap the W stream with the previous call's tail.
+// over x [M, K], BNX-row box.
 template <int BNX>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N, int K,
                 float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
-                uint16_t* __restrict__ out, int S) {
-  using C = SmallCfg<BNX>;
-  const uint32_t rank = cluster_ctarank(), SK = gridDim.x;
-  const int nb = blockIdx.y;
-  const int nkb = (K + kBK - 1) / kBK;
-  const int kb0 = int((int64_t(nkb) * rank) / SK), kb1 = int((int64_t(nkb) * (rank + 1)) / SK);
-#if B200_TCGEN05
-  if (threadIdx.x == 0)
-    for (int kb = kb0; kb < kb1; ++kb) tc::tma_prefetch_2d(&tmW, kb * kBK, nb * kBM);
-#endif
+                uint16_t* __restrict__ out) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   if (scale_ptr != nullptr) scale = *scale_ptr;
+  using C = SmallCfg<BNX>;
+  constexpr int S = C::kStages;
 #if !B200_TCGEN05
   if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
   return;
 #else
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[C::kStages], empty[C::kStages], tfull;
+  __shared__ uint64_t full[S], empty[S], tfull;
   __shared__ uint32_t tmem_base_s;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* part = reinterpret_cast<float*>(smem);  // [128][BNX] fp32 partial tile, after the MMAs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank(), SK = gridDim.x;
+  const int nb = blockIdx.y;
+  const int nkb = (K + kBK - 1) / kBK;
+  const int kb0 = int((int64_t(nkb) * rank) / SK), kb1 = int((int64_t(nkb) * (rank + 1)) / SK);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -462,7 +454,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&tfull, 1);
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) tc::prefetch_tensormap(&tmX);
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tensormap(&tmW);
+    tc::prefetch_tensormap(&tmX);
+  }
   if (warp == 1) {
     tc::tmem_alloc(&tmem_base_s, C::kTmemCols);
     tc::tmem_relinquish();
@@ -475,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {  // TMA producer over this CTA's K range
       for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
-        const uint32_t s = uint32_t(i) % uint32_t(S), ph = (uint32_t(i) / uint32_t(S)) & 1u;
+        const uint32_t s = uint32_t(i) % S, ph = (uint32_t(i) / S) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u)) break;
         mbar_arrive_expect_tx(&full[s], C::kStage);
         uint8_t* a = smem + s * C::kStage;
@@ -488,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // MMA issuer
       const uint32_t id = tc::idesc(kBM, BNX, 0);
       for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
-        const uint32_t s = uint32_t(i) % uint32_t(S), ph = (uint32_t(i) / uint32_t(S)) & 1u;
+        const uint32_t s = uint32_t(i) % S, ph = (uint32_t(i) / S) & 1u;
         if (!mbar_wait(&full[s], ph)) break;
         tc::fence_after_sync();
         const uint32_t a_addr = smem_addr(smem + s * C::kStage);
@@ -695,11 +690,11 @@ inline int launch_tc256(int M, int N, int K, const uint8_t* x, const uint8_t* w,
   return launch_status();
 }
 
-// Split-K factor of the small-M kernel: enough clusters x CTAs for two CTAs per SM, at most 8 (the
+// Split-K factor of the small-M kernel: enough clusters x CTAs to cover the SMs, at most 8 (the
 // portable cluster size) and at most one CTA per 128-byte K block.
 inline int small_split(int N, int K) {
   const int n_tiles = (N + kBM - 1) / kBM, nkb = (K + kBK - 1) / kBK;
-  int sk = 2 * sm_count() / n_tiles;
+  int sk = sm_count() / n_tiles;
   if (sk > 8) sk = 8;
   if (sk > nkb) sk = nkb;
   return sk < 1 ? 1 : sk;
@@ -710,17 +705,13 @@ inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w,
                         const uint16_t* bias, uint16_t* out, cudaStream_t stream) {
   CUtensorMap mw, mx;
   if (!get_maps(w, x, N, M, K, kBM, BNX, &mw, &mx)) return kUnsupported;
-  using SC = SmallCfg<BNX>;
   auto kern = gemv_kernel<BNX>;
-  if (!ensure_dyn_smem(kern, SC::kSmem)) return kCudaError;
+  if (!ensure_dyn_smem(kern, SmallCfg<BNX>::kSmem)) return kCudaError;
   const int sk = small_split(N, K);
-  const int per_cta = ((K + kBK - 1) / kBK + sk - 1) / sk;  // K blocks of the busiest CTA
-  int stages = per_cta < SC::kStages ? per_cta : SC::kStages;
-  if (stages < SC::kMinStages) stages = SC::kMinStages;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(sk), unsigned((N + kBM - 1) / kBM));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = size_t(stages) * SC::kStage + 1024;
+  cfg.dynamicSmemBytes = SmallCfg<BNX>::kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -731,8 +722,7 @@ inline int launch_small(int M, int N, int K, const uint8_t* x, const uint8_t* w,
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (cudaLaunchKernelEx(&cfg, kern, mw, mx, M, N, K, scale, scale_ptr, bias, out, stages) != cudaSuccess)
-    return kCudaError;
+  if (cudaLaunchKernelEx(&cfg, kern, mw, mx, M, N, K, scale, scale_ptr, bias, out) != cudaSuccess) return kCudaError;
   return launch_status();
 }
 
