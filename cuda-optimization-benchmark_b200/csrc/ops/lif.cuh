@@ -47,8 +47,9 @@ __device__ __forceinline__ float step(float& mem, float x, float beta, float th)
 }
 
 constexpr int kSeg = 16;                    // time steps per membrane checkpoint
-constexpr int kMaxDepth = 24;               // x slices in flight per CTA
+constexpr int kMaxDepth = 64;               // x slices in flight per CTA, at most
 constexpr int kSmemBudget = 192 * 1024;      // bytes of the x ring
+constexpr int kInFlight = 168 * 1024;        // bytes of x in flight per CTA the ring aims for
 constexpr int kMaxSlab = (1024 - 32) * 4;    // neurons per CTA: consumer threads + one producer warp
 
 // Spike outputs: fp32 [T, B*H] (the reference layout), bits (bit t % 32 of uint32 word
@@ -248,8 +249,15 @@ inline int run_impl(const float* x, const float* mem0, const float* beta, const 
     S = (S + 127) / 128 * 128;
     if (S > kMaxSlab) S = kMaxSlab;
     const int64_t grid = (NB + S - 1) / S;
-    int depth = int(kSmemBudget / (S * 4));
-    if (depth > kMaxDepth) depth = kMaxDepth;
+    // Ring depth: enough slices for about kInFlight bytes in flight (at least 24, the depth
+    // measured best at the BASELINE size), within the shared-memory budget.  Narrow slabs (few
+    // neurons per SM, e.g. one rank's share of a batch split over GPUs) get deeper rings, so the
+    // bytes in flight per SM, and with them the HBM rate, do not shrink with the slab.
+    const int64_t slice = S * 4;
+    int depth = int(kSmemBudget / slice);
+    const int64_t want = (kInFlight + slice - 1) / slice;
+    const int cap = want > 24 ? int(want < kMaxDepth ? want : kMaxDepth) : 24;
+    if (depth > cap) depth = cap;
     if (depth < 2) depth = 2;
     const size_t smem = size_t(depth) * size_t(S) * 4;
     auto kern = lif_slab_kernel<kOut, kCkpt>;
