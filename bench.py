@@ -1008,12 +1008,60 @@ def sharded_ops(ops, lib, dev, world, rank):
     shard_step()
     torch.cuda.synchronize(dev)
     same = bool(torch.equal(out.view(torch.int32), whole.view(torch.int32)))
-    us = graph_ms(shard_step, dev, world, 20) * 1e3
+    us_nccl = graph_ms(shard_step, dev, world, 20) * 1e3
     us_part = graph_ms(partials_only, dev, world, 20) * 1e3
-    entry("robust_l1 2^26", us, us_whole, {"bit_identical_to_1gpu": same},
-          f"{counts[rank]} chunks of {chunk} elements per rank; chunk partials all-gathered "
-          + ("(NCCL, in the graph)" if world > 1 else "(one rank: none)"),
+    # The exchange fused into the kernel (each rank pushes its chunk partials to every rank over
+    # NVLink, every rank runs the same finish): one launch per call.  Its epochs advance per call,
+    # so it is timed as eager back-to-back launches with pre-bound arguments, not from a graph.
+    us_x, same_x, ex = None, None, None
+    if world > 1:
+        try:
+            ex = ops.RobustL1Exchange(world, rank, n)
+        except Exception as e:  # noqa: BLE001 - any failure leaves the NCCL form as the result
+            print(f"rank {rank}: robust-L1 peer exchange unavailable ({e})", file=sys.stderr)
+        okx = torch.tensor([1 if ex is not None else 0], device=dev)
+        dist.all_reduce(okx, op=dist.ReduceOp.MIN)
+        if int(okx.item()) == 0 and ex is not None:
+            ex.close()
+            ex = None
+    if ex is not None:
+        out_x = torch.empty((), device=dev)
+        ws_x = torch.zeros(256, dtype=torch.uint8, device=dev)
+        fx = lib.b200_robust_l1_exchange_async
+        cs = P(torch.cuda.current_stream(dev).cuda_stream)
+        xargs = (P(xs.data_ptr()), P(ys.data_ptr()), n, P(out_x.data_ptr()), P(ws_x.data_ptr()), 256, ex.handle)
+        st = [0]
+
+        def xstep():
+            ex.epoch = lib.b200_peer_next_epoch(ex.epoch)
+            st[0] |= fx(*xargs, ex.epoch, cs)
+        for _ in range(5):
+            xstep()
+        torch.cuda.synchronize(dev)
+        same_x = bool(torch.equal(out_x.view(torch.int32), whole.view(torch.int32)))
+        barrier(world)
+        a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_ev.record()
+        for _ in range(20):
+            xstep()
+        b_ev.record()
+        torch.cuda.synchronize(dev)
+        us_x = max_over_ranks(a_ev.elapsed_time(b_ev) / 20, world) * 1e3
+        if st[0] != 0:
+            raise RuntimeError(f"robust_l1 exchange returned status {st[0]}")
+        barrier(world)
+        ex.close()
+        barrier(world)
+    checks = {"bit_identical_to_1gpu": same}
+    if same_x is not None:
+        checks["exchange_bit_identical_to_1gpu"] = same_x
+    us = us_x if us_x is not None else us_nccl
+    entry("robust_l1 2^26", us, us_whole, checks,
+          f"{counts[rank]} chunks of {chunk} elements per rank; "
+          + ("chunk partials pushed to every rank over NVLink inside the kernel (one launch)" if us_x is not None
+             else "chunk partials all-gathered (NCCL, in a graph)" if world > 1 else "one rank: no exchange"),
           {"us_partials_kernel": us_part, "us_exchange_and_finish": us - us_part,
+           "us_nccl_allgather_form": us_nccl if world > 1 else None,
            "bytes_per_rank": 8 * (hi - lo), "frac_of_hbm_partials": 8 * (hi - lo) / (us_part * 1e-6) / 1e9
            / peaks()[0]})
     del xs, ys, parts, allp

@@ -63,6 +63,9 @@ SIGNATURES = {
     "b200_peer_exchange_create": (c_int, [c_int, c_int, c_i64, c_sz, c_p, c_p]),
     "b200_peer_exchange_open": (c_int, [c_p, c_p]),
     "b200_peer_exchange_destroy": (c_int, [c_p]),
+    "b200_robust_l1_exchange_record_bytes": (c_sz, []),
+    "b200_robust_l1_exchange_slots": (c_i64, [c_i64, c_int]),
+    "b200_robust_l1_exchange_async": (c_int, [c_p, c_p, c_i64, c_p, c_p, c_sz, c_p, ctypes.c_uint, c_p]),
     "b200_rl_step_exchange_async": (c_int, [c_p, c_p, c_f, c_i32, c_i32, c_p, c_p, c_p, c_p, c_p, c_i64, c_f, c_p, c_p,
                                             c_sz, c_p, ctypes.c_uint, ctypes.c_uint, c_p]),
     # GAE

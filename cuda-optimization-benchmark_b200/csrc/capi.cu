@@ -211,6 +211,18 @@ int b200_rl_step_exchange_async(const float* reward, const uint8_t* done, float 
                                 as_stream(stream));
 }
 
+size_t b200_robust_l1_exchange_record_bytes(void) { return b200::robust_l1::kExchangeRecordBytes; }
+int64_t b200_robust_l1_exchange_slots(int64_t n_total, int world) {
+  if (n_total < 0 || world < 1) return -1;
+  return b200::robust_l1::exchange_slots(n_total, world);
+}
+int b200_robust_l1_exchange_async(const float* inp, const float* target, int64_t n_total, float* output,
+                                  void* workspace, size_t workspace_bytes, void* exchange, unsigned epoch,
+                                  void* stream) {
+  return b200::robust_l1::run_exchange(inp, target, n_total, output, workspace, workspace_bytes,
+                                       static_cast<const b200::PeerExchange*>(exchange), epoch, as_stream(stream));
+}
+
 // ----------------------------------------------------------------------------------------- GAE
 int b200_gae_async(const float* reward, const float* value, const float* next_value, const uint8_t* done,
                    const uint8_t* terminated, float gamma, float lmbda, int32_t B, int32_t T, float* advantage,

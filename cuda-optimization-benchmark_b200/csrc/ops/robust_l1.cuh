@@ -15,6 +15,8 @@
 #pragma once
 
 #include "../common/b200_common.cuh"
+#include "../common/ll.cuh"
+#include "../common/peer.cuh"
 #include "../common/workspace.cuh"
 
 namespace b200 {
@@ -25,7 +27,7 @@ constexpr int kVecPerThread = 8;                                         // floa
 constexpr int64_t kChunk = int64_t(kThreads) * kVecPerThread * 4;      // 8192 elements per chunk
 
 // Workspace: [ticket u32 | pad to 256 B][double partials[n_chunks]].
-inline int64_t num_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
+__host__ __device__ inline int64_t num_chunks(int64_t n) { return (n + kChunk - 1) / kChunk; }
 inline size_t workspace_bytes(int64_t n) { return 256 + align256(size_t(num_chunks(n)) * sizeof(double)); }
 
 // One element, in the prompt's order: d = a - b; p = |d|^2; s = p + 1e-6; v = sqrt(s).
@@ -159,6 +161,85 @@ inline int shard_partials(const float* a, const float* b, int64_t n, double* par
 inline int shard_finish(const double* partials, int64_t n_parts, int64_t n_total, float* out, cudaStream_t stream) {
   if (n_parts < 0 || n_total < 0 || out == nullptr || (n_parts > 0 && partials == nullptr)) return kInvalidArgument;
   return launch_pdl(finish_kernel, 1, kThreads, 0, stream, partials, n_parts, inv_count(n_total), out);
+}
+
+// ------------------------------------------------------------- multi-GPU: exchange in the kernel
+// One process per GPU; rank r holds the elements of global chunks [c0(r), c0(r + 1)) with
+// c0(r) = floor(n_chunks * r / world) (the split of dist.shard_range).  One launch per rank: every
+// CTA stores each chunk partial it computes, as a 16-byte LL record (the double's two words, each
+// with the epoch), into slot (r, local chunk) of every rank's exchange buffer, its own included,
+// over NVLink peer memory; the rank's last CTA then reads all n_chunks records from its own buffer
+// in global chunk order (each wait bounded) and runs finish()'s fixed-order sum.  Every rank
+// writes the same output, bit-identical to run() over the whole range on one GPU for any number
+// of ranks.  All writes, records included, come after pdl_wait: a rank stores epoch e + 1 records
+// only once its epoch-e launch has completed, i.e. after reading every peer's epoch-e records,
+// so a peer never finds a half it is still reading overwritten (peer.cuh).
+constexpr size_t kExchangeRecordBytes = 16;
+
+__host__ __device__ __forceinline__ int64_t first_chunk(int64_t n_chunks, int world, int r) {
+  return (n_chunks * r) / world;
+}
+inline int64_t exchange_slots(int64_t n, int world) {
+  const int64_t nc = num_chunks(n);
+  int64_t most = 0;
+  for (int r = 0; r < world; ++r) {
+    const int64_t c = first_chunk(nc, world, r + 1) - first_chunk(nc, world, r);
+    most = c > most ? c : most;
+  }
+  return most;
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(kThreads) exchange_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                                            int64_t n_total, unsigned* __restrict__ ticket,
+                                                            double inv_n, float* __restrict__ out, const PeerView pv) {
+  pdl_begin();  // every write below (records included) follows the previous launch's completion
+  const int64_t nc = num_chunks(n_total);
+  const int64_t c0 = first_chunk(nc, pv.world, pv.rank), c1 = first_chunk(nc, pv.world, pv.rank + 1);
+  const int64_t n_local = (c1 * kChunk < n_total ? c1 * kChunk : n_total) - c0 * kChunk;
+  for (int64_t c = blockIdx.x; c < c1 - c0; c += gridDim.x) {
+    const float t = thread_chunk_sum<kVec>(a, b, c * kChunk, n_local);
+    const double s = cta_sum(double(t));
+    if (threadIdx.x == 0) {
+      const unsigned long long bits = __double_as_longlong(s);
+      for (int r = 0; r < pv.world; ++r)
+        ll_store2<LLScope::kSys>(peer_record(pv, r, pv.rank, c), ll_word(uint32_t(bits), pv.epoch),
+                                 ll_word(uint32_t(bits >> 32), pv.epoch));
+    }
+  }
+  if (!elect_last_cta(ticket)) return;
+  // finish() over the gathered records: thread t sums global chunks t, t + kThreads, ... in order.
+  LLReader<2, LLScope::kSys> rd{peer_record(pv, pv.rank, 0, 0), pv.epoch};
+  double s = 0.0;
+  for (int64_t g = threadIdx.x; g < nc; g += kThreads) {
+    const int owner = int(((g + 1) * pv.world - 1) / nc);  // the rank whose chunk range holds g
+    uint32_t w[2];
+    rd.read(int64_t(owner) * pv.slots + (g - first_chunk(nc, pv.world, owner)), w);
+    s += __hiloint2double(int(w[1]), int(w[0]));
+  }
+  s = cta_sum(s);
+  if (threadIdx.x == 0) out[0] = float(s * inv_n);
+}
+
+// One rank's call: a, b hold this rank's elements (the global chunk range above); workspace: 256
+// bytes whose first 4 are zero before the first call (left zero); the exchange was created with
+// kExchangeRecordBytes records and at least exchange_slots(n_total, world) slots, and opened.
+inline int run_exchange(const float* a, const float* b, int64_t n_total, float* out, void* workspace,
+                        size_t ws_bytes, const PeerExchange* x, unsigned epoch, cudaStream_t stream) {
+  if (n_total < 0 || out == nullptr || x == nullptr || epoch == 0) return kInvalidArgument;
+  if (x->rec_bytes != kExchangeRecordBytes || x->slots < exchange_slots(n_total, x->world)) return kInvalidArgument;
+  for (int r = 0; r < x->world; ++r)
+    if (x->base[r] == nullptr) return kInvalidArgument;  // not opened
+  const int64_t nc = num_chunks(n_total);
+  const int64_t local = first_chunk(nc, x->world, x->rank + 1) - first_chunk(nc, x->world, x->rank);
+  if (local > 0 && (a == nullptr || b == nullptr)) return kInvalidArgument;
+  if (workspace == nullptr || ws_bytes < 256) return kWorkspaceTooSmall;
+  unsigned* ticket = static_cast<unsigned*>(workspace);
+  const PeerView pv = peer_view(*x, epoch);
+  const bool vec = aligned16(a) && aligned16(b);
+  auto kern = vec ? exchange_kernel<true> : exchange_kernel<false>;
+  const int grid = balanced_grid(local > 0 ? local : 1, resident_ctas_per_sm(kern, kThreads, 0));
+  return launch_pdl(kern, grid, kThreads, 0, stream, a, b, n_total, ticket, inv_count(n_total), out, pv);
 }
 
 // Element count of the reference ABI's (batch_size, 4, height, width) tensors, or -1 when a

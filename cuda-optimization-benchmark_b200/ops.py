@@ -350,12 +350,16 @@ class PeerExchange:
     `swap(handle) -> list of handles` must return every rank's 64-byte handle in rank order; with
     torch.distributed initialised, the default does that with all_gather_object."""
 
-    def __init__(self, world, rank, n, swap=None):
+    def __init__(self, world, rank, n, swap=None, slots=None, record_bytes=None):
+        """An exchange for the RL step over n samples per rank (the default), or, with `slots` and
+        `record_bytes`, for another op's records (e.g. RobustL1Exchange)."""
         lib = _lib()
         self._ptr = ctypes.c_void_p()
         handle = (ctypes.c_char * lib.b200_peer_handle_bytes())()
-        _native.check(lib.b200_peer_exchange_create(int(world), int(rank), 1, lib.b200_rl_step_exchange_record_bytes(),
-                                                    ctypes.byref(self._ptr), handle), "peer_exchange_create")
+        slots = 1 if slots is None else int(slots)
+        rec = lib.b200_rl_step_exchange_record_bytes() if record_bytes is None else int(record_bytes)
+        _native.check(lib.b200_peer_exchange_create(int(world), int(rank), slots, rec, ctypes.byref(self._ptr),
+                                                    handle), "peer_exchange_create")
         if swap is None:
             import torch.distributed as dist
 
@@ -378,6 +382,44 @@ class PeerExchange:
         if self._ptr:
             _native.check(_lib().b200_peer_exchange_destroy(self._ptr), "peer_exchange_destroy")
             self._ptr = ctypes.c_void_p()
+
+
+class RobustL1Exchange(PeerExchange):
+    """The NVLink exchange of the multi-GPU robust-L1 mean over n_total elements (one process per
+    GPU; every rank builds one with the same n_total, collectively)."""
+
+    def __init__(self, world, rank, n_total, swap=None):
+        lib = _lib()
+        super().__init__(world, rank, n_total, swap=swap, slots=lib.b200_robust_l1_exchange_slots(int(n_total), world),
+                         record_bytes=lib.b200_robust_l1_exchange_record_bytes())
+
+    def shard_range(self):
+        """[lo, hi) global element range this rank holds (whole chunks, as dist.shard_range)."""
+        lib = _lib()
+        chunk = lib.b200_robust_l1_chunk_elems()
+        n_chunks = (self.n + chunk - 1) // chunk
+        c0, c1 = (n_chunks * self.rank) // self.world, (n_chunks * (self.rank + 1)) // self.world
+        return min(c0 * chunk, self.n), min(c1 * chunk, self.n)
+
+
+def robust_l1_exchange(exchange, inp_shard, tgt_shard, out=None):
+    """The robust-L1 mean over every rank's elements, from this rank's shard (its
+    exchange.shard_range() elements); every rank gets the same bits, those of robust_l1 over the
+    whole range on one GPU.  Every rank must call it the same number of times."""
+    _need(inp_shard, "inp", torch.float32)
+    _need(tgt_shard, "target", torch.float32, inp_shard.device)
+    lo, hi = exchange.shard_range()
+    if inp_shard.numel() != hi - lo or tgt_shard.numel() != hi - lo:
+        raise ValueError(f"this rank holds elements [{lo}, {hi}); got {inp_shard.numel()}")
+    dev = inp_shard.device
+    out = torch.empty((), dtype=torch.float32, device=dev) if out is None else out
+    lib = _lib()
+    ws = workspace("robust_l1_exchange", 256, dev)
+    exchange.epoch = lib.b200_peer_next_epoch(exchange.epoch)
+    _native.check(lib.b200_robust_l1_exchange_async(_opt_ptr(inp_shard, out), _opt_ptr(tgt_shard, out), exchange.n,
+                                                    _ptr(out), _ptr(ws), ws.numel(), exchange.handle, exchange.epoch,
+                                                    _stream(dev)), "robust_l1_exchange")
+    return out
 
 
 def rl_step_exchange(exchange, reward, done, gamma, cur, old, adv, clip_epsilon, entropy=None, rtg_out=None,

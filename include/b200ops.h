@@ -226,6 +226,26 @@ int b200_rl_step_exchange_async(const float* reward, const uint8_t* done, float 
                                 float* ppo_out, void* workspace, size_t workspace_bytes, void* exchange,
                                 unsigned epoch, unsigned flags, void* stream);
 
+/* Robust-L1 over GPUs with the partial exchange fused into the kernel (one process per GPU of one
+ * node; no counterpart in the reference, whose op runs on one device: it is
+ * reference/pow_abs_sqrt_mean/solution.cu:99-118's reduction split over ranks).  Rank r holds the
+ * elements of global chunks [floor(C r / world), floor(C (r + 1) / world)) of the n_total-element
+ * range, C = ceil(n_total / b200_robust_l1_chunk_elems()) (inp / target point at the first of them).
+ * Each rank creates an exchange with b200_peer_exchange_create(world, rank,
+ * b200_robust_l1_exchange_slots(n_total, world), b200_robust_l1_exchange_record_bytes(), ...),
+ * the ranks swap handles and open them as for the RL step, and every call passes the same `epoch` on
+ * every rank (1 first, then b200_peer_next_epoch(previous)).  Each rank's kernel pushes its chunk
+ * partials to every rank over NVLink as they are computed and every rank reduces all of them in
+ * chunk order: every rank's output[0] is bit-identical to b200_robust_l1_async over the whole range
+ * on one GPU, for any number of ranks.  workspace: 256 bytes, the first 4 zero before the first
+ * call (left zero).  A rank whose partials do not arrive within 2 s makes the others set bit 0 of
+ * the device fault word instead of hanging. */
+size_t b200_robust_l1_exchange_record_bytes(void);
+int64_t b200_robust_l1_exchange_slots(int64_t n_total, int world);
+int b200_robust_l1_exchange_async(const float* inp, const float* target, int64_t n_total, float* output,
+                                  void* workspace, size_t workspace_bytes, void* exchange, unsigned epoch,
+                                  void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Generalised advantage estimation (no reference counterpart: the step between reward_to_go and
  * ppo_clip in the reference's source library, TorchRL's generalized_advantage_estimate; Schulman
