@@ -199,6 +199,30 @@ def profiled_traffic(kernel):
     return int(m.group(1)) if m else None
 
 
+def bind_to_gpu_numa_node(dev):
+    """Restrict this process to the CPUs of the NUMA node the GPU's PCIe link hangs off (from sysfs),
+    so that pinned host memory allocated afterwards is local to that link.  Returns the node, or
+    None when the machine does not say (single-node hosts, containers without sysfs)."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        base = Path("/sys/bus/pci/devices") / bus
+        node = int((base / "numa_node").read_text().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in (base / "local_cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= set(os.sched_getaffinity(0))
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return node
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def workload_config(world):
     """The workload both arms run (identical dicts, so the two JSON lines name the same config)."""
     return {"workload": "rl_pipeline: reward_to_go + ppo_clip_ext", "B": B, "T": T, "H": 1,
@@ -474,6 +498,10 @@ def run_b200(args, world, rank, local):
         graph_ms = g0.elapsed_time(g1) / args.steps
         del graphs
 
+    # ---- e2e: the host buffers live on the CPU socket the GPU is attached to: with one process per
+    # GPU, pinned buffers on the far socket would send every rank's copies across the socket link.
+    all_cpus = os.sched_getaffinity(0)
+    numa = bind_to_gpu_numa_node(dev)
     # ---- e2e: same entry points, inputs from pinned host memory, results read back each step.
     # PCIe is full duplex: a step's results are read back on a copy stream while the next step's
     # inputs go up, so the outputs and their host copies alternate between two buffers (step i + 2
@@ -535,6 +563,7 @@ def run_b200(args, world, rank, local):
     torch.cuda.synchronize(dev)
     barrier(world)
     e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps, world)
+    os.sched_setaffinity(0, all_cpus)  # the CPU baselines below use every core again
 
     extra, sharded, cpu_ops = {}, None, None
     if not args.no_ops:
@@ -617,7 +646,8 @@ def run_b200(args, world, rank, local):
         "e2e": {"value": world * N_SAMPLES / (e2e_ms * 1e-3), "unit": "samples/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "pipeline": "each step's results are read back on a second stream while the next step's inputs "
-                            "go up (PCIe full duplex)"},
+                            "go up (PCIe full duplex)",
+                "host_numa_node": numa},
         "gpu_launches": per_step_launches * args.steps,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                    "samples": clk["samples"],

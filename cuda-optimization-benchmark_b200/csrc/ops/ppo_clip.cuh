@@ -574,6 +574,25 @@ __device__ __forceinline__ bool chunk_records(const float* __restrict__ cur, con
   return s_claim != 0u;
 }
 
+// Before waiting for the previous kernel, thread 0 asks L2 for this CTA's chunks of every input
+// stream (16 KB bulk prefetches, 16-byte aligned inputs only): the whole batch starts streaming
+// from HBM at once, overlapping the previous kernel's tail, instead of as each thread's first loads
+// are issued.  L2 is the point of coherence, so this is safe even if that kernel writes the inputs.
+template <bool kEnt>
+__device__ __forceinline__ void prefetch_chunks(const float* cur, const float* old, const float* adv,
+                                                const float* ent, int64_t n, int64_t cta, int64_t n_ctas) {
+  const int64_t n_chunks = num_chunks(n);
+  for (int64_t c = cta; c < n_chunks; c += n_ctas) {
+    const int64_t e0 = c * kChunk, cnt = (n - e0 < kChunk ? n - e0 : kChunk);
+    const uint32_t bytes = uint32_t(cnt * 4) & ~15u;
+    if (bytes == 0) continue;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(cur + e0), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(old + e0), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(adv + e0), "r"(bytes) : "memory");
+    if (kEnt) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ent + e0), "r"(bytes) : "memory");
+  }
+}
+
 // One launch of the whole op (CTA c handles chunks c, c + gridDim.x, ...; the grid is one resident
 // wave, so the reducer's waits always end).  kVec: 128-bit loads for full chunks (16-byte aligned
 // inputs).
@@ -583,6 +602,7 @@ __global__ void __launch_bounds__(kThreads, 4) loss_kernel(const float* __restri
                                                         int64_t n, Clip clip, ulonglong2* __restrict__ recs,
                                                         Control* __restrict__ ctl, double inv_n,
                                                         float* __restrict__ out) {
+  if (kVec && threadIdx.x == 0) prefetch_chunks<kEnt>(cur, old, adv, ent, n, blockIdx.x, gridDim.x);
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   unsigned epoch;
   if (!chunk_records<kVec, kEnt>(cur, old, adv, ent, n, clip, recs, ctl, blockIdx.x, gridDim.x, &epoch)) return;
@@ -600,6 +620,7 @@ __global__ void __launch_bounds__(kThreads, 4) partials_kernel(const float* __re
                                                             const float* __restrict__ adv,
                                                             const float* __restrict__ ent, int64_t n, Clip clip,
                                                             Partial* __restrict__ partials) {
+  if (kVec && threadIdx.x == 0) prefetch_chunks<kEnt>(cur, old, adv, ent, n, blockIdx.x, gridDim.x);
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
   chunk_partials<kVec, kEnt>(cur, old, adv, ent, n, clip, partials, blockIdx.x, gridDim.x);
 }
