@@ -46,7 +46,7 @@ constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kBKe = 64;       // fp16 elements of K per stage (one 128-byte swizzle row)
 constexpr int kUmmaK = 16;     // K per tcgen05.mma for 16-bit operands
-constexpr int kThreads = 192;  // warp 0 loads, warp 1 issues MMAs, warps 2-5 epilogue
+constexpr int kThreads = 320;  // warp 0 loads, warp 1 issues MMAs, warps 2-9 epilogue
 constexpr int kGroupM = 8;
 constexpr float kLoScale = 2048.0f;      // 2^11
 constexpr float kLoUnscale = 1.0f / 2048.0f;
@@ -440,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(&tfull, 1);
-    mbar_init(&tempty, 4);
+    mbar_init(&tempty, 8);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -507,8 +507,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::mma_commit(&tfull);
       }
     }
-  } else {  // epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32)
-    const int q = warp & 3;
+  } else {  // epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32), column half (w-2)/4
+    const int q = warp & 3, h = (warp - 2) >> 2;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       int mb, nb;
@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool vec_ok = (N % 4) == 0;
       const int parts = nkb < kD0Parts ? nkb : kD0Parts;  // D0 accumulators written this tile
 #pragma unroll 1
-      for (int cc = 0; cc < kBN / 32; ++cc) {
+      for (int cc = h * (kBN / 64); cc < (h + 1) * (kBN / 64); ++cc) {
         uint32_t a[32], c[32], t[32];
         const uint32_t lane_off = uint32_t(q * 32) << 16;
         tc::tmem_ld32(tmem + lane_off + uint32_t(cc * 32), a);

@@ -254,7 +254,8 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
                                                                      float* __restrict__ unscale) {
   pdl_begin();
   // The cubic forms take 64 batch rows per tile (each input's reciprocals serve 8 rows per thread;
-  // plane rows are written as half2 pairs, 128 bytes per warp); the general form 32.
+  // a plane row's 64 values go out as two 64-byte warp stores of lanes' consecutive words, which
+  // reads the tile row without bank conflicts); the general form 32.
   constexpr int kW = at_tile_rows(NK);
   extern __shared__ float s_t[];  // [1 + C][kTile][kW + 1]
   const int tx = threadIdx.x, ty = threadIdx.y;
@@ -293,9 +294,10 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
     const float f = p == 0 ? kan::fp16_row_factor(__uint_as_float(amax_x[i0 + ii])) : 1.0f;
     if (blockIdx.y == 0 && tx == 0) unscale[kr] = 1.0f / f;
     const float* srow = s_t + (p * kTile + ii) * (kW + 1);
-    if (kW == 64) {  // b0 + 64 <= kp (kp is a multiple of 64)
-      const int64_t b = b0 + 2 * tx;
-      kan::split_store2(srow[2 * tx] * f, srow[2 * tx + 1] * f, hi + kr * kp + b, lo + kr * kp + b);
+    if (kW == 64) {  // b0 + 64 <= kp (kp is a multiple of 64); consecutive lanes read consecutive words
+      const int64_t b = b0 + tx;
+      kan::split_store(srow[tx] * f, hi + kr * kp + b, lo + kr * kp + b);
+      kan::split_store(srow[tx + 32] * f, hi + kr * kp + b + 32, lo + kr * kp + b + 32);
     } else {
       const int64_t b = b0 + tx;
       if (b < kp) kan::split_store(srow[tx] * f, hi + kr * kp + b, lo + kr * kp + b);
