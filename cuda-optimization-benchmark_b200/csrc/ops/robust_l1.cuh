@@ -209,13 +209,26 @@ __global__ void __launch_bounds__(kThreads) exchange_kernel(const float* __restr
   }
   if (!elect_last_cta(ticket)) return;
   // finish() over the gathered records: thread t sums global chunks t, t + kThreads, ... in order.
+  // The records are read kBatch at a time (all loads of a batch in flight together: a system-scope
+  // load takes microseconds, so one record at a time would serialise them).
+  constexpr int kBatch = 16;
   LLReader<2, LLScope::kSys> rd{peer_record(pv, pv.rank, 0, 0), pv.epoch};
   double s = 0.0;
-  for (int64_t g = threadIdx.x; g < nc; g += kThreads) {
-    const int owner = int(((g + 1) * pv.world - 1) / nc);  // the rank whose chunk range holds g
-    uint32_t w[2];
-    rd.read(int64_t(owner) * pv.slots + (g - first_chunk(nc, pv.world, owner)), w);
-    s += __hiloint2double(int(w[1]), int(w[0]));
+  for (int64_t g0 = threadIdx.x; g0 < nc; g0 += int64_t(kBatch) * kThreads) {
+    int64_t idx[kBatch];
+    bool use[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t g = g0 + int64_t(u) * kThreads;
+      use[u] = g < nc;
+      const int owner = use[u] ? int(((g + 1) * pv.world - 1) / nc) : 0;  // the rank whose chunk range holds g
+      idx[u] = use[u] ? int64_t(owner) * pv.slots + (g - first_chunk(nc, pv.world, owner)) : 0;
+    }
+    uint32_t w[kBatch][2];
+    rd.read<kBatch>(idx, use, w);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (use[u]) s += __hiloint2double(int(w[u][1]), int(w[u][0]));
   }
   s = cta_sum(s);
   if (threadIdx.x == 0) out[0] = float(s * inv_n);
