@@ -1432,6 +1432,28 @@ def run_profile(ops_list, reps):
             lib.b200_efficient_kan_async(t["x"].data_ptr(), t["grid"].data_ptr(), t["base_weight"].data_ptr(),
                                          t["spline_weight"].data_ptr(), t["spline_scaler"].data_ptr(), 5, 3, s["B"],
                                          s["I"], s["O"], out.data_ptr(), ws.data_ptr(), nb, None)
+    if "gae" in ops_list:  # configs[1] batch, as the bench's `ops` line
+        s = inputs.baseline_inputs("rl_pipeline", seed=0)
+        r, dn = s["reward"].to(dev), s["done"].to(dev)
+        vv = torch.randn(r.shape, device=dev) * 0.5
+        nv = torch.roll(vv, -1, dims=1)
+        adv, tgt = torch.empty_like(r), torch.empty_like(r)
+        for _ in range(reps):
+            ops.gae(r, vv, nv, dn, dn, 0.99, 0.95, advantage=adv, value_target=tgt)
+    if "rtg_long" in ops_list:  # 8 rows of 2^21 steps, chunked along T
+        g = torch.Generator(device=dev).manual_seed(0)
+        r = torch.rand(8, 1 << 21, device=dev, generator=g)
+        dn = torch.rand(8, 1 << 21, device=dev, generator=g) < 0.001
+        out = torch.empty_like(r)
+        for _ in range(reps):
+            ops.reward_to_go_chunked(r, dn, 0.99, out=out)
+    if "fp8_quant" in ops_list:  # bf16 16384 x 8192, as the bench's `ops` line
+        g = torch.Generator(device=dev).manual_seed(0)
+        xq = torch.randn(16384, 8192, device=dev, generator=g).to(torch.bfloat16)
+        qq = torch.empty(xq.shape, dtype=torch.float8_e4m3fn, device=dev)
+        sq = torch.empty(1, device=dev)
+        for _ in range(reps):
+            ops.fp8_quantize(xq, q=qq, scale=sq)
     if "kan_timed" in ops_list:  # the reference's timed case (tasks/efficient_kan/tests/task.json, G = 8)
         s = inputs.task_inputs("efficient_kan", {"B": 4096, "I": 256, "O": 512}, 305)
         t = {k: s[k].to(dev) for k in ["x", "grid", "base_weight", "spline_weight", "spline_scaler"]}
@@ -1467,7 +1489,8 @@ def main():
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op lines of the other streaming ops")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--profile", default=None,
-                    help="comma list of ops (rl_step, rtg, ppo, lif, lif_packed, lif_backward, robust_l1, kan, kan_timed, "
+                    help="comma list of ops (rl_step, rtg, ppo, gae, rtg_long, fp8_quant, lif, lif_packed, lif_backward, "
+                         "robust_l1, kan, kan_timed, "
                          "kan_backward, fp8_m16, fp8_m1024, "
                          "fp8_8192, "
                          "fp8_16384, fp8_ref_timed): run each --steps times for ncu, no timing")
