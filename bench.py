@@ -1038,8 +1038,10 @@ def sharded_ops(ops, lib, dev, world, rank):
     shard_step()
     torch.cuda.synchronize(dev)
     same = bool(torch.equal(out.view(torch.int32), whole.view(torch.int32)))
-    us_nccl = graph_ms(shard_step, dev, world, 20) * 1e3
-    us_part = graph_ms(partials_only, dev, world, 20) * 1e3
+    # 100 calls per timing so the ranks' start skew after the barrier (tens of µs between
+    # processes) is a small share of the per-call figure of the forms that wait for every rank.
+    us_nccl = graph_ms(shard_step, dev, world, 100) * 1e3
+    us_part = graph_ms(partials_only, dev, world, 100) * 1e3
     # The exchange fused into the kernel (each rank pushes its chunk partials to every rank over
     # NVLink, every rank runs the same finish): one launch per call.  Its epochs advance per call,
     # so it is timed as eager back-to-back launches with pre-bound arguments, not from a graph.
@@ -1072,11 +1074,11 @@ def sharded_ops(ops, lib, dev, world, rank):
         barrier(world)
         a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a_ev.record()
-        for _ in range(20):
+        for _ in range(100):
             xstep()
         b_ev.record()
         torch.cuda.synchronize(dev)
-        us_x = max_over_ranks(a_ev.elapsed_time(b_ev) / 20, world) * 1e3
+        us_x = max_over_ranks(a_ev.elapsed_time(b_ev) / 100, world) * 1e3
         if st[0] != 0:
             raise RuntimeError(f"robust_l1 exchange returned status {st[0]}")
         barrier(world)

@@ -18,11 +18,12 @@
 //     each stage back to the loader and each finished accumulator to the epilogue;
 //   - warps 2-9: epilogue; tcgen05.ld the accumulator (one TMEM lane quarter and one half of the
 //     columns per warp, one output row per thread), fused acc * (1/(sx*sw)) + bias, round to
-//     bf16, 128-bit stores; it drains one accumulator while the MMAs fill the other.  Measured on
-//     M = 2048, N = 4096, K = 1024 (one or two tiles per CTA): the epilogue's stores are about
-//     half of the launch (16.1 us with them, 8.7 us without), eight warps take 14.9 us against
-//     four warps' 16.1, and staging the rows through shared memory for coalesced or TMA stores
-//     was slower (19-25 us).
+//     bf16; it drains one accumulator while the MMAs fill the other.  For BN >= 128 each warp
+//     stages 32 rows x 64 columns through a bank-conflict-free 4 KB shared-memory block so a
+//     128-bit store instruction writes four whole 128-byte row segments (store_rows64_staged);
+//     stored from registers, each instruction touched 32 rows.  Measured on M = 2048, N = 4096,
+//     K = 1024 (one or two tiles per CTA): 16.1 us with four epilogue warps storing from
+//     registers, 8.7 us with the stores removed, 14.9 us with eight warps, 13.9 us staged.
 // Small problems take BN = 128 or 64 so more SMs get tiles; M <= 64 swaps the operands and splits
 // K over a cluster (gemv_kernel).  Other shapes (K not a multiple of 16, unaligned operands) take a
 // shared-memory tiled CUDA-core kernel with the same arithmetic.
@@ -54,7 +55,9 @@ struct Cfg {
   static constexpr int kStage = kATile + kBTile;
   static constexpr int kStages = (192 * 1024) / kStage;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmem = kStages * kStage + 1024;  // + alignment slack for the 1024 B atoms
+  // Per-epilogue-warp staging of 32 rows x 64 bf16 columns (4 KB each, eight warps) for BN >= 128.
+  static constexpr int kStageOut = BN >= 128 ? 8 * 4096 : 0;
+  static constexpr int kSmem = kStages * kStage + kStageOut + 1024;  // + alignment slack for the 1024 B atoms
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int n_m, int n_n, int& mb, int& nb) {
@@ -100,6 +103,53 @@ __device__ __forceinline__ void store_row32(const uint32_t (&r)[32], int row, in
       }
     }
   }
+}
+
+// Epilogue of 64 consecutive columns n0..n0+63 for a warp's 32 rows row0..row0+31 (this lane's
+// accumulator row is row0 + lane: r0 holds its columns 0-31, r1 columns 32-63), through the warp's
+// 4 KB staging area so that each 128-bit global store instruction writes four whole 128-byte row
+// segments instead of 32 scattered 16-byte pieces.  Staging layout: row r at byte 128 r, its
+// 16-byte chunk c at ((c ^ (r & 7)) * 16), so the writes (a lane's 8 chunks of its row) and the
+// reads (8 lanes per row) are both free of bank conflicts.  N % 8 == 0 and out 16-byte aligned;
+// bias_vec: bias 16-byte aligned.  The arithmetic is store_row32's.
+__device__ __forceinline__ void store_rows64_staged(const uint32_t (&r0)[32], const uint32_t (&r1)[32], int row0,
+                                                    int lane, int n0, int M, int N, float scale,
+                                                    const uint16_t* __restrict__ bias, bool bias_vec,
+                                                    uint16_t* __restrict__ out, uint8_t* stage) {
+  const int nb = N - n0 < 64 ? N - n0 : 64;  // columns of this block inside the output (multiple of 8)
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t bw[4] = {0u, 0u, 0u, 0u};  // bias of columns 8c .. 8c+7 as bf16 pairs
+    if (8 * c < nb) {
+      if (bias_vec) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(bias + n0) + c);
+        bw[0] = v.x; bw[1] = v.y; bw[2] = v.z; bw[3] = v.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          bw[j] = uint32_t(__ldg(bias + n0 + 8 * c + 2 * j)) | (uint32_t(__ldg(bias + n0 + 8 * c + 2 * j + 1)) << 16);
+      }
+    }
+    uint32_t p[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = 8 * c + 2 * j;  // column within the block
+      const uint32_t a0 = e < 32 ? r0[e] : r1[e - 32], a1 = e < 32 ? r0[e + 1] : r1[e - 31];
+      p[j] = pack_bf16x2(fmaf(__uint_as_float(a0), scale, __uint_as_float(bw[j] << 16)),
+                         fmaf(__uint_as_float(a1), scale, __uint_as_float(bw[j] & 0xffff0000u)));
+    }
+    *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+  }
+  __syncwarp();
+  const int c = lane & 7;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int rr = 4 * k + (lane >> 3);
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+    const int row = row0 + rr;
+    if (row < M && 8 * c < nb) *reinterpret_cast<uint4*>(out + int64_t(row) * N + n0 + 8 * c) = v;
+  }
+  __syncwarp();
 }
 
 // Operands of at most kPrefetchBytes together are brought into L2 at kernel start, before the
@@ -224,12 +274,27 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       mbar_wait(&tfull[acc], aph);
       tc::fence_after_sync();
       const int row = mb * kBM + q * 32 + lane;
+      if (BN >= 128 && (vec_ok & 1)) {
+        uint8_t* stage = smem + S * C::kStage + (warp - 2) * 4096;
 #pragma unroll 1
-      for (int cc = h * (BN / 64); cc < (h + 1) * (BN / 64); ++cc) {
-        uint32_t r[32];
-        tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + acc * BN + uint32_t(cc * 32), r);
-        tc::tmem_ld_wait();
-        store_row32(r, row, nb * BN + cc * 32, M, N, scale, bias, out, vec_ok != 0);
+        for (int c64 = 0; c64 < BN / 128; ++c64) {
+          const int col = h * (BN / 2) + c64 * 64;
+          if (nb * BN + col >= N) break;
+          uint32_t r0[32], r1[32];
+          tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + acc * BN + uint32_t(col), r0);
+          tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + acc * BN + uint32_t(col + 32), r1);
+          tc::tmem_ld_wait();
+          store_rows64_staged(r0, r1, mb * kBM + q * 32, lane, nb * BN + col, M, N, scale, bias, (vec_ok & 2) != 0,
+                              out, stage);
+        }
+      } else {
+#pragma unroll 1
+        for (int cc = h * (BN / 64); cc < (h + 1) * (BN / 64); ++cc) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + acc * BN + uint32_t(cc * 32), r);
+          tc::tmem_ld_wait();
+          store_row32(r, row, nb * BN + cc * 32, M, N, scale, bias, out, (vec_ok & 1) != 0);
+        }
       }
       tc::fence_before_sync();
       __syncwarp();
@@ -677,7 +742,7 @@ inline int launch_tc(int M, int N, int K, const uint8_t* x, const uint8_t* w, fl
   if (!ensure_dyn_smem(kern, Cfg<BN>::kSmem)) return kCudaError;
   const int n_tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
-  const int vec_ok = (N % 8 == 0) && aligned16(out);
+  const int vec_ok = ((N % 8 == 0) && aligned16(out) ? 1 : 0) | (aligned16(bias) ? 2 : 0);
   launch_pdl(kern, grid, kThreadsG, Cfg<BN>::kSmem, stream, a, b, M, N, K, scale, scale_ptr, bias, out, vec_ok, x, w);
   return launch_status();
 }

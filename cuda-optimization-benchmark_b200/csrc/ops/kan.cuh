@@ -22,8 +22,8 @@
 // are scaled by powers of two so every value fits fp16; the epilogue undoes them.
 //   1. prep_w_kernel: W' hi/lo planes (one CTA per output row);
 //   2. silu + Cox-de Boor bases of x in fp32, hi/lo planes: for the cubic cases row_scale_kernel and
-//      prep_a2_kernel (a thread per two inputs down a block of rows, reciprocal knot differences
-//      computed once per input), otherwise prep_a_kernel (one CTA per batch row);
+//      prep_a3_kernel (a thread per two inputs down a block of rows, only the four non-zero bases
+//      of each input formed), otherwise prep_a_kernel (one CTA per batch row);
 //   3. gemm_kernel: persistent warp-specialised tcgen05 GEMM (kind::f16, 128 x 128 tiles, TMEM
 //      = [D0a | D0b | D0c | D1], 128-byte-swizzled TMA loads of the four planes in a 3-stage ring,
 //      12 MMAs per stage), fused combine/rescale epilogue writing fp32 rows.
@@ -290,25 +290,10 @@ __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x
 }
 
 // ----------------------------------------------------------------- A planes, column-major form
-// prep_a_kernel gives each batch row to one CTA, so every (row, input) pays the whole Cox-de Boor
-// recurrence with its divisions by knot differences, which depend on the input alone.  The
-// column-major form computes each input's reciprocal knot differences once and reuses them down a
-// block of rows, with every basis step a multiply:
+// prep_a_kernel gives each batch row to one CTA.  For the cubic cases the column-major form instead
+// gives each thread two adjacent inputs down a block of rows (prep_a3_kernel below), after
 //   row_scale_kernel: per row the power-of-two factor that keeps silu and the bases inside fp16
-//     (the same rule as prep_a_kernel), and the row's zero K padding;
-//   prep_a2_kernel: a thread owns two adjacent inputs (i, i + 1) and a block of up to kPrepRows
-//     rows; it writes the hi / lo planes with 4-byte half2 stores (each warp a contiguous 128 bytes
-//     per plane).  The rows per block shrink (prep_rows) until the grid has about three CTAs per SM,
-//     so narrow layers (few inputs) still fill the GPU.
-constexpr int kPrepRows = 32;
-constexpr int kPrepThreads = 128;
-
-inline int prep_rows(int B, int I) {
-  const int64_t xblocks = (I + 2 * kPrepThreads - 1) / (2 * kPrepThreads);
-  int rows = kPrepRows;
-  while (rows > 4 && xblocks * ((B + rows - 1) / rows) < 3 * int64_t(sm_count())) rows /= 2;
-  return rows;
-}
+//     (the same rule as prep_a_kernel), and the row's zero K padding.
 
 // One warp per row.  The amax takes silu with fast intrinsics: the factor is a power of two chosen
 // with a 4x margin below the fp16 maximum (kFp16Safe), so an amax a few ulps low can at most double
@@ -352,57 +337,137 @@ __device__ __forceinline__ void split_store2(float v0, float v1, __half* hi, __h
                                                    __float2half_rn((v1 - __half2float(h1)) * kLoScale));
 }
 
-// grid = (ceil(I / (2 * kPrepThreads)), ceil(B / rows)); I even.  rs from row_scale_kernel.
-template <int NK, int KO>
-__global__ void __launch_bounds__(kPrepThreads) prep_a2_kernel(const float* __restrict__ x,
-                                                               const float* __restrict__ grid, int B, int I,
-                                                               int64_t kp, const float* __restrict__ rs,
-                                                               __half* __restrict__ a_hi,
-                                                               __half* __restrict__ a_lo, int rows) {
+// ------------------------------------------------------------ A planes, sparse cubic form
+// For strictly increasing knots and g[s] <= x < g[s+1], only the cubic bases s-3 .. s can be
+// non-zero, and each is the same two-term expression as in the full recurrence with the exact-zero
+// terms left out (tasks/efficient_kan/reference.py:33-39).  prep_a3_kernel forms those four from
+// the six knots g[s-2 .. s+3] (9 recurrence terms instead of 36, 6 reciprocals instead of 42
+// register-held ones), so a thread needs few registers and the grid can fill the SMs.  The knot
+// values are bit-identical to the full recurrence's with reciprocal knot differences (the same
+// reciprocals, products and sums); only the sign of a zero basis can differ.  A thread owns inputs (i, i + 1); their knots are staged in
+// shared memory as s_g[j][u][t] (input i0 + 2t + u), so the dynamic knot reads of a warp hit 32
+// distinct banks.  The four bases go to their planes through a per-thread shared-memory row
+// (a register array cannot take the dynamic plane index), so the global stores stay one
+// contiguous 128-byte half2 row per warp and plane.
+// A non-finite x gives NaN bases, as the full recurrence does; a column whose knots are not
+// strictly increasing takes the full recurrence (bases_fixed).
+constexpr int kPrep3Threads = 128;
+
+// Rows per CTA: the fewest that fit the whole grid in one wave of resident CTAs (a second, partial
+// wave would run at a fraction of the occupancy).
+inline int prep3_rows(int B, int I, int ctas_per_sm) {
+  const int64_t xblocks = (I + 2 * kPrep3Threads - 1) / (2 * kPrep3Threads);
+  const int64_t wave = int64_t(sm_count()) * (ctas_per_sm > 0 ? ctas_per_sm : 1);
+  const int64_t row_blocks = wave / xblocks > 0 ? wave / xblocks : 1;
+  return int((B + row_blocks - 1) / row_blocks);
+}
+
+__device__ __forceinline__ void split_half(float v, __half* hi, __half* lo) {
+  const __half h = __float2half_rn(v);
+  *hi = h;
+  *lo = __float2half_rn((v - __half2float(h)) * kLoScale);
+}
+
+// The four cubic bases s-3 .. s of x (g[s] <= x < g[s+1]) from the knots gm2..g3 = g[s-2 .. s+3].
+__device__ __forceinline__ void cubic_local(float x, float gm2, float gm1, float g0, float g1, float g2, float g3,
+                                            float (&n)[4]) {
+  const float d0 = 1.0f / __fsub_rn(g1, g0);
+  const float a1 = __fmul_rn(__fsub_rn(g1, x), d0);  // order 1, basis s-1
+  const float b1 = __fmul_rn(__fsub_rn(x, g0), d0);  // order 1, basis s
+  const float e1 = 1.0f / __fsub_rn(g1, gm1), e2 = 1.0f / __fsub_rn(g2, g0);
+  const float c0 = __fmul_rn(__fmul_rn(__fsub_rn(g1, x), e1), a1);  // order 2, basis s-2
+  const float c1 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, gm1), e1), a1),
+                             __fmul_rn(__fmul_rn(__fsub_rn(g2, x), e2), b1));
+  const float c2 = __fmul_rn(__fmul_rn(__fsub_rn(x, g0), e2), b1);
+  const float f1 = 1.0f / __fsub_rn(g1, gm2), f2 = 1.0f / __fsub_rn(g2, gm1), f3 = 1.0f / __fsub_rn(g3, g0);
+  n[0] = __fmul_rn(__fmul_rn(__fsub_rn(g1, x), f1), c0);
+  n[1] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, gm2), f1), c0), __fmul_rn(__fmul_rn(__fsub_rn(g2, x), f2), c1));
+  n[2] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, gm1), f2), c1), __fmul_rn(__fmul_rn(__fsub_rn(g3, x), f3), c2));
+  n[3] = __fmul_rn(__fmul_rn(__fsub_rn(x, g0), f3), c2);
+}
+
+// grid = (ceil(I / (2 * kPrep3Threads)), ceil(B / rows)); I even, x and grid 8-byte aligned.  rs
+// from row_scale_kernel.
+template <int NK>
+__global__ void __launch_bounds__(kPrep3Threads, 6) prep_a3_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ grid, int B, int I,
+                                                                int64_t kp, const float* __restrict__ rs,
+                                                                __half* __restrict__ a_hi,
+                                                                __half* __restrict__ a_lo, int rows) {
+  constexpr int C = NK - 4;
+  __shared__ float s_g[NK][2][kPrep3Threads];
+  __shared__ float2 s_v[NK - 4][kPrep3Threads];  // per-thread basis scratch (dynamic plane index)
+  const int t = threadIdx.x;
+  const int i = 2 * (int(blockIdx.x) * kPrep3Threads + t);
   pdl_begin();  // the row scales are written by row_scale_kernel just before this kernel
-  constexpr int C = NK - KO - 1;
-  const int i = 2 * (int(blockIdx.x) * kPrepThreads + int(threadIdx.x));
   if (i >= I) return;
-  // Knots and reciprocal knot differences of both inputs: rc[u][k-1][j] = 1 / (g[j+k] - g[j]).
-  float g[2][NK], rc[2][KO][NK - 1];
+  // The thread's 2 * NK knots are contiguous (grid 8-byte aligned, i even): NK float2 loads.  Only
+  // this thread reads its s_g column, so no block barrier is needed.
+  bool inc = true;
+  {
+    float gv[2 * NK];
+    const float2* gp = reinterpret_cast<const float2*>(grid + int64_t(i) * NK);
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
+    for (int e = 0; e < NK; ++e) {
+      const float2 v = __ldg(gp + e);
+      gv[2 * e] = v.x;
+      gv[2 * e + 1] = v.y;
+    }
 #pragma unroll
-    for (int j = 0; j < NK; ++j) g[u][j] = __ldg(grid + int64_t(i + u) * NK + j);
-#pragma unroll
-    for (int k = 1; k <= KO; ++k)
-#pragma unroll
-      for (int j = 0; j + k < NK; ++j) rc[u][k - 1][j] = 1.0f / __fsub_rn(g[u][j + k], g[u][j]);
+    for (int e = 0; e < 2 * NK; ++e) {
+      s_g[e % NK][e / NK][t] = gv[e];
+      if (e % NK != 0) inc = inc && gv[e - 1] < gv[e];
+    }
   }
   const int b0 = int(blockIdx.y) * rows;
+#pragma unroll 1
   for (int bb = 0; bb < rows; ++bb) {
     const int b = b0 + bb;
     if (b >= B) break;
     const float f = 1.0f / __ldg(rs + b);  // a power of two: exact
     const float2 xv = *reinterpret_cast<const float2*>(x + int64_t(b) * I + i);
-    float v[2][1 + C];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float xu = u == 0 ? xv.x : xv.y;
-      float bs[NK - 1];
-#pragma unroll
-      for (int j = 0; j < NK - 1; ++j) bs[j] = (xu >= g[u][j] && xu < g[u][j + 1]) ? 1.0f : 0.0f;
-#pragma unroll
-      for (int k = 1; k <= KO; ++k)
-#pragma unroll
-        for (int j = 0; j < NK - 1 - k; ++j) {
-          const float l = __fmul_rn(__fsub_rn(xu, g[u][j]), rc[u][k - 1][j]);
-          const float r = __fmul_rn(__fsub_rn(g[u][j + k + 1], xu), rc[u][k - 1][j + 1]);
-          bs[j] = __fadd_rn(__fmul_rn(l, bs[j]), __fmul_rn(r, bs[j + 1]));
-        }
-      v[u][0] = silu(xu) * f;
-#pragma unroll
-      for (int c = 0; c < C; ++c) v[u][1 + c] = bs[c] * f;
-    }
     __half* hr = a_hi + int64_t(b) * kp + i;
     __half* lr = a_lo + int64_t(b) * kp + i;
+    split_store2(silu(xv.x) * f, silu(xv.y) * f, hr, lr);
+    if (inc) {
+      // The thread's own 2 x C basis values in shared memory (float2 per plane): zeros (NaN for a
+      // non-finite x, as the full recurrence gives), then the four non-zero bases of each input
+      // written at their plane, then read back for coalesced half2 plane stores.
+      const float za = fabsf(xv.x) <= 3.402823466e38f ? 0.0f : __int_as_float(0x7fc00000);
+      const float zb = fabsf(xv.y) <= 3.402823466e38f ? 0.0f : __int_as_float(0x7fc00000);
 #pragma unroll
-    for (int p = 0; p <= C; ++p) split_store2(v[0][p], v[1][p], hr + int64_t(p) * I, lr + int64_t(p) * I);
+      for (int c = 0; c < C; ++c) s_v[c][t] = make_float2(za, zb);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float xu = u == 0 ? xv.x : xv.y;
+        int cnt = 0;
+#pragma unroll
+        for (int j = 0; j < NK; ++j) cnt += xu >= s_g[j][u][t] ? 1 : 0;
+        if (cnt < 1 || cnt > NK - 1) continue;  // outside [g0, g[NK-1]) or NaN: zero (or NaN) bases
+        const int sj = cnt - 1;
+        auto kn = [&](int m) { return s_g[min(max(sj + m, 0), NK - 1)][u][t]; };
+        float n[4];
+        cubic_local(xu, kn(-2), kn(-1), kn(0), kn(1), kn(2), kn(3), n);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int p = sj - 3 + m;  // basis index; invalid ones (outside 0 .. C-1) use clamped knots
+          if (p >= 0 && p < C) reinterpret_cast<float*>(&s_v[p][t])[u] = n[m];
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const float2 v = s_v[c][t];
+        split_store2(v.x * f, v.y * f, hr + int64_t(1 + c) * I, lr + int64_t(1 + c) * I);
+      }
+    } else {
+#pragma unroll 1
+      for (int u = 0; u < 2; ++u) {
+        float bsv[NK - 1];
+        bases_fixed<NK, 3>(u == 0 ? xv.x : xv.y, grid + int64_t(i + u) * NK, bsv);
+#pragma unroll
+        for (int c = 0; c < C; ++c) split_half(bsv[c] * f, hr + int64_t(1 + c) * I + u, lr + int64_t(1 + c) * I + u);
+      }
+    }
   }
 }
 
@@ -594,15 +659,15 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   const int64_t kp = padded_k(I, C);
   launch_pdl(prep_w_kernel, O, 256, 0, stream, wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
   // Column-major form for the cubic cases; its float2 loads of x need I even and x 8-byte aligned.
-  if (K == 3 && (G == 5 || G == 8) && I % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) {
+  if (K == 3 && (G == 5 || G == 8) && I % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0 &&
+      (reinterpret_cast<uintptr_t>(grid) & 7u) == 0) {
     launch_pdl(row_scale_kernel, unsigned((B + kScaleRowsPerCta - 1) / kScaleRowsPerCta), 32 * kScaleRowsPerCta, 0,
                stream, x, B, I, C, kp, rs, a_hi, a_lo);
-    const int rows = prep_rows(B, I);
-    const dim3 pg(unsigned((I + 2 * kPrepThreads - 1) / (2 * kPrepThreads)), unsigned((B + rows - 1) / rows));
-    if (G == 5) launch_pdl(prep_a2_kernel<12, 3>, pg, kPrepThreads, 0, stream, x, grid, B, I, kp,
-                           static_cast<const float*>(rs), a_hi, a_lo, rows);
-    else launch_pdl(prep_a2_kernel<15, 3>, pg, kPrepThreads, 0, stream, x, grid, B, I, kp,
-                    static_cast<const float*>(rs), a_hi, a_lo, rows);
+    auto pk = G == 5 ? prep_a3_kernel<12> : prep_a3_kernel<15>;
+    const int rows = prep3_rows(B, I, resident_ctas_per_sm(pk, kPrep3Threads, 0));
+    const dim3 pg(unsigned((I + 2 * kPrep3Threads - 1) / (2 * kPrep3Threads)), unsigned((B + rows - 1) / rows));
+    launch_pdl(pk, pg, kPrep3Threads, 0, stream, x, grid, B, I, kp, static_cast<const float*>(rs), a_hi, a_lo,
+               rows);
   } else if (G == 5 && K == 3) {
     launch_pdl(prep_a_kernel<12, 3>, B, 256, 0, stream, x, grid, I, C, K, kp, a_hi, a_lo, rs);
   } else if (G == 8 && K == 3) {
