@@ -368,18 +368,27 @@ __device__ __forceinline__ void split_half(float v, __half* hi, __half* lo) {
   *lo = __float2half_rn((v - __half2float(h)) * kLoScale);
 }
 
-// The four cubic bases s-3 .. s of x (g[s] <= x < g[s+1]) from the knots gm2..g3 = g[s-2 .. s+3].
+__device__ __forceinline__ float rcp_approx(float v) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+// The four cubic bases s-3 .. s of x (g[s] <= x < g[s+1]) from the knots gm2..g3 = g[s-2 .. s+3]:
+// the terms of the Cox-de Boor recurrence with reciprocal knot differences (hardware reciprocal,
+// within an ulp of the rounded one), in its order of products and sums.
 __device__ __forceinline__ void cubic_local(float x, float gm2, float gm1, float g0, float g1, float g2, float g3,
                                             float (&n)[4]) {
-  const float d0 = 1.0f / __fsub_rn(g1, g0);
+  const float d0 = rcp_approx(__fsub_rn(g1, g0));
   const float a1 = __fmul_rn(__fsub_rn(g1, x), d0);  // order 1, basis s-1
   const float b1 = __fmul_rn(__fsub_rn(x, g0), d0);  // order 1, basis s
-  const float e1 = 1.0f / __fsub_rn(g1, gm1), e2 = 1.0f / __fsub_rn(g2, g0);
+  const float e1 = rcp_approx(__fsub_rn(g1, gm1)), e2 = rcp_approx(__fsub_rn(g2, g0));
   const float c0 = __fmul_rn(__fmul_rn(__fsub_rn(g1, x), e1), a1);  // order 2, basis s-2
   const float c1 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, gm1), e1), a1),
                              __fmul_rn(__fmul_rn(__fsub_rn(g2, x), e2), b1));
   const float c2 = __fmul_rn(__fmul_rn(__fsub_rn(x, g0), e2), b1);
-  const float f1 = 1.0f / __fsub_rn(g1, gm2), f2 = 1.0f / __fsub_rn(g2, gm1), f3 = 1.0f / __fsub_rn(g3, g0);
+  const float f1 = rcp_approx(__fsub_rn(g1, gm2)), f2 = rcp_approx(__fsub_rn(g2, gm1)),
+              f3 = rcp_approx(__fsub_rn(g3, g0));
   n[0] = __fmul_rn(__fmul_rn(__fsub_rn(g1, x), f1), c0);
   n[1] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, gm2), f1), c0), __fmul_rn(__fmul_rn(__fsub_rn(g2, x), f2), c1));
   n[2] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, gm1), f2), c1), __fmul_rn(__fmul_rn(__fsub_rn(g3, x), f3), c2));
@@ -395,8 +404,9 @@ __global__ void __launch_bounds__(kPrep3Threads, 6) prep_a3_kernel(const float* 
                                                                 __half* __restrict__ a_hi,
                                                                 __half* __restrict__ a_lo, int rows) {
   constexpr int C = NK - 4;
+  static_assert(NK >= 5 && NK <= 16, "the binary search below covers up to 16 knots");
   __shared__ float s_g[NK][2][kPrep3Threads];
-  __shared__ float2 s_v[NK - 4][kPrep3Threads];  // per-thread basis scratch (dynamic plane index)
+  __shared__ uint2 s_w[NK - 4][kPrep3Threads];  // per-thread plane words {hi half2, lo half2}
   const int t = threadIdx.x;
   const int i = 2 * (int(blockIdx.x) * kPrep3Threads + t);
   pdl_begin();  // the row scales are written by row_scale_kernel just before this kernel
@@ -430,19 +440,24 @@ __global__ void __launch_bounds__(kPrep3Threads, 6) prep_a3_kernel(const float* 
     __half* lr = a_lo + int64_t(b) * kp + i;
     split_store2(silu(xv.x) * f, silu(xv.y) * f, hr, lr);
     if (inc) {
-      // The thread's own 2 x C basis values in shared memory (float2 per plane): zeros (NaN for a
-      // non-finite x, as the full recurrence gives), then the four non-zero bases of each input
-      // written at their plane, then read back for coalesced half2 plane stores.
+      // The thread's own C plane words in shared memory (a register array cannot take the
+      // dynamic plane index): zeros (NaN for a non-finite x, as the full recurrence gives), then
+      // the split halves of the four non-zero bases of each input at their plane, then read back
+      // for coalesced half2 plane stores.
       const float za = fabsf(xv.x) <= 3.402823466e38f ? 0.0f : __int_as_float(0x7fc00000);
       const float zb = fabsf(xv.y) <= 3.402823466e38f ? 0.0f : __int_as_float(0x7fc00000);
+      const __half2 z2 = __halves2half2(__float2half_rn(za), __float2half_rn(zb));
+      const uint32_t zw = *reinterpret_cast<const uint32_t*>(&z2);
 #pragma unroll
-      for (int c = 0; c < C; ++c) s_v[c][t] = make_float2(za, zb);
+      for (int c = 0; c < C; ++c) s_w[c][t] = make_uint2(zw, zw);
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
         const float xu = u == 0 ? xv.x : xv.y;
+        // cnt = #{j : g[j] <= x} by binary search (the knots increase strictly); NaN gives 0.
         int cnt = 0;
 #pragma unroll
-        for (int j = 0; j < NK; ++j) cnt += xu >= s_g[j][u][t] ? 1 : 0;
+        for (int step = 8; step >= 1; step >>= 1)
+          if (cnt + step <= NK && s_g[min(cnt + step - 1, NK - 1)][u][t] <= xu) cnt += step;
         if (cnt < 1 || cnt > NK - 1) continue;  // outside [g0, g[NK-1]) or NaN: zero (or NaN) bases
         const int sj = cnt - 1;
         auto kn = [&](int m) { return s_g[min(max(sj + m, 0), NK - 1)][u][t]; };
@@ -451,13 +466,20 @@ __global__ void __launch_bounds__(kPrep3Threads, 6) prep_a3_kernel(const float* 
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
           const int p = sj - 3 + m;  // basis index; invalid ones (outside 0 .. C-1) use clamped knots
-          if (p >= 0 && p < C) reinterpret_cast<float*>(&s_v[p][t])[u] = n[m];
+          if (p >= 0 && p < C) {
+            const float v = n[m] * f;
+            const __half h = __float2half_rn(v);
+            __half* w = reinterpret_cast<__half*>(&s_w[p][t]);
+            w[u] = h;
+            w[2 + u] = __float2half_rn((v - __half2float(h)) * kLoScale);
+          }
         }
       }
 #pragma unroll
       for (int c = 0; c < C; ++c) {
-        const float2 v = s_v[c][t];
-        split_store2(v.x * f, v.y * f, hr + int64_t(1 + c) * I, lr + int64_t(1 + c) * I);
+        const uint2 w = s_w[c][t];
+        *reinterpret_cast<uint32_t*>(hr + int64_t(1 + c) * I) = w.x;
+        *reinterpret_cast<uint32_t*>(lr + int64_t(1 + c) * I) = w.y;
       }
     } else {
 #pragma unroll 1
