@@ -14,8 +14,10 @@
 // a NaN flag, one partial per CTA, the last CTA to finish combines the partials (max is order-free,
 // so the result is exact) and writes scale (and, for the fused linear layer, the GEMM epilogue
 // factor) to device memory.
-// cast_kernel waits for it through programmatic dependent launch and writes the bytes.  Traffic:
-// 2 reads of x and 1 byte written per element.
+// cast_kernel waits for it through programmatic dependent launch and writes the bytes, walking the
+// groups in the reverse of amax_kernel's order so that the part of x still in L2 after the amax
+// pass is read first.  Traffic: 2 reads of x (less what the second finds in L2) and 1 byte written
+// per element.
 #pragma once
 
 #include <cuda_fp8.h>
@@ -203,18 +205,20 @@ __global__ void __launch_bounds__(kThreads) cast_kernel(const void* __restrict__
     for (int k = 0; k < 4; ++k) w[k] = to_e4m3x4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3], scale);
     *reinterpret_cast<uint4*>(q + gi * kGroup) = make_uint4(w[0], w[1], w[2], w[3]);
   };
+  // Groups in reverse order (group groups-1-g at step g): the amax pass read x front to back, so
+  // its last-read lines, still in L2, are the first ones read here.
   int64_t g = t0;
   for (; g + (kUnroll - 1) * stride < groups; g += kUnroll * stride) {  // kUnroll groups in flight
     float v[kUnroll][kGroup];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) load16<kBf16>(x, g + u * stride, v[u]);
+    for (int u = 0; u < kUnroll; ++u) load16<kBf16>(x, groups - 1 - (g + u * stride), v[u]);
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) put(g + u * stride, v[u]);
+    for (int u = 0; u < kUnroll; ++u) put(groups - 1 - (g + u * stride), v[u]);
   }
   for (; g < groups; g += stride) {
     float v[kGroup];
-    load16<kBf16>(x, g, v);
-    put(g, v);
+    load16<kBf16>(x, groups - 1 - g, v);
+    put(groups - 1 - g, v);
   }
   for (int64_t i = groups * kGroup + t0; i < n; i += stride) q[i] = to_e4m3(load1<kBf16>(x, i), scale);
 }

@@ -7,9 +7,9 @@
 //   1. map_kernel: each chunk's affine map y_left = B + A * y_right in fp64 (the lane runs and the
 //      warp composition of rtg::scan_pass, with the slots before a short chunk's start as
 //      identities);
-//   2. carry_kernel: per row, one warp composes the chunk maps from the end of the row (a lane
-//      owns a block of consecutive chunks; a warp scan of the blocks' maps, then each lane walks its
-//      block) and writes the value entering every chunk from the right, starting from y0 = 0, or
+//   2. carry_kernel: per row, one CTA composes the chunk maps from the end of the row (a thread
+//      owns a block of consecutive chunks; a CTA scan of the blocks' maps, then each thread walks
+//      its block) and writes the value entering every chunk from the right, starting from y0 = 0, or
 //      from this rank's carry-in when the row's steps are sharded over ranks; it can also write the
 //      map of the whole row slice;
 //   3. scan_kernel: each chunk re-runs rtg::scan_pass from its exact fp64 carry, so every output
@@ -32,7 +32,7 @@ namespace rtgc {
 
 constexpr int kWarps = 4;  // chunks in flight per CTA, one staging buffer each
 constexpr int kThreads = 32 * kWarps;
-constexpr int kCarryThreads = 128;  // 4 rows per CTA in carry_kernel
+constexpr int kCarryThreads = 256;  // one row per CTA in carry_kernel
 
 struct Map {
   double a, b;  // y_left = b + a * y_right
@@ -146,20 +146,28 @@ __global__ void __launch_bounds__(kCarryThreads) carry_kernel(const Map* __restr
                                                               double* __restrict__ carries,
                                                               Map* __restrict__ slice_out) {
   pdl_begin();
-  const int lane = threadIdx.x & 31;
-  const int64_t row = int64_t(blockIdx.x) * (kCarryThreads / 32) + (threadIdx.x >> 5);
-  if (row >= B) return;
+  __shared__ Map s_warp[kCarryThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
   const Map* m = maps + row * nch;
-  const int64_t per = (nch + 31) / 32;  // chunks per lane block
-  const int64_t k0 = lane * per, k1 = k0 + per < nch ? k0 + per : nch;
-  // Block map: M_{k1-1} o ... o M_{k0} (later k applied after earlier k: y moves leftwards).
+  const int64_t per = (nch + kCarryThreads - 1) / kCarryThreads;  // chunks per thread block
+  const int64_t k0 = threadIdx.x * per < nch ? threadIdx.x * per : nch, k1 = k0 + per < nch ? k0 + per : nch;
+  // Block map: M_{k1-1} o ... o M_{k0} (later k applied after earlier k: y moves leftwards).  The
+  // maps are loaded kUnroll at a time so their loads are in flight together.
+  constexpr int kUnroll = 8;
   double A = 1.0, Bv = 0.0;
-  for (int64_t k = k0; k < k1; ++k) {
-    const Map q = m[k];
-    Bv = fma(q.a, Bv, q.b);
-    A *= q.a;
+  for (int64_t k = k0; k < k1; k += kUnroll) {
+    Map q[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) q[u] = k + u < k1 ? m[k + u] : Map{1.0, 0.0};
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      Bv = fma(q[u].a, Bv, q[u].b);
+      A *= q[u].a;
+    }
   }
-  // Inclusive prefix over lanes: lane l gets G_l o ... o G_0.
+  // Inclusive prefix over the CTA's threads: thread t gets G_t o ... o G_0 (a warp scan, then the
+  // warp totals' exclusive prefix applied first).
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
     const double A2 = __shfl_up_sync(0xffffffffu, A, d);
@@ -169,7 +177,17 @@ __global__ void __launch_bounds__(kCarryThreads) carry_kernel(const Map* __restr
       A *= A2;
     }
   }
-  if (slice_out != nullptr && lane == 31) slice_out[row] = Map{A, Bv};
+  if (lane == 31) s_warp[warp] = Map{A, Bv};
+  __syncthreads();
+  double Pa = 1.0, Pb = 0.0;  // W_{warp-1} o ... o W_0
+  for (int w = 0; w < warp; ++w) {
+    const Map q = s_warp[w];
+    Pb = fma(q.a, Pb, q.b);
+    Pa *= q.a;
+  }
+  Bv = fma(A, Pb, Bv);
+  A *= Pa;
+  if (slice_out != nullptr && threadIdx.x == kCarryThreads - 1) slice_out[row] = Map{A, Bv};
   if (carries == nullptr) return;
   double y0 = 0.0;
   if (slices != nullptr)
@@ -180,15 +198,20 @@ __global__ void __launch_bounds__(kCarryThreads) carry_kernel(const Map* __restr
   // Exclusive prefix applied to y0: the value entering chunk k0.
   double Ae = __shfl_up_sync(0xffffffffu, A, 1), Be = __shfl_up_sync(0xffffffffu, Bv, 1);
   if (lane == 0) {
-    Ae = 1.0;
-    Be = 0.0;
+    Ae = Pa;
+    Be = Pb;
   }
   double y = fma(Ae, y0, Be);
   double* c = carries + row * nch;
-  for (int64_t k = k0; k < k1; ++k) {
-    c[k] = y;
-    const Map q = m[k];
-    y = fma(q.a, y, q.b);
+  for (int64_t k = k0; k < k1; k += kUnroll) {
+    Map q[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) q[u] = k + u < k1 ? m[k + u] : Map{1.0, 0.0};
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (k + u < k1) c[k + u] = y;
+      y = fma(q[u].a, y, q[u].b);
+    }
   }
 }
 
@@ -212,10 +235,8 @@ inline int launch_chunks(bool scan, const float* reward, const void* done, float
 
 inline int launch_carries(const Map* maps, int32_t B, int32_t T, const Map* slices, int world, int rank,
                           double* carries, Map* slice_out, cudaStream_t stream) {
-  const int rows_per_cta = kCarryThreads / 32;
-  const unsigned grid = unsigned((int64_t(B) + rows_per_cta - 1) / rows_per_cta);
-  return launch_pdl(carry_kernel, grid, kCarryThreads, 0, stream, maps, int64_t(B), chunk_count(T), slices, world,
-                    rank, carries, slice_out);
+  return launch_pdl(carry_kernel, unsigned(B), kCarryThreads, 0, stream, maps, int64_t(B), chunk_count(T), slices,
+                    world, rank, carries, slice_out);
 }
 
 struct Ws {
