@@ -1141,9 +1141,12 @@ def sharded_ops(ops, lib, dev, world, rank):
     same = bool(torch.equal(out_s.view(torch.int32), out_w[b0:b1].view(torch.int32)))
     del out_w, ref
     us = graph_ms(lambda: ops.efficient_kan(xks, grid, bw, sw, sc, G, K, out=out_s), dev, world, 5) * 1e3
+    # The pass criterion is the tolerance: the one-GPU call splits its last partial round of tiles
+    # into K halves (their fp32 partials added once more), which a shard's tile count may not.
     entry("efficient_kan B8192 I1024 O1024 G5", us, us_whole,
-          {"within_task_tolerance_of_1gpu": ok_tol, "bit_identical_to_1gpu": same},
-          f"batch rows [{b0}, {b1}) of {Bk} on this rank, weights replicated")
+          {"within_task_tolerance_of_1gpu": ok_tol},
+          f"batch rows [{b0}, {b1}) of {Bk} on this rank, weights replicated",
+          {"bit_identical_to_1gpu": same})
     del xks, out_s, bw, sw, sc, grid
 
     # FP8

@@ -20,8 +20,9 @@
 // D0 is therefore spread round-robin by k-block over three accumulators (a third of the chain
 // each) and summed in the epilogue, which keeps K' = 9216 well inside 1e-5.  Rows of A and of W'
 // are scaled by powers of two so every value fits fp16; the epilogue undoes them.
-//   1. prep_w_kernel: W' hi/lo planes (one CTA per output row);
-//   2. silu + Cox-de Boor bases of x in fp32, hi/lo planes: for the cubic cases row_scale_kernel and
+//   1. prep_wr_kernel: W' hi/lo planes (one CTA per output row), in the same launch the row scales
+//      of the cubic cases (row_scale_rows);
+//   2. silu + Cox-de Boor bases of x in fp32, hi/lo planes: for the cubic cases
 //      prep_a3_kernel (a thread per two inputs down a block of rows, only the four non-zero bases
 //      of each input formed), otherwise prep_a_kernel (one CTA per batch row);
 //   3. gemm_kernel: persistent warp-specialised tcgen05 GEMM (kind::f16, 128 x 128 tiles, TMEM
@@ -65,8 +66,14 @@ inline int64_t padded_k(int I, int C) { return (int64_t(I) * (1 + C) + kBKe - 1)
 // Workspace layout (all 256-byte aligned): A_hi, A_lo [B][Kp] fp16; W_hi, W_lo [O][Kp] fp16;
 // row scales rs[B], col scales cs[O] (fp32 powers of two).
 struct Layout {
-  size_t a_hi, a_lo, w_hi, w_lo, rs, cs, total;
+  size_t a_hi, a_lo, w_hi, w_lo, rs, cs, part, cnt, total;
 };
+
+// The GEMM's last, partial round of tiles is split in two K halves when that evens out the CTAs'
+// work (split_tiles); each half leaves a 128 x 128 fp32 partial tile, and one counter per
+// (split tile, epilogue warp) tells the second half to add the first's.
+constexpr int kEpiWarps = 8;
+inline int max_split_tiles() { return sm_count() / 2; }
 
 inline Layout layout(int B, int I, int O, int C) {
   const int64_t kp = padded_k(I, C);
@@ -83,6 +90,8 @@ inline Layout layout(int B, int I, int O, int C) {
   L.w_lo = take(size_t(O) * kp * 2);
   L.rs = take(size_t(B) * 4);
   L.cs = take(size_t(O) * 4);
+  L.part = take(size_t(2) * max_split_tiles() * kBM * kBN * 4);
+  L.cnt = take(size_t(max_split_tiles()) * kEpiWarps * 4);
   L.total = off;
   return L;
 }
@@ -120,13 +129,10 @@ __device__ __forceinline__ float block_max(float v, float* s_red) {
 // its C contiguous spline weights and the warp's reads are contiguous).  w'(p=0, i) = W_base[o,i];
 // w'(p=1+c, i) = sw[o,i,c] * scaler[o,i] (the fp32 product the reference forms,
 // tasks/efficient_kan/reference.py:45).  Pass 1 finds the row's max |w'|, pass 2 writes the planes.
-__global__ void __launch_bounds__(256) prep_w_kernel(const float* __restrict__ wb, const float* __restrict__ sw,
-                                                     const float* __restrict__ sc, int I, int O, int C, int64_t kp,
-                                                     __half* __restrict__ w_hi, __half* __restrict__ w_lo,
-                                                     float* __restrict__ cs) {
-  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
-  __shared__ float s_red[33];
-  const int o = blockIdx.x;
+__device__ __forceinline__ void prep_w_row(int o, const float* __restrict__ wb, const float* __restrict__ sw,
+                                           const float* __restrict__ sc, int I, int C, int64_t kp,
+                                           __half* __restrict__ w_hi, __half* __restrict__ w_lo,
+                                           float* __restrict__ cs, float* s_red) {
   const float* wbr = wb + int64_t(o) * I;
   const float* swr = sw + int64_t(o) * I * C;
   const float* scr = sc + int64_t(o) * I;
@@ -292,20 +298,18 @@ __global__ void __launch_bounds__(256) prep_a_kernel(const float* __restrict__ x
 // ----------------------------------------------------------------- A planes, column-major form
 // prep_a_kernel gives each batch row to one CTA.  For the cubic cases the column-major form instead
 // gives each thread two adjacent inputs down a block of rows (prep_a3_kernel below), after
-//   row_scale_kernel: per row the power-of-two factor that keeps silu and the bases inside fp16
+//   row_scale_rows: per row the power-of-two factor that keeps silu and the bases inside fp16
 //     (the same rule as prep_a_kernel), and the row's zero K padding.
 
 // One warp per row.  The amax takes silu with fast intrinsics: the factor is a power of two chosen
 // with a 4x margin below the fp16 maximum (kFp16Safe), so an amax a few ulps low can at most double
 // the factor and every scaled value still fits fp16.
 constexpr int kScaleRowsPerCta = 8;
-__global__ void __launch_bounds__(32 * kScaleRowsPerCta) row_scale_kernel(const float* __restrict__ x, int B, int I,
-                                                                          int C, int64_t kp, float* __restrict__ rs,
-                                                                          __half* __restrict__ a_hi,
-                                                                          __half* __restrict__ a_lo) {
-  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+__device__ __forceinline__ void row_scale_rows(int blk, const float* __restrict__ x, int B, int I, int C, int64_t kp,
+                                               float* __restrict__ rs, __half* __restrict__ a_hi,
+                                               __half* __restrict__ a_lo) {
   const int lane = threadIdx.x & 31;
-  const int bi = int(blockIdx.x) * kScaleRowsPerCta + int(threadIdx.x >> 5);
+  const int bi = blk * kScaleRowsPerCta + int(threadIdx.x >> 5);
   if (bi >= B) return;
   const float* xr = x + int64_t(bi) * I;
   float amax = 0.0f;
@@ -328,6 +332,28 @@ __global__ void __launch_bounds__(32 * kScaleRowsPerCta) row_scale_kernel(const 
     a_hi[int64_t(bi) * kp + q] = __float2half_rn(0.0f);
     a_lo[int64_t(bi) * kp + q] = __float2half_rn(0.0f);
   }
+}
+
+// The W' planes and, for the column-major A path, the row scales in one launch (the two are
+// independent): CTAs [0, O) each prepare one output row of W', the scale_ctas CTAs after them
+// kScaleRowsPerCta batch rows' scales each.
+constexpr int kPrepThreads = 256;
+static_assert(kPrepThreads == 32 * kScaleRowsPerCta, "a row-scale CTA is one warp per row");
+__global__ void __launch_bounds__(kPrepThreads) prep_wr_kernel(const float* __restrict__ wb,
+                                                               const float* __restrict__ sw,
+                                                               const float* __restrict__ sc, int I, int O, int C,
+                                                               int64_t kp, __half* __restrict__ w_hi,
+                                                               __half* __restrict__ w_lo, float* __restrict__ cs,
+                                                               const float* __restrict__ x, int B,
+                                                               float* __restrict__ rs, __half* __restrict__ a_hi,
+                                                               __half* __restrict__ a_lo, unsigned* __restrict__ cnt,
+                                                               int n_cnt) {
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  __shared__ float s_red[33];
+  if (blockIdx.x == 0)  // the GEMM's split-tile counters start each call at zero
+    for (int q = threadIdx.x; q < n_cnt; q += blockDim.x) cnt[q] = 0u;
+  if (int(blockIdx.x) < O) prep_w_row(int(blockIdx.x), wb, sw, sc, I, C, kp, w_hi, w_lo, cs, s_red);
+  else row_scale_rows(int(blockIdx.x) - O, x, B, I, C, kp, rs, a_hi, a_lo);
 }
 
 __device__ __forceinline__ void split_store2(float v0, float v1, __half* hi, __half* lo) {
@@ -396,7 +422,7 @@ __device__ __forceinline__ void cubic_local(float x, float gm2, float gm1, float
 }
 
 // grid = (ceil(I / (2 * kPrep3Threads)), ceil(B / rows)); I even, x and grid 8-byte aligned.  rs
-// from row_scale_kernel.
+// from prep_wr_kernel.
 template <int NK>
 __global__ void __launch_bounds__(kPrep3Threads, 6) prep_a3_kernel(const float* __restrict__ x,
                                                                 const float* __restrict__ grid, int B, int I,
@@ -409,7 +435,7 @@ __global__ void __launch_bounds__(kPrep3Threads, 6) prep_a3_kernel(const float* 
   __shared__ uint2 s_w[NK - 4][kPrep3Threads];  // per-thread plane words {hi half2, lo half2}
   const int t = threadIdx.x;
   const int i = 2 * (int(blockIdx.x) * kPrep3Threads + t);
-  pdl_begin();  // the row scales are written by row_scale_kernel just before this kernel
+  pdl_begin();  // the row scales are written by prep_wr_kernel just before this kernel
   if (i >= I) return;
   // The thread's 2 * NK knots are contiguous (grid 8-byte aligned, i even): NK float2 loads.  Only
   // this thread reads its s_g column, so no block barrier is needed.
@@ -504,10 +530,24 @@ __device__ __forceinline__ void tile_coords(int tile, int n_m, int n_n, int& mb,
   nb = r / gm;
 }
 
+// Work unit u of the persistent schedule: tiles 0 .. n_tiles - n_split - 1 whole, then each of the
+// last n_split tiles as two halves of its K blocks (units n_tiles - n_split + 2s + h).
+struct Unit {
+  int tile, kb0, kb1, split, half;  // split: index among the split tiles, -1 for a whole tile
+};
+
+__device__ __forceinline__ Unit unit_of(int u, int n_tiles, int n_split, int nkb) {
+  const int whole = n_tiles - n_split;
+  if (u < whole) return Unit{u, 0, nkb, -1, 0};
+  const int v = u - whole, sp = v >> 1, h = v & 1;
+  return Unit{whole + sp, h ? nkb / 2 : 0, h ? nkb : nkb / 2, sp, h};
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                 const __grid_constant__ CUtensorMap tm_whi, const __grid_constant__ CUtensorMap tm_wlo, int M, int N,
-                int64_t kp, const float* __restrict__ rs, const float* __restrict__ cs, float* __restrict__ out) {
+                int64_t kp, const float* __restrict__ rs, const float* __restrict__ cs, float* __restrict__ out,
+                float* __restrict__ part, unsigned* __restrict__ cnt, int n_split) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
 #if !B200_TCGEN05
   if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
@@ -520,6 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_m = (M + kBM - 1) / kBM, n_n = (N + kBN - 1) / kBN, n_tiles = n_m * n_n;
   const int nkb = int(kp / kBKe);
+  const int n_units = n_tiles + n_split;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -527,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(&tfull, 1);
-    mbar_init(&tempty, 8);
+    mbar_init(&tempty, kEpiWarps);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -548,10 +589,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       uint32_t kb_all = 0;
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const Unit un = unit_of(u, n_tiles, n_split, nkb);
         int mb, nb;
-        tile_coords(tile, n_m, n_n, mb, nb);
-        for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
+        tile_coords(un.tile, n_m, n_n, mb, nb);
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ++kb_all) {
           const uint32_t s = kb_all % kStages, ph = (kb_all / kStages) & 1u;
           mbar_wait(&empty[s], ph ^ 1u);
           mbar_arrive_expect_tx(&full[s], kStage);
@@ -569,10 +611,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id = tc::idesc(kBM, kBN, 0);  // F16 x F16 -> F32
       uint32_t kb_all = 0, it = 0;
       const uint32_t d1 = tmem + kD0Parts * kBN;
-      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
+        const Unit un = unit_of(u, n_tiles, n_split, nkb);
         mbar_wait(&tempty, (it & 1u) ^ 1u);
         tc::fence_after_sync();
-        for (int kb = 0; kb < nkb; ++kb, ++kb_all) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ++kb_all) {
           const uint32_t s = kb_all % kStages, ph = (kb_all / kStages) & 1u;
           mbar_wait(&full[s], ph);
           tc::fence_after_sync();
@@ -581,12 +624,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t alo = tc::sdesc_kmajor_sw128(base + kATile);
           const uint64_t whi = tc::sdesc_kmajor_sw128(base + 2 * kATile);
           const uint64_t wlo = tc::sdesc_kmajor_sw128(base + 2 * kATile + kWTile);
-          const uint32_t d0 = tmem + uint32_t(kb % kD0Parts) * kBN;
+          const int kr = kb - un.kb0;  // k block within the unit
+          const uint32_t d0 = tmem + uint32_t(kr % kD0Parts) * kBN;
 #pragma unroll
           for (int k = 0; k < kBKe / kUmmaK; ++k) {
             const uint64_t adv = uint64_t((k * kUmmaK * 2) >> 4);
-            tc::mma_f16(d0, ahi + adv, whi + adv, id, (kb >= kD0Parts || k != 0) ? 1u : 0u);
-            tc::mma_f16(d1, ahi + adv, wlo + adv, id, (kb | k) != 0 ? 1u : 0u);
+            tc::mma_f16(d0, ahi + adv, whi + adv, id, (kr >= kD0Parts || k != 0) ? 1u : 0u);
+            tc::mma_f16(d1, ahi + adv, wlo + adv, id, (kr | k) != 0 ? 1u : 0u);
             tc::mma_f16(d1, alo + adv, whi + adv, id, 1u);
           }
           tc::mma_commit(&empty[s]);
@@ -596,20 +640,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {  // epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32), column half (w-2)/4
     const int q = warp & 3, h = (warp - 2) >> 2;
+    const uint32_t lane_off = uint32_t(q * 32) << 16;
     uint32_t it = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++it) {
+      const Unit un = unit_of(u, n_tiles, n_split, nkb);
       int mb, nb;
-      tile_coords(tile, n_m, n_n, mb, nb);
+      tile_coords(un.tile, n_m, n_n, mb, nb);
       mbar_wait(&tfull, it & 1u);
       tc::fence_after_sync();
       const int row = mb * kBM + q * 32 + lane;
       const float rsc = row < M ? rs[row] : 0.0f;
       const bool vec_ok = (N % 4) == 0;
-      const int parts = nkb < kD0Parts ? nkb : kD0Parts;  // D0 accumulators written this tile
-#pragma unroll 1
-      for (int cc = h * (kBN / 64); cc < (h + 1) * (kBN / 64); ++cc) {
+      const int nkb_u = un.kb1 - un.kb0;
+      const int parts = nkb_u < kD0Parts ? nkb_u : kD0Parts;  // D0 accumulators written this unit
+      // The unscaled value D0 + D1 * 2^-11 of this lane's row, columns cc*32 .. cc*32+31.
+      auto combine = [&](int cc, float (&v)[32]) {
         uint32_t a[32], c[32], t[32];
-        const uint32_t lane_off = uint32_t(q * 32) << 16;
         tc::tmem_ld32(tmem + lane_off + uint32_t(cc * 32), a);
         tc::tmem_ld32(tmem + lane_off + uint32_t(kD0Parts * kBN + cc * 32), c);
         tc::tmem_ld_wait();
@@ -619,23 +665,69 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) a[j] = __float_as_uint(__uint_as_float(a[j]) + __uint_as_float(t[j]));
         }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(c[j]), kLoUnscale, __uint_as_float(a[j]));
+      };
+      auto store = [&](int cc, const float (&v)[32]) {
         const int n0 = nb * kBN + cc * 32;
-        if (row < M) {
-          float* o = out + int64_t(row) * N + n0;
-          if (vec_ok && n0 + 32 <= N) {
+        if (row >= M) return;
+        float* o = out + int64_t(row) * N + n0;
+        if (vec_ok && n0 + 32 <= N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 w;
+            w.x = v[j + 0] * rsc * cs[n0 + j + 0];
+            w.y = v[j + 1] * rsc * cs[n0 + j + 1];
+            w.z = v[j + 2] * rsc * cs[n0 + j + 2];
+            w.w = v[j + 3] * rsc * cs[n0 + j + 3];
+            *reinterpret_cast<float4*>(o + j) = w;
+          }
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < N) o[j] = v[j] * rsc * cs[n0 + j];
+        }
+      };
+      if (un.split < 0) {
+#pragma unroll 1
+        for (int cc = h * (kBN / 64); cc < (h + 1) * (kBN / 64); ++cc) {
+          float v[32];
+          combine(cc, v);
+          store(cc, v);
+        }
+      } else {
+        // Half of a split tile: leave this half's unscaled values in its partial tile; the half
+        // that counts second adds the other's (fp32 addition commutes, so the bits do not depend
+        // on which half finishes first) and writes the output.
+        float* mine = part + (size_t(2 * un.split + un.half) * kBM + q * 32 + lane) * kBN;
+        const float* other = part + (size_t(2 * un.split + (un.half ^ 1)) * kBM + q * 32 + lane) * kBN;
+#pragma unroll 1
+        for (int cc = h * (kBN / 64); cc < (h + 1) * (kBN / 64); ++cc) {
+          float v[32];
+          combine(cc, v);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(mine + cc * 32 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(&cnt[un.split * kEpiWarps + (warp - 2)], 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == 1u) {
+          __threadfence();
+#pragma unroll 1
+          for (int cc = h * (kBN / 64); cc < (h + 1) * (kBN / 64); ++cc) {
+            float v[32];
+            combine(cc, v);
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
-              float4 v;
-              v.x = fmaf(__uint_as_float(c[j + 0]), kLoUnscale, __uint_as_float(a[j + 0])) * rsc * cs[n0 + j + 0];
-              v.y = fmaf(__uint_as_float(c[j + 1]), kLoUnscale, __uint_as_float(a[j + 1])) * rsc * cs[n0 + j + 1];
-              v.z = fmaf(__uint_as_float(c[j + 2]), kLoUnscale, __uint_as_float(a[j + 2])) * rsc * cs[n0 + j + 2];
-              v.w = fmaf(__uint_as_float(c[j + 3]), kLoUnscale, __uint_as_float(a[j + 3])) * rsc * cs[n0 + j + 3];
-              *reinterpret_cast<float4*>(o + j) = v;
+              const float4 w = __ldcg(reinterpret_cast<const float4*>(other + cc * 32 + j));
+              v[j] += w.x;
+              v[j + 1] += w.y;
+              v[j + 2] += w.z;
+              v[j + 3] += w.w;
             }
-          } else {
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < N)
-                o[j] = fmaf(__uint_as_float(c[j]), kLoUnscale, __uint_as_float(a[j])) * rsc * cs[n0 + j];
+            store(cc, v);
           }
         }
       }
@@ -654,6 +746,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 inline size_t workspace_bytes(int B, int I, int O, int C) { return layout(B, I, O, C).total; }
+
+// Tiles of the last round split into K halves: the rem = n_tiles mod grid tiles of a partial last
+// round, when their 2 * rem halves fit one round (the CTAs' work then differs by half a tile
+// instead of a whole one) and each half keeps enough K blocks.
+inline int split_tiles(int n_tiles, int grid, int nkb) {
+  if (n_tiles <= grid) return 0;
+  const int rem = n_tiles % grid;
+  if (rem == 0 || 2 * rem > grid || rem > max_split_tiles() || nkb < 4 * kD0Parts) return 0;
+  return rem;
+}
 
 // Full op with a caller workspace of workspace_bytes() bytes (no initialisation needed).
 inline int run(const float* x, const float* grid, const float* wb, const float* sw, const float* sc, int32_t G,
@@ -679,12 +781,14 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   float* rs = reinterpret_cast<float*>(w + L.rs);
   float* cs = reinterpret_cast<float*>(w + L.cs);
   const int64_t kp = padded_k(I, C);
-  launch_pdl(prep_w_kernel, O, 256, 0, stream, wb, sw, sc, I, O, C, kp, w_hi, w_lo, cs);
   // Column-major form for the cubic cases; its float2 loads of x need I even and x 8-byte aligned.
-  if (K == 3 && (G == 5 || G == 8) && I % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0 &&
-      (reinterpret_cast<uintptr_t>(grid) & 7u) == 0) {
-    launch_pdl(row_scale_kernel, unsigned((B + kScaleRowsPerCta - 1) / kScaleRowsPerCta), 32 * kScaleRowsPerCta, 0,
-               stream, x, B, I, C, kp, rs, a_hi, a_lo);
+  const bool columns = K == 3 && (G == 5 || G == 8) && I % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0 &&
+                       (reinterpret_cast<uintptr_t>(grid) & 7u) == 0;
+  const int scale_ctas = columns ? (B + kScaleRowsPerCta - 1) / kScaleRowsPerCta : 0;
+  unsigned* cnt = reinterpret_cast<unsigned*>(w + L.cnt);
+  launch_pdl(prep_wr_kernel, unsigned(O + scale_ctas), kPrepThreads, 0, stream, wb, sw, sc, I, O, C, kp, w_hi, w_lo,
+             cs, x, B, rs, a_hi, a_lo, cnt, max_split_tiles() * kEpiWarps);
+  if (columns) {
     auto pk = G == 5 ? prep_a3_kernel<12> : prep_a3_kernel<15>;
     const int rows = prep3_rows(B, I, resident_ctas_per_sm(pk, kPrep3Threads, 0));
     const dim3 pg(unsigned((I + 2 * kPrep3Threads - 1) / (2 * kPrep3Threads)), unsigned((B + rows - 1) / rows));
@@ -706,7 +810,9 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   if (!ensure_dyn_smem(gemm_kernel, kSmem)) return kCudaError;
   const int n_tiles = ((B + kBM - 1) / kBM) * ((O + kBN - 1) / kBN);
   const int grid_ctas = n_tiles < sm_count() ? n_tiles : sm_count();
-  launch_pdl(gemm_kernel, grid_ctas, kThreads, kSmem, stream, m_ahi, m_alo, m_whi, m_wlo, B, O, kp, rs, cs, out);
+  const int n_split = split_tiles(n_tiles, grid_ctas, int(kp / kBKe));
+  launch_pdl(gemm_kernel, grid_ctas, kThreads, kSmem, stream, m_ahi, m_alo, m_whi, m_wlo, B, O, kp, rs, cs, out,
+             reinterpret_cast<float*>(w + L.part), cnt, n_split);
   return launch_status();
 }
 

@@ -8,6 +8,9 @@
 - Inputs with |silu(x)| far beyond the fp16 range (the row scaling path).
 - The row-major A-plane preparation (odd I, or x not 8-byte aligned), beside the column-major one
   the cubic cases take otherwise.
+- A shape whose GEMM tiles leave a partial last round (168 tiles on 148 SMs), so its last 20 tiles
+  run as two K halves whose partial tiles are added: every row against the fp64 oracle, and three
+  calls bit-identical (the per-call counters start at zero each call).
 """
 import numpy as np
 import pytest
@@ -109,3 +112,17 @@ def test_row_major_prep_path(lib, I, shift):
     ref = exact.efficient_kan(s)["out"]
     bad, worst = exact.within(out.double().cpu().numpy(), ref, ATOL, RTOL)
     assert bad == 0, worst
+
+
+def test_split_tail_tiles(lib):
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n_tiles = sms + 20  # O = 1024 gives 8 column tiles per 128-row block
+    B = 128 * ((n_tiles + 7) // 8)
+    s = inputs.task_inputs("efficient_kan", {"B": B, "I": 64, "O": 1024}, 21)
+    outs = [_run_async(lib, s) for _ in range(3)]
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int32), outs[0].view(torch.int32))
+    ref = exact.efficient_kan(s)["out"]
+    bad, worst = exact.within(outs[0].double().cpu().numpy(), ref, ATOL, RTOL)
+    assert bad == 0, worst
+    assert pkg().load().b200_device_fault() == 0
