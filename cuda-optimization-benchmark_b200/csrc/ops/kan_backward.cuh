@@ -235,6 +235,59 @@ __device__ __forceinline__ void bases_recip(float x, const float (&g)[NK], const
   }
 }
 
+// The four cubic bases s-3 .. s of x (g[s] <= x < g[s+1]) and, with kDeriv, their derivatives,
+// from the knots kn[0..6) = g[s-2 .. s+3]: the two-term steps of the recurrence (and of its
+// derivative, as bases_recip carries it) restricted to the bases that can be non-zero, on hardware
+// reciprocals of the knot differences.
+template <bool kDeriv>
+__device__ __forceinline__ void cubic_dual(float x, const float (&kn)[6], float (&n)[4], float (&dn)[4]) {
+  float N[4] = {1.0f, 0.0f, 0.0f, 0.0f}, D[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int k = 1; k <= 3; ++k) {
+    float Nn[4] = {0.0f, 0.0f, 0.0f, 0.0f}, Dn[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int m = 0; m <= k; ++m) {  // basis s - k + m of order k
+      float v = 0.0f, dv = 0.0f;
+      if (m >= 1) {  // (x - g[j]) / (g[j+k] - g[j]) * b[j],  j = s - k + m
+        const float il = kan::rcp_approx(kn[m + 2] - kn[m - k + 2]);
+        const float l = (x - kn[m - k + 2]) * il;
+        v = l * N[m - 1];
+        if (kDeriv) dv = il * N[m - 1] + l * D[m - 1];
+      }
+      if (m <= k - 1) {  // (g[j+k+1] - x) / (g[j+k+1] - g[j+1]) * b[j+1]
+        const float ir = kan::rcp_approx(kn[m + 3] - kn[m - k + 3]);
+        const float r = (kn[m + 3] - x) * ir;
+        v = m >= 1 ? v + r * N[m] : r * N[m];
+        if (kDeriv) dv = dv - ir * N[m] + r * D[m];
+      }
+      Nn[m] = v;
+      Dn[m] = dv;
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      N[m] = Nn[m];
+      D[m] = Dn[m];
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    n[m] = N[m];
+    dn[m] = D[m];
+  }
+}
+
+// Knot interval of x in a thread's knot column col[j * stride] (strictly increasing knots): the
+// count of knots <= x, by binary search (NaN gives 0).
+template <int NK>
+__device__ __forceinline__ int knots_le(float x, const float* col, int stride) {
+  static_assert(NK <= 16, "the binary search covers up to 16 knots");
+  int cnt = 0;
+#pragma unroll
+  for (int step = 8; step >= 1; step >>= 1)
+    if (cnt + step <= NK && col[min(cnt + step - 1, NK - 1) * stride] <= x) cnt += step;
+  return cnt;
+}
+
 __host__ __device__ constexpr int at_tile_rows(int nk) { return nk > 0 ? 64 : kTile; }
 inline size_t at_tile_smem(int C, int nk) {
   return size_t(1 + C) * kTile * (at_tile_rows(nk) + 1) * sizeof(float);
@@ -262,20 +315,55 @@ __global__ void __launch_bounds__(kTile * kTileRows) at_split_kernel(const float
   const int i0 = blockIdx.x * kTile, b0 = blockIdx.y * kW;
   const int i = i0 + tx;
   const int nk = C + K + 1;
-  constexpr int NKr = NK > 0 ? NK : 2, KOr = KO > 0 ? KO : 1;
-  float gr[NKr], rk[KOr][NKr];
-  if (NK > 0 && i < I) load_knots<NKr, KOr>(grid + int64_t(i) * nk, gr, rk);
+  constexpr int NKr = NK > 0 ? NK : 2;
+  // Cubic forms: the tile's knots in shared memory, column tx = input i0 + tx (the tile's 8 thread
+  // rows read the same column: broadcasts); only the four non-zero bases of each x are formed.
+  __shared__ float s_kn[NKr][kTile];
+  __shared__ int s_inc[kTile];
+  if (NK > 0 && ty == 0) {
+    bool inc = true;
+    float prev = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NKr; ++j) {
+      const float g = i < I ? __ldg(grid + int64_t(i) * nk + j) : 0.0f;
+      s_kn[j][tx] = g;
+      if (j > 0) inc = inc && prev < g;
+      prev = g;
+    }
+    s_inc[tx] = inc ? 1 : 0;
+  }
+  if (NK > 0) __syncthreads();
   for (int y = ty; y < kW; y += kTileRows) {
     const int b = b0 + y;
     const bool ok = i < I && b < B;
     const float xv = ok ? x[int64_t(b) * I + i] : 0.0f;
     s_t[(0 * kTile + tx) * (kW + 1) + y] = ok ? kan::silu(xv) : 0.0f;
     if (NK > 0) {
-      float bs[NKr];
-      if (ok) bases_recip<NKr, KOr, false>(xv, gr, rk, bs, nullptr);
+      constexpr int Cc = NK > 0 ? NK - 4 : 1;
+      if (!ok || s_inc[tx]) {
+        // Zeros (NaN for a non-finite x, as the full recurrence gives), then the four bases.
+        const float z = fabsf(xv) <= 3.402823466e38f ? 0.0f : __int_as_float(0x7fc00000);
 #pragma unroll
-      for (int c = 0; c < (NK > 0 ? NK - KO - 1 : 1); ++c)
-        s_t[((1 + c) * kTile + tx) * (kW + 1) + y] = ok ? bs[c] : 0.0f;
+        for (int c = 0; c < Cc; ++c) s_t[((1 + c) * kTile + tx) * (kW + 1) + y] = z;
+        const int cnt = ok ? knots_le<NKr>(xv, &s_kn[0][tx], kTile) : 0;
+        if (cnt >= 1 && cnt <= NK - 1) {
+          const int sj = cnt - 1;
+          float kv[6], nb[4], dnb[4];
+#pragma unroll
+          for (int o = 0; o < 6; ++o) kv[o] = s_kn[min(max(sj - 2 + o, 0), NK - 1)][tx];
+          cubic_dual<false>(xv, kv, nb, dnb);
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const int c = sj - 3 + m;  // invalid ones (outside 0 .. C-1) used clamped knots
+            if (c >= 0 && c < Cc) s_t[((1 + c) * kTile + tx) * (kW + 1) + y] = nb[m];
+          }
+        }
+      } else {  // knots not strictly increasing: the full recurrence
+        float bs[NKr];
+        kan::bases_fixed<NKr, 3>(xv, grid + int64_t(i) * nk, bs);
+#pragma unroll
+        for (int c = 0; c < Cc; ++c) s_t[((1 + c) * kTile + tx) * (kW + 1) + y] = bs[c];
+      }
     } else {
       float g[kMaxKnots], bs[kMaxKnots];
       if (ok) {
@@ -340,10 +428,20 @@ __global__ void __launch_bounds__(kGradThreads) grad_x_kernel(const float* __res
   const int nk = C + K + 1;
   const int64_t nkp = int64_t(I) * (1 + C);
   constexpr int NKr = NK > 0 ? NK : 2, KOr = KO > 0 ? KO : 1;
-  float gr[NKr], rk[KOr][NKr];
+  // Cubic forms: this thread's knot column in shared memory (only this thread reads it, so no
+  // barrier), and only the four non-zero bases' derivatives of each x.
+  __shared__ float s_kn[NKr][kGradThreads];
+  bool inc = true;
   float g[NK > 0 ? 1 : kMaxKnots];
   if (NK > 0) {
-    load_knots<NKr, KOr>(grid + int64_t(i) * nk, gr, rk);
+    float prev = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NKr; ++j) {
+      const float v = __ldg(grid + int64_t(i) * nk + j);
+      s_kn[j][threadIdx.x] = v;
+      if (j > 0) inc = inc && prev < v;
+      prev = v;
+    }
   } else {
     for (int j = 0; j < nk; ++j) g[j] = grid[int64_t(i) * nk + j];
   }
@@ -356,10 +454,26 @@ __global__ void __launch_bounds__(kGradThreads) grad_x_kernel(const float* __res
     const float dsilu = s * (1.0f + xv * (1.0f - s));
     const float* row = ga + b * nkp + i;
     float acc = row[0] * dsilu;
-    if (NK > 0) {
-      float bs[NKr], dbs[NKr];
-      bases_recip<NKr, KOr, true>(xv, gr, rk, bs, dbs);
+    if (NK > 0 && inc) {
+      // Zero derivative outside [g0, g[NK-1]); NaN for a non-finite x, as the full recurrence.
+      if (!(fabsf(xv) <= 3.402823466e38f)) acc = __int_as_float(0x7fc00000);
+      const int cnt = knots_le<NKr>(xv, &s_kn[0][threadIdx.x], kGradThreads);
+      if (cnt >= 1 && cnt <= NK - 1) {
+        const int sj = cnt - 1;
+        float kv[6], nb[4], dnb[4];
 #pragma unroll
+        for (int o = 0; o < 6; ++o) kv[o] = s_kn[min(max(sj - 2 + o, 0), NK - 1)][threadIdx.x];
+        cubic_dual<true>(xv, kv, nb, dnb);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int c = sj - 3 + m;
+          if (c >= 0 && c < NKr - KOr - 1) acc = fmaf(row[int64_t(1 + c) * I], dnb[m], acc);
+        }
+      }
+    } else if (NK > 0) {  // knots not strictly increasing: the full recurrence (rare; local arrays)
+      float gk[NKr], bs[NKr], dbs[NKr];
+      for (int j = 0; j < NKr; ++j) gk[j] = s_kn[j][threadIdx.x];
+      bases_dual(xv, gk, NKr, KOr, bs, dbs);
       for (int c = 0; c < NKr - KOr - 1; ++c) acc = fmaf(row[int64_t(1 + c) * I], dbs[c], acc);
     } else {
       float bs[kMaxKnots], dbs[kMaxKnots];

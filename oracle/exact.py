@@ -350,7 +350,7 @@ def efficient_kan_backward(inp, grad_out, rows=None):
     gw_base_abs = np.abs(G).T @ np.abs(silu)
     bflat = bases.reshape(B, I * C)
     gw_spl = (G.T @ bflat).reshape(O, I, C)
-    gw_spl_abs = (np.abs(G).T @ bflat).reshape(O, I, C)
+    gw_spl_abs = (np.abs(G).T @ np.abs(bflat)).reshape(O, I, C)  # bases can be negative on unordered knots
     return {"grad_x": grad_x, "grad_base_weight": gw_base, "grad_spline_weight": gw_spl * sc[:, :, None],
             "grad_spline_scaler": (gw_spl * sw).sum(axis=2),
             "grad_x_abs": grad_x_abs, "grad_base_weight_abs": gw_base_abs,

@@ -12,7 +12,9 @@ GPU, through the C ABI: every gradient against the oracle within 2e-5 times the 
 magnitudes plus 1e-6 (the two GEMMs run on split-fp16 tensor-core products, 22 significant bits,
 with fp32 accumulation), on the golden cases, ragged shapes (B, I, O not multiples of 32 or 64,
 G = 5, 8 and K = 2), each gradient requested alone, the BASELINE.json KAN size (grad_x on a row
-subset, the weight gradients in full), and through torch.autograd (KANLinearFunction).
+subset, the weight gradients in full), knot grids that are not uniform and for a few inputs not
+increasing (the sparse-basis kernels and their full-recurrence fallback), and through
+torch.autograd (KANLinearFunction).
 """
 import hashlib
 import json
@@ -116,6 +118,17 @@ def test_baseline_size(ops):
     got = run(ops, s, go)
     rows = np.random.default_rng(0).choice(B, size=256, replace=False)
     check(got, exact.efficient_kan_backward(s, go, rows=rows), rows=rows)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("G", [5, 8])
+def test_uneven_and_unordered_knots(ops, G):
+    from test_kan_gpu import uneven_grid
+    case = {"B": 130, "I": 64, "O": 40, "grid_size": G, "spline_order": 3, "x_range": 1.6}
+    s = inputs.task_inputs("efficient_kan", case, 41 + G)
+    s["grid"] = uneven_grid(64, G, 3, 17 + G)
+    go = torch.randn(130, 40, generator=torch.Generator().manual_seed(G))
+    check(run(ops, s, go), exact.efficient_kan_backward(s, go))
 
 
 @pytest.mark.gpu

@@ -8,6 +8,8 @@
 - Inputs with |silu(x)| far beyond the fp16 range (the row scaling path).
 - The row-major A-plane preparation (odd I, or x not 8-byte aligned), beside the column-major one
   the cubic cases take otherwise.
+- Knot grids that are not uniform, and for a few inputs not increasing (the sparse-basis A planes
+  and their full-recurrence fallback), against the fp64 oracle.
 - A shape whose GEMM tiles leave a partial last round (168 tiles on 148 SMs), so its last 20 tiles
   run as two K halves whose partial tiles are added: every row against the fp64 oracle, and three
   calls bit-identical (the per-call counters start at zero each call).
@@ -126,3 +128,26 @@ def test_split_tail_tiles(lib):
     bad, worst = exact.within(outs[0].double().cpu().numpy(), ref, ATOL, RTOL)
     assert bad == 0, worst
     assert pkg().load().b200_device_fault() == 0
+
+
+def uneven_grid(I, G, K, seed):
+    """Per-input knots: sorted uniform draws on [-1.5, 1.5]; inputs 3 and 10 get two middle knots
+    swapped (a decreasing pair), which the kernels meet with the full recurrence."""
+    g = torch.Generator().manual_seed(seed)
+    knots = torch.sort(torch.rand(I, G + 2 * K + 1, generator=g) * 3.0 - 1.5, dim=1).values
+    for i in (3, 10):
+        if i < I:
+            m = knots.shape[1] // 2
+            knots[i, m], knots[i, m + 1] = knots[i, m + 1].clone(), knots[i, m].clone()
+    return knots.contiguous()
+
+
+@pytest.mark.parametrize("G", [5, 8])
+def test_uneven_and_unordered_knots(lib, G):
+    s = inputs.task_inputs("efficient_kan", {"B": 96, "I": 64, "O": 70, "grid_size": G, "spline_order": 3,
+                                             "x_range": 1.6}, 31 + G)
+    s["grid"] = uneven_grid(64, G, 3, 7 + G)
+    out = _run_async(lib, s)
+    ref = exact.efficient_kan(s)["out"]
+    bad, worst = exact.within(out.double().cpu().numpy(), ref, ATOL, RTOL)
+    assert bad == 0, worst
