@@ -461,6 +461,8 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+constexpr int kMaxSplit = 8;  // CTAs per cluster of the small-M kernel (the portable cluster size)
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -595,15 +597,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int j = 0; j < BNX; ++j) acc[j] = 0.f;
     const uint32_t base = smem_addr(part + r * BNX);
-    for (uint32_t k = 0; k < SK; ++k) {  // rank order: the same sum on every call
-      const uint32_t src = map_cluster_smem(base, k);
+    // 16 columns at a time: the loads from every rank's partial tile are issued together (their
+    // distributed shared memory round trips overlap), then added in rank order (the same sum on
+    // every call).
 #pragma unroll
-      for (int j = 0; j < BNX; j += 4) {
-        const float4 t = ld_cluster_f4(src + uint32_t(j) * 4u);
-        acc[j] += t.x;
-        acc[j + 1] += t.y;
-        acc[j + 2] += t.z;
-        acc[j + 3] += t.w;
+    for (int j0 = 0; j0 < BNX; j0 += 16) {
+      constexpr int kQ = BNX < 16 ? BNX / 4 : 4;
+      float4 t[kMaxSplit][kQ];
+#pragma unroll
+      for (int k = 0; k < kMaxSplit; ++k) {
+        if (uint32_t(k) < SK) {
+          const uint32_t src = map_cluster_smem(base, uint32_t(k)) + uint32_t(j0) * 4u;
+#pragma unroll
+          for (int q = 0; q < kQ; ++q) t[k][q] = ld_cluster_f4(src + uint32_t(q) * 16u);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kMaxSplit; ++k) {
+        if (uint32_t(k) < SK) {
+#pragma unroll
+          for (int q = 0; q < kQ; ++q) {
+            acc[j0 + 4 * q] += t[k][q].x;
+            acc[j0 + 4 * q + 1] += t[k][q].y;
+            acc[j0 + 4 * q + 2] += t[k][q].z;
+            acc[j0 + 4 * q + 3] += t[k][q].w;
+          }
+        }
       }
     }
     if (n < N) {
@@ -765,7 +784,7 @@ inline int launch_tc256(int M, int N, int K, const uint8_t* x, const uint8_t* w,
 inline int small_split(int N, int K) {
   const int n_tiles = (N + kBM - 1) / kBM, nkb = (K + kBK - 1) / kBK;
   int sk = sm_count() / n_tiles;
-  if (sk > 8) sk = 8;
+  if (sk > kMaxSplit) sk = kMaxSplit;
   if (sk > nkb) sk = nkb;
   return sk < 1 ? 1 : sk;
 }
