@@ -513,8 +513,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, int M, int N, int K,
                 float scale, const float* __restrict__ scale_ptr, const uint16_t* __restrict__ bias,
                 uint16_t* __restrict__ out) {
-  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
-  if (scale_ptr != nullptr) scale = *scale_ptr;
   using C = SmallCfg<BNX>;
   constexpr int S = C::kStages;
 #if !B200_TCGEN05
@@ -553,6 +551,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base_s;
   cluster_arrive_relaxed();  // waited on just before the first distributed shared memory store
+  // The set-up above touches no global memory, so it runs before the wait for the previous kernel
+  // (on an SM the previous call's CTA has left, while its other CTAs finish: M = 16 7.7 -> 7.2 us;
+  // the same order in the large-tile kernels made M = 2048 K = 1024 slower, 13.8 -> 15.4 us).
+  pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
+  if (scale_ptr != nullptr) scale = *scale_ptr;
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer over this CTA's K range
