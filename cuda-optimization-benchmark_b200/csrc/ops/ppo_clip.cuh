@@ -638,12 +638,7 @@ template <bool kVec, bool kEnt>
 inline void launch_loss(const float* cur, const float* old, const float* adv, const float* ent, int64_t n,
                         const Clip& clip, ulonglong2* recs, Control* ctl, float* out, cudaStream_t stream) {
   auto kern = loss_kernel<kVec, kEnt>;
-  // The whole resident wave (chunk c on CTA c mod grid): the SMs' chunk counts then differ by at
-  // most one (1000 chunks: 6 or 7 per SM), where equal chunk counts per CTA leave some SMs with an
-  // extra CTA's worth (500 CTAs of 2 chunks: 6 or 8 per SM).
-  const int64_t wave = int64_t(sm_count()) * resident_ctas_per_sm(kern, kThreads, 0);
-  const int64_t chunks = num_chunks(n);
-  const int grid = int(chunks < 1 ? 1 : (chunks < wave ? chunks : wave));
+  const int grid = balanced_grid(num_chunks(n), resident_ctas_per_sm(kern, kThreads, 0));
   launch_pdl(kern, grid, kThreads, 0, stream, cur, old, adv, ent, n, clip, recs, ctl, inv_count(n), out);
 }
 
