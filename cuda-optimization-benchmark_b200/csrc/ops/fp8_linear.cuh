@@ -346,6 +346,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 // each one 256-row TMA box per stage, the two fp32 accumulators fill all 512 TMEM columns (one
 // tile at a time; the MMAs of the next tile wait for the epilogue), and eight epilogue warps
 // drain them, two per TMEM lane quarter (warps 2-5 the upper 128 rows, warps 6-9 the lower).
+// Each epilogue thread reads and rounds its whole 256-column row (bias from shared memory, staged
+// there while the MMAs run), releases TMEM, and only then stores, through the staging area, while
+// the next tile's MMAs run: the next tile waits for the accumulator reads, not for the stores
+// (16384 x 28672 x 8192: about 8 % faster, interleaved runs on one box).
 constexpr int kBM2 = 256;          // rows of x per tile (two UMMAs of 128)
 constexpr int kBN2 = 256;          // columns (rows of w) per tile
 constexpr int kThreads2 = 320;     // warp 0 loads, warp 1 issues MMAs, warps 2-9 epilogue
@@ -355,7 +359,8 @@ struct Cfg2 {
   static constexpr int kStage = kATile + kBTile;  // 64 KB
   static constexpr int kStages = (200 * 1024) / kStage;
   static constexpr int kTmemCols = 512;
-  static constexpr int kSmem = kStages * kStage + 1024;
+  static constexpr int kStageOut = 8 * 4096;  // per-epilogue-warp staging of 32 rows x 64 columns
+  static constexpr int kSmem = kStages * kStage + kStageOut + 1024;
 };
 
 __global__ void __launch_bounds__(kThreads2, 1)
@@ -374,6 +379,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[S], empty[S], tfull, tempty;
   __shared__ uint32_t tmem_base_s;
+  __shared__ uint32_t s_bias[2][kBN2 / 2];  // a tile's bias as bf16 pairs, by tile parity
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_m = (M + kBM2 - 1) / kBM2, n_n = (N + kBN2 - 1) / kBN2, n_tiles = n_m * n_n;
@@ -448,23 +454,69 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
   } else {  // epilogue warps 2..9: warp w reads TMEM lanes of quarter w % 4; w < 6: D0, else D1
     const int q = warp & 3, half = warp < 6 ? 0 : 1;
+    const bool staged = (vec_ok & 1) != 0;
+    uint8_t* stage = smem + S * C::kStage + (warp - 2) * 4096;
+    const int et = int(threadIdx.x) - 64;  // 0 .. 255 over the epilogue warps
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
       int mb, nb;
       tile_coords(tile, n_m, n_n, mb, nb);
+      const int n0 = nb * kBN2;
+      if (staged) {
+        // The tile's bias into shared memory while its MMAs run (one pair per thread of the first
+        // 128); the epilogue warps' barrier makes it visible, and the parity buffers keep a fast
+        // warp's next tile from overwriting what a slow warp still reads.
+        if (et < kBN2 / 2) {
+          const int c = n0 + 2 * et;
+          uint32_t v = 0u;
+          if (c < N)
+            v = (vec_ok & 2) ? __ldg(reinterpret_cast<const uint32_t*>(bias + c))
+                             : uint32_t(__ldg(bias + c)) | (uint32_t(__ldg(bias + c + 1)) << 16);
+          s_bias[it & 1u][et] = v;
+        }
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
       if (!mbar_wait(&tfull, it & 1u)) break;
       tc::fence_after_sync();
       const int row = mb * kBM2 + half * 128 + q * 32 + lane;
+      if (staged) {
+        // Read and round the whole accumulator row first, then free TMEM for the next tile's MMAs,
+        // then store through the staging area while they run.
+        uint32_t pk[kBN2 / 2];
+#pragma unroll
+        for (int cc = 0; cc < kBN2 / 32; ++cc) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(half * 256 + cc * 32), r);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t bw = s_bias[it & 1u][cc * 16 + j];
+            pk[cc * 16 + j] = pack_bf16x2(fmaf(__uint_as_float(r[2 * j]), scale, __uint_as_float(bw << 16)),
+                                          fmaf(__uint_as_float(r[2 * j + 1]), scale, __uint_as_float(bw & 0xffff0000u)));
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty);
+#pragma unroll
+        for (int b = 0; b < kBN2 / 64; ++b) {
+          uint32_t pb[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) pb[j] = pk[32 * b + j];
+          if (n0 + 64 * b < N) store_packed64_staged(pb, mb * kBM2 + half * 128 + q * 32, lane, n0 + 64 * b, M, N, out, stage);
+        }
+      } else {
 #pragma unroll 1
-      for (int cc = 0; cc < kBN2 / 32; ++cc) {
-        uint32_t r[32];
-        tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(half * 256 + cc * 32), r);
-        tc::tmem_ld_wait();
-        store_row32(r, row, nb * kBN2 + cc * 32, M, N, scale, bias, out, vec_ok != 0);
+        for (int cc = 0; cc < kBN2 / 32; ++cc) {
+          uint32_t r[32];
+          tc::tmem_ld32(tmem + (uint32_t(q * 32) << 16) + uint32_t(half * 256 + cc * 32), r);
+          tc::tmem_ld_wait();
+          store_row32(r, row, n0 + cc * 32, M, N, scale, bias, out, false);
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty);
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty);
     }
   }
   tc::fence_before_sync();
@@ -816,7 +868,7 @@ inline int launch_tc256(int M, int N, int K, const uint8_t* x, const uint8_t* w,
   if (!ensure_dyn_smem(gemm256_kernel, Cfg2::kSmem)) return kCudaError;
   const int n_tiles = ((M + kBM2 - 1) / kBM2) * ((N + kBN2 - 1) / kBN2);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
-  const int vec_ok = (N % 8 == 0) && aligned16(out);
+  const int vec_ok = ((N % 8 == 0) && aligned16(out) ? 1 : 0) | (aligned16(bias) ? 2 : 0);
   launch_pdl(gemm256_kernel, grid, kThreads2, Cfg2::kSmem, stream, a, b, M, N, K, scale, scale_ptr, bias, out,
              vec_ok, x, w);
   return launch_status();
