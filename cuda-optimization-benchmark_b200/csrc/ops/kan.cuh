@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                 const __grid_constant__ CUtensorMap tm_whi, const __grid_constant__ CUtensorMap tm_wlo, int M, int N,
                 int64_t kp, const float* __restrict__ rs, const float* __restrict__ cs, float* __restrict__ out,
-                float* __restrict__ part, unsigned* __restrict__ cnt, int n_split) {
+                float* __restrict__ part, unsigned* __restrict__ cnt, int n_split, int vec_ok) {
   pdl_begin();  // launched with PDL: wait for the previous kernel, let the next one queue
 #if !B200_TCGEN05
   if (threadIdx.x == 0) atomicOr(&g_b200_fault, kFaultNoTensorCore);
@@ -649,8 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&tfull, it & 1u);
       tc::fence_after_sync();
       const int row = mb * kBM + q * 32 + lane;
-      const float rsc = row < M ? rs[row] : 0.0f;
-      const bool vec_ok = (N % 4) == 0;
+      const float rsc = row < M ? rs[row] : 0.0f;  // vec_ok: N % 4 == 0 and out 16-byte aligned
       const int nkb_u = un.kb1 - un.kb0;
       const int parts = nkb_u < kD0Parts ? nkb_u : kD0Parts;  // D0 accumulators written this unit
       // The unscaled value D0 + D1 * 2^-11 of this lane's row, columns cc*32 .. cc*32+31.
@@ -812,7 +811,7 @@ inline int run(const float* x, const float* grid, const float* wb, const float* 
   const int grid_ctas = n_tiles < sm_count() ? n_tiles : sm_count();
   const int n_split = split_tiles(n_tiles, grid_ctas, int(kp / kBKe));
   launch_pdl(gemm_kernel, grid_ctas, kThreads, kSmem, stream, m_ahi, m_alo, m_whi, m_wlo, B, O, kp, rs, cs, out,
-             reinterpret_cast<float*>(w + L.part), cnt, n_split);
+             reinterpret_cast<float*>(w + L.part), cnt, n_split, (O % 4 == 0 && aligned16(out)) ? 1 : 0);
   return launch_status();
 }
 

@@ -520,7 +520,8 @@ inline int gemm(const __half* a_hi, const __half* a_lo, int M, const __half* w_h
   const int n_tiles = ((M + kan::kBM - 1) / kan::kBM) * ((N + kan::kBN - 1) / kan::kBN);
   const int grid = n_tiles < sm_count() ? n_tiles : sm_count();
   return launch_pdl(kan::gemm_kernel, grid, kan::kThreads, kan::kSmem, stream, m_ahi, m_alo, m_whi, m_wlo, M, N, kp,
-                    rs, cs, out, static_cast<float*>(nullptr), static_cast<unsigned*>(nullptr), 0);
+                    rs, cs, out, static_cast<float*>(nullptr), static_cast<unsigned*>(nullptr), 0,
+                    (N % 4 == 0 && aligned16(out)) ? 1 : 0);
 }
 
 inline size_t workspace_bytes(int B, int I, int O, int C) { return layout(B, I, O, C).total; }

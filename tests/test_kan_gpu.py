@@ -8,6 +8,7 @@
 - Inputs with |silu(x)| far beyond the fp16 range (the row scaling path).
 - The row-major A-plane preparation (odd I, or x not 8-byte aligned), beside the column-major one
   the cubic cases take otherwise.
+- An output buffer that is not 16-byte aligned (the GEMM epilogue's scalar stores).
 - Knot grids that are not uniform, and for a few inputs not increasing (the sparse-basis A planes
   and their full-recurrence fallback), against the fp64 oracle.
 - A shape whose GEMM tiles leave a partial last round (168 tiles on 148 SMs), so its last 20 tiles
@@ -150,4 +151,20 @@ def test_uneven_and_unordered_knots(lib, G):
     out = _run_async(lib, s)
     ref = exact.efficient_kan(s)["out"]
     bad, worst = exact.within(out.double().cpu().numpy(), ref, ATOL, RTOL)
+    assert bad == 0, worst
+
+
+def test_unaligned_output(lib):
+    s = inputs.task_inputs("efficient_kan", {"B": 130, "I": 64, "O": 72}, 13)
+    dev = torch.device("cuda")
+    t = {k: s[k].to(dev) for k in IN_NAMES}
+    raw = torch.empty(130 * 72 + 1, device=dev)
+    out = raw[1:].view(130, 72)  # 4 bytes past a 16-byte boundary
+    nbytes = lib.b200_efficient_kan_workspace_bytes(s["grid_size"], s["spline_order"], 130, 64, 72)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    st = lib.b200_efficient_kan_async(*(t[k].data_ptr() for k in IN_NAMES), s["grid_size"], s["spline_order"],
+                                      130, 64, 72, out.data_ptr(), ws.data_ptr(), nbytes, None)
+    torch.cuda.synchronize()
+    assert st == 0
+    bad, worst = exact.within(out.double().cpu().numpy(), exact.efficient_kan(s)["out"], ATOL, RTOL)
     assert bad == 0, worst
