@@ -18,6 +18,8 @@
 // the next (step_prologue).
 #pragma once
 
+#include <cstdlib>
+
 #include "../common/b200_common.cuh"
 #include "../common/peer.cuh"
 #include "ppo_clip.cuh"
@@ -284,6 +286,17 @@ inline int run(const float* reward, const void* done, float gamma, int32_t B, in
   return vec ? launch<true, false, false, false>(a, stream) : launch<false, false, false, false>(a, stream);
 }
 
+// Lead of the PPO role in the multi-GPU step's CTA split (see run_exchange): 0.25 measured best
+// at N = 2 (22.1 us per step against 22.5 us with none and 24.2 us with 0.5); B200_RL_PPO_LEAD in
+// the environment overrides it for tuning runs.
+inline double ppo_lead() {
+  static const double v = [] {
+    const char* e = std::getenv("B200_RL_PPO_LEAD");
+    return e != nullptr ? std::atof(e) : 0.25;
+  }();
+  return v;
+}
+
 // The fused multi-GPU step: every rank calls this with its own batch (the same B, T and n on
 // every rank) and the same `epoch` (1 on the first step, peer_next_epoch() of the previous one
 // after); ppo_out receives the PPO outputs of all ranks' samples on every rank.  The exchange must
@@ -319,8 +332,12 @@ inline int run_exchange(const float* reward, const void* done, float gamma, int3
   a.ppo_out = ppo_out;
   a.inv_n = ppo::inv_count(int64_t(x->world) * n);
   const int64_t slots = int64_t(sm_count()) * B200_RL_MIN_CTAS;
-  split_roles(a.B, row_bytes(T, done_bits), ppo::num_chunks(n), (ent != nullptr ? 16 : 12) * ppo::kChunk, slots,
-              true, &a.rtg_ctas, &a.ppo_ctas);
+  // The exchange starts when the rank's PPO chunks are done, so the PPO role gets a share of the
+  // CTAs as if its chunks were (1 + lead) times their bytes: it finishes first and the peer
+  // records travel while the reward-to-go rows finish.
+  const double lead = ppo_lead();
+  const int64_t cb = int64_t(double((ent != nullptr ? 16 : 12) * ppo::kChunk) * (1.0 + lead));
+  split_roles(a.B, row_bytes(T, done_bits), ppo::num_chunks(n), cb, slots, true, &a.rtg_ctas, &a.ppo_ctas);
   const PeerView pv = peer_view(*x, epoch);
   const bool vec = aligned16(cur) && aligned16(old) && aligned16(adv) && (ent == nullptr || aligned16(ent));
   auto go = [&](auto kern) {
