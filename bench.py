@@ -18,8 +18,9 @@ against the one-op entry); a failed check exits non-zero.  `exchange_us` is the 
 samples (the exchange alone at N > 1, the step's fixed cost at N = 1).
 
 `ops_sharded`: robust-L1, LIF, KAN and FP8 at their BASELINE sizes split over the N ranks (strong
-scaling: element ranges with an NCCL all-gather of chunk partials; batch rows; batch rows; rows of
-M with W replicated), each checked against the same op run whole on one GPU.
+scaling: element ranges whose chunk partials are exchanged, by an NCCL all-gather in a CUDA graph
+or by the kernel's own pushes over NVLink, the faster form reported and both listed; batch rows;
+batch rows; rows of M with W replicated), each checked against the same op run whole on one GPU.
 
 Timing: W untimed warm-up steps, then exactly K steps between barriers and device syncs, timed
 with CUDA events on the launching stream, max over ranks.  Each step reads a different one of
