@@ -857,7 +857,9 @@ def other_ops(ops, dev, world, rank):
     del gsets, s
 
     # Long rows (T >> B): 8 rows of 2^21 steps (151 MB of reward and done flags), the one-warp-per-
-    # row scan against the chunked one (a warp per 1056-step chunk).  9 algorithmic bytes per step.
+    # row scan against the chunked one (a warp per 1056-step chunk, one cooperative launch).  9
+    # algorithmic bytes per step; the chunked form's second read of the chunks is served in part by
+    # L2 (DRAM bytes per call from ncu in profiles/rtg_chunked_B8_T2097152.txt).
     g = torch.Generator(device=dev).manual_seed(rank)
     r = torch.rand(8, 1 << 21, device=dev, generator=g)
     dn = torch.rand(8, 1 << 21, device=dev, generator=g) < 0.001
@@ -868,8 +870,7 @@ def other_ops(ops, dev, world, rank):
                                                           "frac_of_hbm": nbytes / ms / 1e6 / peak}
     ms = timeit(lambda: ops.reward_to_go_chunked(r, dn, 0.99, out=out))
     res["reward_to_go B8 T2097152 (chunked along T)"] = {"us": ms * 1e3, "bytes": nbytes, "gbs": nbytes / ms / 1e6,
-                                                         "frac_of_hbm": nbytes / ms / 1e6 / peak,
-                                                         "moved_bytes": 14 * r.numel()}
+                                                         "frac_of_hbm": nbytes / ms / 1e6 / peak}
     del r, dn, out
 
     # Tensor-core ops against the measured dense bf16 peak, burst and sustained (the long GEMMs run

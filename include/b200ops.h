@@ -138,19 +138,22 @@ int b200_reward_to_go_bits_async(const float* reward, const uint32_t* done_bits,
                                  float* output, void* stream);
 
 /* Long rows (no reference counterpart): reward-to-go parallel along T.  The row is cut into
- * 1056-step chunks, each on its own warp (chunk maps in fp64, a per-row carry pass, then each chunk
- * rescanned from its exact carry), so a batch of few long rows fills the GPU; 14 instead of 9
- * bytes moved per step.  done is bytes [B, T], or with done_is_bits != 0 the words of
+ * 1056-step chunks, each on its own warp (chunk maps in fp64, the carries composed from them, then
+ * each chunk rescanned from its carry), so a batch of few long rows fills the GPU.  One cooperative
+ * launch of one CTA per SM: 9 bytes per step from HBM, plus the second read of the chunks that L2
+ * does not serve.  done is bytes [B, T], or with done_is_bits != 0 the words of
  * b200_pack_done_async.  Outputs within the reward-to-go tolerance of the oracle (the carries'
- * fp64 association differs from b200_reward_to_go_async's).  Workspace:
- * b200_reward_to_go_chunked_workspace_bytes(B, T) bytes (-1 for negative sizes).
+ * fp64 association differs from b200_reward_to_go_async's) and the same bits on every call.
+ * Workspace: b200_reward_to_go_chunked_workspace_bytes(B, T) bytes (-1 for negative sizes),
+ * 8-byte aligned, zero-filled once before first use (its first 8 bytes count grid-barrier
+ * arrivals), used on one stream at a time.
  *
  * Sharded over time across GPUs: rank r holds steps [offset_r, offset_r + T_local) of every row
  * (any T_local >= 1 per rank; the same B everywhere).  Each rank calls
  * b200_reward_to_go_slice_maps_async (writes its [B] slice maps, two doubles per row), the ranks
  * all-gather them into [world, B, 2] doubles in rank order, and each rank calls
  * b200_reward_to_go_slice_scan_async with the same workspace (it still holds the chunk maps) to
- * write its [B, T_local] outputs. */
+ * write its [B, T_local] outputs (these two read each chunk twice from HBM: 14 bytes per step). */
 int64_t b200_reward_to_go_chunked_workspace_bytes(int32_t B, int32_t T);
 int b200_reward_to_go_chunked_async(const float* reward, const void* done, int done_is_bits, float gamma, int32_t B,
                                     int32_t T, float* output, void* workspace, int64_t workspace_bytes,

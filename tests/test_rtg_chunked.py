@@ -74,6 +74,36 @@ def test_chunked_golden(ops, cid, rec):
     check(got, s["reward"], s["done"], s["gamma"])
 
 
+LARGE = [
+    (8, 1 << 21),   # CTA ranges that cross rows; 8 superblocks per row (shared-memory carry path)
+    (1, 1 << 24),   # one row over every CTA: up to 62 superblocks before a CTA's range
+    (1, 70_000_000),  # more than 256 superblocks in the row: the global-memory carry path
+    (4096, 160_000),  # more than 512 blocks per CTA: the global-memory carry path over many rows
+]
+
+
+@pytest.mark.parametrize("B,T", LARGE, ids=[f"B{b}_T{t}" for b, t in LARGE])
+def test_chunked_large_paths(ops, B, T):
+    """Every carry path of the one-launch form against the one-warp-per-row scan (each within the
+    task tolerance of the fp64 oracle, so within twice of each other), with done as bytes and as
+    bits (the same bits), and run twice (the same bits)."""
+    g = torch.Generator(device="cuda").manual_seed(B + T)
+    r = torch.rand(B, T, device="cuda", generator=g)
+    d = torch.rand(B, T, device="cuda", generator=g) < 0.001
+    ref = ops.reward_to_go(r, d, 0.99)
+    got = ops.reward_to_go_chunked(r, d, 0.99).clone()
+    again = ops.reward_to_go_chunked(r, d, 0.99).clone()
+    bits = ops.reward_to_go_chunked(r, ops.pack_done(d), 0.99)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int32), again.view(torch.int32))
+    assert torch.equal(got.view(torch.int32), bits.view(torch.int32))
+    atol, rtol = TOL
+    err = ((got - ref).abs() - 2 * (atol + rtol * ref.abs())).max().item()
+    assert err <= 0, err
+    del r, d, ref, got, again, bits
+    torch.cuda.empty_cache()
+
+
 def emulate(ops, r, d, gamma, cuts, bits=False):
     """Ranks emulated on one GPU: rank k holds steps [cuts[k], cuts[k+1]) of every row."""
     lib = pkg().load()
