@@ -205,6 +205,39 @@ __device__ __forceinline__ void land_pass(const Pass& p, const Edges& e, float* 
   __syncwarp();
 }
 
+// A rescanned pass's outputs (staged over its rewards in shared memory) to dst, the pass's first
+// output.  When dst has the rewards' 16-byte phase, lane 0 writes the aligned interior with one
+// bulk copy and the lanes store the ragged ends; otherwise drain_floats.  The bulk copy may still
+// be reading the buffer when this returns: outputs_read before the buffer is refilled,
+// outputs_done before the warp is finished with its buffers.  One bulk copy per pass instead of
+// 128-bit stores from every lane: reward-to-go B4096 T1000 7.7 -> 7.3 us, the fused RL step
+// 17.1 -> 16.9 us.
+__device__ __forceinline__ void store_pass(const Pass& p, const float* s_r, float* dst, int lane) {
+  const float* src = s_r + p.sr;
+  const int dphase = int((reinterpret_cast<uintptr_t>(dst) >> 2) & 3);
+  if (dphase != p.pr || p.ebr <= p.ear) {
+    drain_floats(dst, p.len, s_r + (p.sr - p.pr), p.pr, lane);
+    return;
+  }
+  fence_proxy_async_smem();  // the rescan's shared-memory writes come before the copy's reads
+  __syncwarp();
+  if (lane == 0) {
+    bulk_s2g(dst + p.ear, src + p.ear, uint32_t(p.ebr - p.ear) * 4u);
+    bulk_commit();
+  }
+  const int hr = min(p.len, p.ear), tr = p.len - p.ebr;
+  if (lane < hr) dst[lane] = src[lane];
+  if (lane < tr) dst[p.ebr + lane] = src[p.ebr + lane];
+}
+__device__ __forceinline__ void outputs_read(int lane) {
+  if (lane == 0) bulk_wait_read<0>();
+  __syncwarp();
+}
+__device__ __forceinline__ void outputs_done(int lane) {
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
 // gamma^kLane in fp64 (the composed factor of a run of kLane steps without a done flag).
 __device__ __forceinline__ double gamma_run(double gamma) {
   double a = 1.0, q = gamma;
@@ -317,6 +350,7 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
     if (has_next && nbuf == 2) {
       const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
       nxt = make_pass<kBits>(reward + nrow * int64_t(T), drow(nrow), nt0, nt1 - nt0, nw);
+      outputs_read(lane);  // buffer nb's outputs (the previous pass) have left shared memory
       enxt = issue_pass<kBits>(nxt, s_rb(nb), s_db(nb), &bars[nb], lane);
     }
     const uint32_t cb = nbuf == 2 ? (k & 1u) : 0u;
@@ -325,12 +359,13 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
     const double first = scan_pass<kBits>(cur, ecur, s_rb(cb), s_db(cb), carry, g, g_run, gamma, lane);
     const int t0 = t1 > kSeg ? t1 - kSeg : 0;
     if (k == 0) pdl_wait();  // first global write of this warp (no-op without PDL)
-    drain_floats(out + row * int64_t(T) + t0, cur.len, s_rb(cb) + (cur.sr - cur.pr), cur.pr, lane);
+    store_pass(cur, s_rb(cb), out + row * int64_t(T) + t0, lane);
     __syncwarp();
     if (!has_next) break;
     if (nbuf == 1) {
       const int nt0 = nt1 > kSeg ? nt1 - kSeg : 0;
       nxt = make_pass<kBits>(reward + nrow * int64_t(T), drow(nrow), nt0, nt1 - nt0, nw);
+      outputs_read(lane);
       enxt = issue_pass<kBits>(nxt, s_rb(0), s_db(0), &bars[0], lane);
     }
     carry = (nrow == row) ? first : 0.0;
@@ -340,6 +375,7 @@ __device__ __forceinline__ void warp_rows(const float* __restrict__ reward, cons
     ecur = enxt;
     ++k;
   }
+  outputs_done(lane);
 }
 
 // Warp w of CTA c handles rows c*kWarps + w, + gridDim.x*kWarps, ...

@@ -376,6 +376,7 @@ __device__ __forceinline__ uint32_t walk(const float* __restrict__ reward, const
     if (q + 1 < cnt) {
       itn = item(q + 1);
       nxt = pass_of(itn);
+      if (kScan) rtg::outputs_read(lane);  // buffer nb holds the previous chunk: its outputs are read
       enxt = rtg::issue_pass<kBits>(nxt, s_r(nb), s_d(nb), &bars[nb], lane);
     }
     double carry = 0.0;
@@ -395,13 +396,14 @@ __device__ __forceinline__ uint32_t walk(const float* __restrict__ reward, const
       }
     } else {
       rescan_pass<kBits>(cur, ecur, s_r(cb), s_d(cb), suffix, carry, gamma, lane);
-      rtg::drain_floats(out + (cur.rs - reward), cur.len, s_r(cb) + (cur.sr - cur.pr), cur.pr, lane);
+      rtg::store_pass(cur, s_r(cb), out + (cur.rs - reward), lane);
     }
     __syncwarp();
     cur = nxt;
     ecur = enxt;
     it = itn;
   }
+  if (kScan) rtg::outputs_done(lane);  // the outputs are written before the CTA ends
   return phbits;
 }
 
