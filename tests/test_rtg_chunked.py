@@ -11,6 +11,9 @@ GPU, through the C ABI:
   buffer and workspace, slice maps stacked in rank order as the all-gather would), with ragged
   slice lengths, against the oracle and against the one-GPU chunked scan;
 - with several GPUs, the same through torch.distributed (NCCL) with one process per GPU;
+- the one-launch form's carry paths at large sizes (CTA ranges across rows, many superblocks, the
+  global-memory path) against the one-warp-per-row scan, and its grid barrier's bounded wait run
+  out on purpose (the device fault bit, then recovery);
 - status codes.
 """
 import os
@@ -102,6 +105,37 @@ def test_chunked_large_paths(ops, B, T):
     assert err <= 0, err
     del r, d, ref, got, again, bits
     torch.cuda.empty_cache()
+
+
+def test_grid_barrier_wait_runs_out(ops):
+    """Failure detection of the one-launch form's grid barrier, without a GPU fault: a workspace
+    whose arrival count is not a multiple of the grid size (one that was not zero-filled before its
+    first use) leaves a CTA waiting for a count that never comes.  Its bounded wait gives up after
+    2 s and sets bit 0 of the device fault word; the launch completes (its outputs are not
+    meaningful), and a zero-filled workspace works again."""
+    lib = pkg().load()
+    B, T = 4, 50_000
+    r, d = make(B, T, seed=11)
+    rc, dc = r.cuda(), d.cuda()
+    nbytes = lib.b200_reward_to_go_chunked_workspace_bytes(B, T)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ws[:8].view(torch.int64).fill_(1)
+    out = torch.empty_like(rc)
+    torch.cuda.synchronize()
+    lib.b200_device_fault()  # read and clear
+    st = lib.b200_reward_to_go_chunked_async(rc.data_ptr(), dc.data_ptr(), 0, 0.99, B, T, out.data_ptr(),
+                                             ws.data_ptr(), nbytes, None)
+    assert st == 0
+    torch.cuda.synchronize()
+    fault = lib.b200_device_fault()
+    assert fault > 0 and fault & 1, fault
+    ws.zero_()
+    st = lib.b200_reward_to_go_chunked_async(rc.data_ptr(), dc.data_ptr(), 0, 0.99, B, T, out.data_ptr(),
+                                             ws.data_ptr(), nbytes, None)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert lib.b200_device_fault() == 0
+    check(out, r, d, 0.99)
 
 
 def emulate(ops, r, d, gamma, cuts, bits=False):
