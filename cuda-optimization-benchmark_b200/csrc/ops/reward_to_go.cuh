@@ -24,7 +24,7 @@
 //      value entering its run;
 //   5. lane l re-runs its steps from that value in fp32 (at most kLane roundings per output, no
 //      error carried between runs) and writes the outputs over the rewards in shared memory,
-//      and the warp streams them out with 128-bit stores.
+//      and lane 0 writes them out with one bulk copy (store_pass).
 // One warp per row and 40 warps per SM put every row of the BASELINE batch in flight at once.
 //
 // Done flags come as one byte per step (the reference layout) or, with kBits, as bits: uint32 words
