@@ -63,6 +63,20 @@ def test_no_host_only_queries_need_a_gpu(lib):
     assert lib.b200_status_string(0) == b"ok"
 
 
+def test_chunked_reward_to_go_workspace_layout(lib):
+    """The chunked reward-to-go's workspace: 256 bytes of control words (the grid-barrier count),
+    then per 1056-step chunk its map (16 B), carry (8 B) and 32 lane suffix maps (512 B), and per
+    block of 8 chunks its map (16 B) and carry (8 B); -1 for negative sizes, 0 for empty ones."""
+    def expect(B, T):
+        nch = (T + 1055) // 1056
+        nblk = (nch + 7) // 8
+        return 256 + B * nch * (16 + 8 + 512) + B * nblk * (16 + 8)
+    for B, T in [(1, 1), (8, 1 << 21), (3, 9000), (4096, 1000), (1, 70_000_000)]:
+        assert lib.b200_reward_to_go_chunked_workspace_bytes(B, T) == expect(B, T), (B, T)
+    assert lib.b200_reward_to_go_chunked_workspace_bytes(0, 5) == 0
+    assert lib.b200_reward_to_go_chunked_workspace_bytes(-1, 5) == -1
+
+
 def test_built_for_sm100a_only():
     """The fatbinary holds sm_100a code (checked from the build command, not by reading binaries)."""
     b = pkg()._build
